@@ -1,0 +1,393 @@
+"""mHC fwd+bwd throughput on B200 (the north-star workload).
+
+One step = the four mHC operators over one batch of T=32768 tokens, N=4,
+D=7168, bf16 storage:
+    mhc_pre_clamp_sinkhorn (need_backward=True)   config-3 inputs
+    mhc_post                                       config-2 inputs
+    mhc_post_backward
+    mhc_pre_clamp_sinkhorn_backward
+and, with N>1 GPUs, one NCCL all-reduce of the packed [grad_phi|grad_alpha|grad_base].
+Each rank owns its own 32768 tokens (weak scaling: the per-GPU work is fixed).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` is whole-job tokens/s with the inputs
+resident in HBM; `e2e` is the same metric through the public API with the
+inputs copied from pinned host memory every step.  `--impl reference` times
+the CPU oracle (the reference's pure-PyTorch algorithm restated) on this host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "flagos-mhc_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+T_TOK, N_HC, D_HID = 32768, 4, 7168
+METRIC = "mHC fwd+bwd tokens/s (T=32768,N=4,D=7168 bf16)"
+WORKLOAD = "pre_clamp_sinkhorn fwd(need_backward)+bwd and post fwd+bwd, T=32768 N=4 D=7168 bf16"
+
+
+# ----------------------------------------------------------------------------- helpers
+def algorithmic_bytes(T, N, D, e=2):
+    """Compulsory HBM bytes per op (each input read once, each output written once)."""
+    HM, HC = N * (N + 2), N * D
+    post_fwd = T * (2 * N * D * e + D * e + N * N * 4 + N * 4)
+    post_bwd = T * (3 * N * D * e + 2 * D * e + 2 * (N * N * 4 + N * 4))
+    pre_fwd = T * (N * D * e + D * e + N * 4 + N * N * 4 + 4 + HC * 4 + HM * 4 + N * N * 4
+                   + N * 4) + HM * HC * 4
+    pre_bwd = T * (2 * N * D * e + D * e + N * 4 + N * N * 4 + 4 + HM * 4 + N * 4) \
+        + 2 * HM * HC * 4 + (3 + HM) * 4
+    return {"pre_fwd": pre_fwd, "post_fwd": post_fwd, "post_bwd": post_bwd, "pre_bwd": pre_bwd}
+
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = (uuid or "").lower()
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [[c.strip() for c in ln.split(",")] for ln in out.splitlines() if ln.strip()]
+        mine = [r for r in rows if self.uuid and self.uuid in r[0].lower()] or rows
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in mine:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(T, N, D, seed, dev):
+    """Config-2 (post) and config-3 (pre) inputs, generated on the device from a seed."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    bf = torch.bfloat16
+    HM, HC = N * (N + 2), N * D
+    inp = {}
+    inp["x_pre"] = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+    inp["phi"] = torch.randn(HM, HC, generator=g, device=dev) / HC ** 0.5
+    inp["alpha"] = torch.rand(3, generator=g, device=dev) + 0.5
+    inp["base"] = torch.randn(HM, generator=g, device=dev) * 0.1
+    inp["gy_pre"] = torch.randn(T, D, generator=g, device=dev).to(bf)
+    inp["gpost"] = torch.randn(T, N, generator=g, device=dev)
+    inp["gcomb"] = torch.randn(T, N, N, generator=g, device=dev)
+    inp["x_post"] = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+    inp["h_out"] = torch.randn(T, D, generator=g, device=dev).to(bf)
+    m = torch.randn(T, N, N, generator=g, device=dev).exp()
+    for _ in range(20):
+        m = m / m.sum(-1, keepdim=True)
+        m = m / m.sum(-2, keepdim=True)
+    inp["h_res"] = m
+    inp["h_post"] = 2 * torch.sigmoid(torch.randn(T, N, generator=g, device=dev))
+    inp["gy_post"] = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+    return inp
+
+
+KW = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
+
+
+def run_step(M, inp, world, ev=None):
+    """The four operators (+ the gradient all-reduce). Returns the small results."""
+    if ev is not None:
+        ev[0].record()
+    out = M.mhc_pre_clamp_sinkhorn(inp["x_pre"], inp["phi"], inp["alpha"], inp["base"],
+                                   need_backward=True, **KW)
+    if ev is not None:
+        ev[1].record()
+    y = M.mhc_post(inp["x_post"], inp["h_res"], inp["h_out"], inp["h_post"])
+    if ev is not None:
+        ev[2].record()
+    pg = M.mhc_post_backward(inp["gy_post"], inp["x_post"], inp["h_res"], inp["h_out"],
+                             inp["h_post"])
+    if ev is not None:
+        ev[3].record()
+    gx, gphi, ga, gb = M.mhc_pre_clamp_sinkhorn_backward(
+        inp["x_pre"], inp["phi"], inp["alpha"], inp["base"], out["inv_rms"], out["x_scaled"],
+        out["mixes"], out["h_res_logits"], out["pre"], inp["gy_pre"], inp["gpost"],
+        inp["gcomb"], **KW)
+    if ev is not None:
+        ev[4].record()
+    if world > 1:
+        from FlagOS_mhc.distributed import allreduce_pre_grads
+        allreduce_pre_grads(gphi, ga, gb)
+    if ev is not None:
+        ev[5].record()
+    return out, y, pg, (gx, gphi, ga, gb)
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_oracle_rate(T_sample, budget_s, max_s, steps=None):
+    """Tokens/s of the CPU oracle (fp32, all host threads) on T_sample-token
+    slices of the benchmark shapes; repeats until budget_s (or `steps` reps)."""
+    from oracle import mhc_oracle as O
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(0)
+    N, D = N_HC, D_HID
+    HM, HC = N * (N + 2), N * D
+    x = torch.randn(T_sample, N, D, generator=g).to(torch.bfloat16)
+    phi = torch.randn(HM, HC, generator=g) / HC ** 0.5
+    alpha, base = torch.rand(3, generator=g) + 0.5, torch.randn(HM, generator=g) * 0.1
+    gy = torch.randn(T_sample, D, generator=g).to(torch.bfloat16)
+    gpost, gcomb = torch.randn(T_sample, N, generator=g), torch.randn(T_sample, N, N, generator=g)
+    h_res = torch.softmax(torch.randn(T_sample, N, N, generator=g), -1)
+    h_post = 2 * torch.sigmoid(torch.randn(T_sample, N, generator=g))
+    h_out = torch.randn(T_sample, D, generator=g).to(torch.bfloat16)
+    gyp = torch.randn(T_sample, N, D, generator=g).to(torch.bfloat16)
+
+    def one():
+        O.pre_fwd(x, phi, alpha, base, **KW)
+        O.post_fwd(x, h_res, h_out, h_post)
+        O.post_bwd(gyp, x, h_res, h_out, h_post)
+        O.pre_bwd(x, phi, alpha, base, gy, gpost, gcomb, **KW)
+
+    times = []
+    t_all = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        el = time.perf_counter() - t_all
+        if steps is not None:
+            if len(times) >= steps:
+                break
+        elif el >= budget_s or el >= max_s:
+            break
+    return T_sample * len(times) / sum(times), times
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    # calibrate the slice so one step is ~4 s of CPU work
+    rate0, _ = cpu_oracle_rate(64, 0, 60, steps=1)
+    T_s = int(max(64, min(4096, rate0 * 4.0)) // 64 * 64)
+    for _ in range(args.warmup):
+        cpu_oracle_rate(T_s, 0, 600, steps=1)
+    rate, times = cpu_oracle_rate(T_s, 0, 3600, steps=args.steps)
+    cores = torch.get_num_threads()
+    sample = (f"{T_s}-token slices of the T=32768,N=4,D=7168 workload (pre fwd+bwd and post "
+              f"fwd+bwd, fp32 CPU oracle); per-token independent ops, so tokens/s is linear in T")
+    line = {
+        "metric": METRIC, "value": rate, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * T_TOK / rate, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "T": T_TOK, "N": N_HC, "D": D_HID,
+                   "parallelism": "rank 0 only (CPU)", "sample_tokens": T_s},
+        "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=T_TOK, help="tokens per GPU")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch.distributed as dist
+    import FlagOS_mhc as M
+    from FlagOS_mhc import _C
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=dev)
+
+    T, N, D = args.tokens, N_HC, D_HID
+    inp = make_inputs(T, N, D, seed=1000 + rank, dev=dev)
+    torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 0)):
+        run_step(M, inp, world)
+    torch.cuda.synchronize()
+
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    n0 = _C.lib().mhc_kernel_launches()
+    start.record()
+    for k in range(K):
+        run_step(M, inp, world, evs[k])
+    stop.record()
+    torch.cuda.synchronize()
+    launches = _C.lib().mhc_kernel_launches() - n0
+    if world > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    ms_total = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / K
+    value = world * T * K / (ms_total / 1e3)
+
+    names = ["pre_fwd", "post_fwd", "post_bwd", "pre_bwd", "allreduce"]
+    op_ms = {n: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K))
+             for i, n in enumerate(names)}
+    ab = algorithmic_bytes(T, N, D)
+    peak, peak_kind = hbm_peak()
+    step_bytes = sum(ab.values())
+    ops = {n: {"ms": op_ms[n], "GB/s": ab[n] / (op_ms[n] / 1e3) / 1e9,
+               "frac_of_" + peak_kind + "_peak": ab[n] / (op_ms[n] / 1e3) / 1e9 / peak}
+           for n in ab}
+    dom = max(ab, key=lambda n: op_ms[n])
+    traffic = ncu_traffic().get(dom)
+    achieved = ab[dom] / (op_ms[dom] / 1e3) / 1e9
+
+    # ---- end to end through the public API, inputs from pinned host memory
+    e2e = None
+    if args.e2e_steps > 0:
+        big = ["x_pre", "gy_pre", "gpost", "gcomb", "x_post", "h_out", "h_res", "h_post",
+               "gy_post"]
+        host = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, pin_memory=True) for k in big}
+        for k in big:
+            host[k].copy_(inp[k])
+        h2d = sum(host[k].numel() * host[k].element_size() for k in big)
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d2h = 0
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e_start.record()
+        for _ in range(args.e2e_steps):
+            for k in big:
+                inp[k].copy_(host[k], non_blocking=True)
+            out, y, pg, grads = run_step(M, inp, world)
+            res = [grads[1], grads[2], grads[3], pg[1], pg[3], out["post_out"], out["comb_frag"]]
+            cpu_res = [r.to("cpu", non_blocking=False) for r in res]
+            d2h = sum(r.numel() * r.element_size() for r in cpu_res)
+        e_stop.record()
+        torch.cuda.synchronize()
+        e_ms = e_start.elapsed_time(e_stop)
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": world * T * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "steps": args.e2e_steps,
+               "note": "H2D of every op input from pinned memory; D2H of the parameter grads "
+                       "and the per-token small outputs (activations stay on the device)"}
+        del host
+
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, times = cpu_oracle_rate(256, 10.0, 30.0)
+        cpu_base = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                    "kind": "port",
+                    "sample": f"{len(times)} x 256-token slices of the same workload (fp32 CPU "
+                              "oracle, pre fwd+bwd + post fwd+bwd); tokens/s is linear in T"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "global_tokens": world * T,
+                       "N": N, "D": D, "hcMix": N * (N + 2), "clamp": [-10.0, 10.0],
+                       "iter_times": 20, "parallelism": f"dp{world} token-sharded"
+                       + (", packed grad_phi NCCL all-reduce" if world > 1 else ""),
+                       "l2": "no flush: every step streams ~21 GB, x alone is 1.88 GB > 126 MB L2"},
+            "hbm_frac_step": step_bytes / (ms_step / 1e3) / 1e9 / peak,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "algorithmic_bytes": ab[dom], "traffic": traffic},
+            "ops": ops, "allreduce_ms": op_ms["allreduce"],
+            "gpu_launches": int(launches),
+            "clocks": ck, "e2e": e2e, "cpu_baseline": cpu_base,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

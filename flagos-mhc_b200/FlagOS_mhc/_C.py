@@ -1,0 +1,105 @@
+"""ctypes binding of libmhc_b200.so (the C ABI declared in include/mhc_b200.h).
+
+The library is loaded once, on first use.  There is no fallback: if the shared
+library is missing or the tensors are not on an sm_100 GPU, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libmhc_b200.so")
+_lib = None
+_lock = threading.Lock()
+
+MHC_F32, MHC_F16, MHC_BF16 = 0, 1, 2
+_DTYPE = {torch.float32: MHC_F32, torch.float16: MHC_F16, torch.bfloat16: MHC_BF16}
+
+MHC_OK = 0
+MHC_ERR_INVALID_ARGUMENT = 1
+MHC_ERR_UNSUPPORTED_N = 2
+MHC_ERR_UNSUPPORTED_DTYPE = 3
+MHC_ERR_WORKSPACE = 4
+MHC_ERR_CUDA = 5
+MHC_ERR_DEVICE = 6
+MHC_ERR_TIMEOUT = 7
+
+_vp, _fp = ctypes.c_void_p, ctypes.c_void_p
+_i64, _i32, _f32, _sz = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_size_t
+
+_SIGS = {
+    "mhc_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "mhc_version": (ctypes.c_int, []),
+    "mhc_kernel_launches": (ctypes.c_uint64, []),
+    "mhc_post_fwd": (ctypes.c_int, [_vp, _fp, _vp, _fp, _vp, _i64, _i32, _i64, _i32, _vp]),
+    "mhc_post_bwd": (ctypes.c_int, [_vp, _vp, _fp, _vp, _fp, _vp, _fp, _vp, _fp, _i64, _i32,
+                                    _i64, _i32, _vp]),
+    "mhc_pre_fwd_workspace_bytes": (_sz, [_i64, _i32, _i64, _i32]),
+    "mhc_pre_fwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _i64, _i32, _i64, _i32, _f32, _f32, _f32,
+                                   _f32, _i32, _vp, _fp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _sz,
+                                   _vp]),
+    "mhc_pre_bwd_workspace_bytes": (_sz, [_i64, _i32, _i64, _i32, _i32]),
+    "mhc_pre_bwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp, _i64, _i32,
+                                   _i64, _i32, _f32, _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp,
+                                   _vp, _sz, _vp]),
+}
+
+
+def lib_path() -> str:
+    return _LIB_PATH
+
+
+def lib():
+    """Load (once) and return the ctypes handle; raise if the library is absent."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(_LIB_PATH):
+                    raise RuntimeError(
+                        f"FlagOS_mhc: CUDA library not found at {_LIB_PATH}; build it with "
+                        "`python flagos-mhc_b200/build.py` (there is no CPU fallback)")
+                h = ctypes.CDLL(_LIB_PATH)
+                for name, (res, args) in _SIGS.items():
+                    fn = getattr(h, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = h
+    return _lib
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def dtype_code(dt):
+    try:
+        return _DTYPE[dt]
+    except KeyError:
+        raise TypeError(f"FlagOS_mhc: unsupported dtype {dt}; expected float32/float16/bfloat16")
+
+
+def stream_of(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def check(status: int, what: str):
+    if status == MHC_OK:
+        return
+    msg = lib().mhc_status_string(status).decode()
+    text = f"FlagOS_mhc.{what}: {msg} (status {status})"
+    if status == MHC_ERR_UNSUPPORTED_N:
+        raise NotImplementedError(text)
+    if status in (MHC_ERR_INVALID_ARGUMENT, MHC_ERR_UNSUPPORTED_DTYPE):
+        raise ValueError(text)
+    raise RuntimeError(text)
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("FlagOS_mhc: operators run only on CUDA (sm_100) tensors; "
+                               f"got a tensor on {t.device}")

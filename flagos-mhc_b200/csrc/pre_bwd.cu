@@ -1,0 +1,389 @@
+// pre_bwd.cu -- mhc_pre_clamp_sinkhorn backward, generic path (any dtype, N 1..8).
+//
+// Stream-ordered kernels:
+//   1. pre_bwd_dots_kernel    grad_pre[t,n] = <grad_y[t,:], x[t,n,:]>      (warp / token)
+//   2. pre_small_bwd_kernel   small-stage VJP -> grad_mixes[t,:], the RMS coefficient
+//                             coef[t] = inv^2/HC * <grad_mixes, mixes>, and per-block
+//                             partial sums of grad_alpha / grad_base       (thread / token)
+//   3. pre_reduce_ab_kernel   fixed-order sum of those partials
+//   4. pre_bwd_gx_kernel      grad_x = gy*pre[n] + inv*(grad_mixes.phi) - coef*x
+//   5. pre_bwd_gphi_kernel    split-T partials of grad_phi = (inv*grad_mixes)^T x
+//   6. pre_reduce_gphi_kernel fixed-order sum of the split-T partials
+// Reference replaced: src/mhc_pre_clamp_sinkhorn_backward.py:1292-1391 (y_bwd, small
+// stage, two torch.mm, fused rms-bwd); VJP order of :1144-1209.
+//
+// Two identities remove the reference's x_scaled traffic:
+//   <x, gxs>  = sum_k grad_mixes[k] * mixes[k] / inv       (mixes = inv * x.phi^T)
+//   grad_phi  = (inv * grad_mixes)^T x                      (x_scaled = inv * x)
+#include "common.cuh"
+#include "pre_common.cuh"
+
+namespace mhc {
+
+template <typename E, int N, bool VEC>
+__global__ void __launch_bounds__(256)
+pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
+                    float* __restrict__ gpre, int64_t T, int64_t D) {
+  constexpr int P = VEC ? Pack<E>::n : 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t nchunk = D / P;
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
+       t += nwarps) {
+    float acc[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) acc[n] = 0.f;
+    const E* xt = x + t * N * D;
+    const E* gt = gy + t * D;
+    for (int64_t c = lane; c < nchunk; c += 32) {
+      float g[P], xv[N][P];
+      load_pack<E, VEC>(gt + c * P, g);
+#pragma unroll
+      for (int n = 0; n < N; ++n) load_pack<E, VEC>(xt + n * D + c * P, xv[n]);
+#pragma unroll
+      for (int n = 0; n < N; ++n)
+#pragma unroll
+        for (int e = 0; e < P; ++e) acc[n] = fmaf(g[e], xv[n][e], acc[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < N; ++n) acc[n] = warp_sum(acc[n]);
+#pragma unroll
+    for (int n = 0; n < N; ++n)
+      if (lane == n) gpre[t * N + n] = acc[n];
+  }
+}
+
+// Small-stage VJP of one token; thread per token.  The Sinkhorn iterates are kept in
+// `hist` ((iters-1) matrices, layout [iter][elem][T] so the stores coalesce).
+template <int N>
+__global__ void __launch_bounds__(128)
+pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ alpha,
+                     const float* __restrict__ base, const float* __restrict__ gpre,
+                     const float* __restrict__ gpost, const float* __restrict__ gcomb,
+                     const float* __restrict__ inv_rms, int64_t T, int64_t HC, SmallParams sp,
+                     float* __restrict__ hist, float* __restrict__ gm_out,
+                     float* __restrict__ coef_out, float* __restrict__ partials) {
+  constexpr int HM = hc_mix(N);
+  constexpr int NN = N * N;
+  constexpr int NP = 3 + HM;
+  __shared__ float sbase[HM];
+  __shared__ float red[128][NP + 1];
+  for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
+  __syncthreads();
+  sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float contrib[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) contrib[i] = 0.f;
+  if (t < T) {
+    float mix[HM];
+#pragma unroll
+    for (int k = 0; k < HM; ++k) mix[k] = mixes[t * HM + k];
+    float logits[NN], P[NN], M[NN];
+    logits_softmax<N>(mix, sbase, sp, logits, P);
+#pragma unroll
+    for (int e = 0; e < NN; ++e) M[e] = P[e] + sp.hc_eps;
+    col_norm<N>(M, sp.hc_eps);
+    for (int it = 1; it < sp.iters; ++it) {
+#pragma unroll
+      for (int e = 0; e < NN; ++e) hist[((int64_t)(it - 1) * NN + e) * T + t] = M[e];
+      row_norm<N>(M, sp.hc_eps);
+      col_norm<N>(M, sp.hc_eps);
+    }
+    // ---- backward through the Sinkhorn iterations ----
+    float g[NN];
+#pragma unroll
+    for (int e = 0; e < NN; ++e) g[e] = gcomb[t * NN + e];
+    for (int it = sp.iters - 1; it >= 1; --it) {
+      float Q[NN], rs[N], cs[N];
+#pragma unroll
+      for (int e = 0; e < NN; ++e) Q[e] = hist[((int64_t)(it - 1) * NN + e) * T + t];
+      row_norm<N>(Q, sp.hc_eps, rs);       // Q = M_in / rs
+      float U[NN];
+#pragma unroll
+      for (int e = 0; e < NN; ++e) U[e] = Q[e];
+      col_norm<N>(U, sp.hc_eps, cs);       // U = Q / cs
+      // col-norm VJP: dQ = (g - sum_i g*U) / cs
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) s += g[i * N + j] * U[i * N + j];
+#pragma unroll
+        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - s) / cs[j];
+      }
+      // row-norm VJP: dM = (dQ - sum_j dQ*Q) / rs
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < N; ++j) s += g[i * N + j] * Q[i * N + j];
+#pragma unroll
+        for (int j = 0; j < N; ++j) g[i * N + j] = (g[i * N + j] - s) / rs[i];
+      }
+    }
+    // iteration 0: U0 = M0 / cs0, M0 = P + eps
+    {
+      float U[NN], cs[N];
+#pragma unroll
+      for (int e = 0; e < NN; ++e) U[e] = P[e] + sp.hc_eps;
+      col_norm<N>(U, sp.hc_eps, cs);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < N; ++i) s += g[i * N + j] * U[i * N + j];
+#pragma unroll
+        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - s) / cs[j];
+      }
+    }
+    // softmax VJP: dl = P * (dP - sum_j dP*P); clamp passes where min <= l <= max
+    float gmx[HM];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < N; ++j) s += g[i * N + j] * P[i * N + j];
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const int e = i * N + j;
+        float d = P[e] * (g[e] - s);
+        if (sp.clamp_on && !(logits[e] >= sp.clamp_min && logits[e] <= sp.clamp_max)) d = 0.f;
+        gmx[2 * N + e] = d * sp.a2;
+        contrib[2] = fmaf(d, mix[2 * N + e], contrib[2]);
+        contrib[3 + 2 * N + e] = d;
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+      const float s0 = sigmoidf_(mix[n] * sp.a0 + sbase[n]);
+      const float s1 = sigmoidf_(mix[N + n] * sp.a1 + sbase[N + n]);
+      const float dz0 = gpre[t * N + n] * s0 * (1.0f - s0);
+      const float dz1 = gpost[t * N + n] * 2.0f * s1 * (1.0f - s1);
+      gmx[n] = dz0 * sp.a0;
+      gmx[N + n] = dz1 * sp.a1;
+      contrib[0] = fmaf(dz0, mix[n], contrib[0]);
+      contrib[1] = fmaf(dz1, mix[N + n], contrib[1]);
+      contrib[3 + n] = dz0;
+      contrib[3 + N + n] = dz1;
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < HM; ++k) {
+      gm_out[t * HM + k] = gmx[k];
+      dot = fmaf(gmx[k], mix[k], dot);
+    }
+    const float inv = inv_rms[t];
+    coef_out[t] = inv * inv / (float)HC * dot;
+  }
+#pragma unroll
+  for (int i = 0; i < NP; ++i) red[threadIdx.x][i] = contrib[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < NP; i += blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < 128; ++r) s += red[r][i];
+    partials[(int64_t)blockIdx.x * NP + i] = s;
+  }
+}
+
+__global__ void pre_reduce_ab_kernel(const float* __restrict__ partials, int nblk, int HM,
+                                     float* __restrict__ grad_alpha,
+                                     float* __restrict__ grad_base) {
+  const int NP = 3 + HM;
+  for (int i = threadIdx.x; i < NP; i += blockDim.x) {
+    float s = 0.f;
+    for (int b = 0; b < nblk; ++b) s += partials[(int64_t)b * NP + i];
+    if (i < 3) grad_alpha[i] = s;
+    else grad_base[i - 3] = s;
+  }
+}
+
+constexpr int kGxTT = 16;   // tokens per CTA
+constexpr int kGxCC = 256;  // columns per CTA (one per thread)
+
+template <typename E, int N>
+__global__ void __launch_bounds__(kGxCC)
+pre_bwd_gx_kernel(const E* __restrict__ x, const E* __restrict__ gy,
+                  const float* __restrict__ phi, const float* __restrict__ gm,
+                  const float* __restrict__ inv_rms, const float* __restrict__ coef,
+                  const float* __restrict__ pre, E* __restrict__ gx, int64_t T, int64_t D) {
+  constexpr int HM = hc_mix(N);
+  const int64_t HC = (int64_t)N * D;
+  __shared__ float sgm[kGxTT][HM];
+  __shared__ float sinv[kGxTT], scoef[kGxTT], spre[kGxTT][N];
+  const int64_t t0 = (int64_t)blockIdx.x * kGxTT;
+  for (int i = threadIdx.x; i < kGxTT * HM; i += blockDim.x) {
+    const int64_t t = t0 + i / HM;
+    sgm[i / HM][i % HM] = t < T ? gm[t * HM + i % HM] : 0.f;
+  }
+  for (int i = threadIdx.x; i < kGxTT; i += blockDim.x) {
+    const int64_t t = t0 + i;
+    sinv[i] = t < T ? inv_rms[t] : 0.f;
+    scoef[i] = t < T ? coef[t] : 0.f;
+  }
+  for (int i = threadIdx.x; i < kGxTT * N; i += blockDim.x) {
+    const int64_t t = t0 + i / N;
+    spre[i / N][i % N] = t < T ? pre[t * N + i % N] : 0.f;
+  }
+  __syncthreads();
+  const int64_t c = (int64_t)blockIdx.y * kGxCC + threadIdx.x;
+  if (c >= HC) return;
+  const int n = (int)(c / D);
+  const int64_t d = c - (int64_t)n * D;
+  float ph[HM];
+#pragma unroll
+  for (int k = 0; k < HM; ++k) ph[k] = __ldg(phi + (int64_t)k * HC + c);
+  for (int tt = 0; tt < kGxTT; ++tt) {
+    const int64_t t = t0 + tt;
+    if (t >= T) break;
+    float gxs = 0.f;
+#pragma unroll
+    for (int k = 0; k < HM; ++k) gxs = fmaf(sgm[tt][k], ph[k], gxs);
+    const float xv = ld1<E>(x + t * HC + c);
+    const float g = ld1<E>(gy + t * D + d);
+    const float r = fmaf(sinv[tt], gxs, -scoef[tt] * xv);
+    st1<E>(gx + t * HC + c, fmaf(g, spre[tt][n], r));
+  }
+}
+
+constexpr int kGpCC = 256;  // columns per CTA
+constexpr int kGpTS = 32;   // tokens staged per step
+
+template <typename E, int N>
+__global__ void __launch_bounds__(kGpCC)
+pre_bwd_gphi_kernel(const E* __restrict__ x, const float* __restrict__ gm,
+                    const float* __restrict__ inv_rms, float* __restrict__ part, int64_t T,
+                    int64_t HC, int64_t tokens_per_split) {
+  constexpr int HM = hc_mix(N);
+  __shared__ float sg[kGpTS][HM];
+  const int64_t c = (int64_t)blockIdx.x * kGpCC + threadIdx.x;
+  const int64_t tb = (int64_t)blockIdx.y * tokens_per_split;
+  const int64_t te = min(T, tb + tokens_per_split);
+  float acc[HM];
+#pragma unroll
+  for (int k = 0; k < HM; ++k) acc[k] = 0.f;
+  for (int64_t ts = tb; ts < te; ts += kGpTS) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kGpTS * HM; i += blockDim.x) {
+      const int64_t t = ts + i / HM;
+      sg[i / HM][i % HM] = t < te ? gm[t * HM + i % HM] * inv_rms[t] : 0.f;
+    }
+    __syncthreads();
+    if (c < HC) {
+      const int nt = (int)min((int64_t)kGpTS, te - ts);
+      for (int tt = 0; tt < nt; ++tt) {
+        const float xv = ld1<E>(x + (ts + tt) * HC + c);
+#pragma unroll
+        for (int k = 0; k < HM; ++k) acc[k] = fmaf(sg[tt][k], xv, acc[k]);
+      }
+    }
+  }
+  if (c < HC) {
+#pragma unroll
+    for (int k = 0; k < HM; ++k) part[((int64_t)blockIdx.y * HM + k) * HC + c] = acc[k];
+  }
+}
+
+__global__ void pre_reduce_gphi_kernel(const float* __restrict__ part, int nsplit, int64_t n,
+                                       float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = 0.f;
+  for (int p = 0; p < nsplit; ++p) s += part[(int64_t)p * n + i];
+  out[i] = s;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static int gphi_splits(int64_t T) {
+  int64_t s = cdiv(T, 2048);
+  return (int)(s < 1 ? 1 : (s > 16 ? 16 : s));
+}
+
+struct BwdWs {
+  float *gpre, *gm, *coef, *partials, *hist, *gphi_part;
+  size_t total;
+};
+
+static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t iters) {
+  const int HM = hc_mix(N);
+  const int64_t HC = (int64_t)N * D;
+  const int64_t nblk = cdiv(T, 128);
+  const int64_t hist_n = (int64_t)(iters > 1 ? iters - 1 : 0) * N * N * T;
+  BwdWs w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { float* p = (float*)(base + off); off += align_up(bytes); return p; };
+  w.gpre = take((size_t)T * N * 4);
+  w.gm = take((size_t)T * HM * 4);
+  w.coef = take((size_t)T * 4);
+  w.partials = take((size_t)nblk * (3 + HM) * 4);
+  w.hist = take((size_t)hist_n * 4);
+  w.gphi_part = take((size_t)gphi_splits(T) * HM * HC * 4);
+  w.total = off;
+  return w;
+}
+
+size_t pre_bwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype, int32_t iters) {
+  (void)dtype;
+  return bwd_layout(nullptr, T, N, D, iters).total;
+}
+
+template <typename E, int N>
+static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
+  constexpr int HM = hc_mix(N);
+  const int64_t T = a.T, D = a.D, HC = (int64_t)N * D;
+  BwdWs w = bwd_layout((char*)a.workspace, T, N, D, a.sp.iters);
+  const int nblk = (int)cdiv(T, 128);
+  if (T == 0) {
+    MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_alpha, 0, 3 * sizeof(float), s));
+    MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_base, 0, HM * sizeof(float), s));
+    MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_phi, 0, (size_t)HM * HC * sizeof(float), s));
+    return MHC_OK;
+  }
+  const bool vec = (D % Pack<E>::n == 0) && aligned16(a.x) && aligned16(a.grad_y);
+  const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;
+  dim3 sgrid((unsigned)(want < cap ? want : cap));
+  if (vec)
+    pre_bwd_dots_kernel<E, N, true><<<sgrid, 256, 0, s>>>((const E*)a.x, (const E*)a.grad_y,
+                                                          w.gpre, T, D);
+  else
+    pre_bwd_dots_kernel<E, N, false><<<sgrid, 256, 0, s>>>((const E*)a.x, (const E*)a.grad_y,
+                                                           w.gpre, T, D);
+  MHC_LAUNCH_CHECK();
+  pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(a.mixes, a.alpha, a.base, w.gpre, a.grad_post,
+                                               a.grad_comb, a.inv_rms, T, HC, a.sp, w.hist,
+                                               w.gm, w.coef, w.partials);
+  MHC_LAUNCH_CHECK();
+  pre_reduce_ab_kernel<<<1, 128, 0, s>>>(w.partials, nblk, HM, a.grad_alpha, a.grad_base);
+  MHC_LAUNCH_CHECK();
+  dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
+  pre_bwd_gx_kernel<E, N><<<ggrid, kGxCC, 0, s>>>((const E*)a.x, (const E*)a.grad_y, a.phi,
+                                                  w.gm, a.inv_rms, w.coef, a.pre,
+                                                  (E*)a.grad_x, T, D);
+  MHC_LAUNCH_CHECK();
+  const int ns = gphi_splits(T);
+  const int64_t tps = cdiv(T, ns);
+  dim3 pgrid((unsigned)cdiv(HC, kGpCC), (unsigned)ns);
+  pre_bwd_gphi_kernel<E, N><<<pgrid, kGpCC, 0, s>>>((const E*)a.x, w.gm, a.inv_rms,
+                                                    w.gphi_part, T, HC, tps);
+  MHC_LAUNCH_CHECK();
+  const int64_t n = (int64_t)HM * HC;
+  pre_reduce_gphi_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.gphi_part, ns, n, a.grad_phi);
+  MHC_LAUNCH_CHECK();
+  return MHC_OK;
+}
+
+template <int N>
+static int pre_bwd_n(const PreBwdArgs& a, cudaStream_t s) {
+  switch (a.dtype) {
+    case MHC_F32: return pre_bwd_impl<float, N>(a, s);
+    case MHC_F16: return pre_bwd_impl<__half, N>(a, s);
+    case MHC_BF16: return pre_bwd_impl<__nv_bfloat16, N>(a, s);
+    default: return MHC_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int pre_bwd_dispatch(const PreBwdArgs& a, cudaStream_t s) { MHC_DISPATCH_N(a.N, pre_bwd_n, a, s); }
+
+}  // namespace mhc

@@ -1,0 +1,86 @@
+// pre_common.cuh -- argument blocks and per-token helpers of the pre operator.
+#pragma once
+#include "common.cuh"
+
+namespace mhc {
+
+struct PreFwdArgs {
+  const void* x;
+  const float* phi;
+  const float* alpha;
+  const float* base;
+  int64_t T, D;
+  int32_t N, dtype;
+  float norm_eps;
+  SmallParams sp;
+  void* y;
+  float* post_out;
+  float* comb_frag;
+  float* inv_rms;
+  float* x_scaled;      // may be null
+  float* mixes;
+  float* h_res_logits;  // may be null
+  float* pre;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+struct PreBwdArgs {
+  const void* x;
+  const float* phi;
+  const float* alpha;
+  const float* base;
+  const float* inv_rms;
+  const float* mixes;
+  const float* pre;
+  const void* grad_y;
+  const float* grad_post;
+  const float* grad_comb;
+  int64_t T, D;
+  int32_t N, dtype;
+  SmallParams sp;
+  void* grad_x;
+  float* grad_phi;
+  float* grad_alpha;
+  float* grad_base;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+// inv_rms = rsqrt(mean(x^2) + eps) over the N*D row (src/mhc_pre_clamp_sinkhorn.py:987-988)
+__device__ __forceinline__ float inv_rms_from_sumsq(float sumsq, int64_t HC, float eps) {
+  const float ms = sumsq / (float)HC;
+  return 1.0f / sqrtf(ms + eps);
+}
+
+// Forward small stage of one token plus the stores of its per-token outputs.
+template <int N>
+__device__ __forceinline__ void small_outputs(const float* mix, const float* base,
+                                              const SmallParams& sp, int64_t t, float inv,
+                                              float* inv_rms, float* mixes, float* pre,
+                                              float* post, float* comb, float* logits_out) {
+  constexpr int HM = hc_mix(N);
+  float pr[N], po[N], lg[N * N], M[N * N];
+  small_forward<N>(mix, base, sp, pr, po, lg, M);
+  inv_rms[t] = inv;
+#pragma unroll
+  for (int k = 0; k < HM; ++k) mixes[t * HM + k] = mix[k];
+#pragma unroll
+  for (int n = 0; n < N; ++n) {
+    pre[t * N + n] = pr[n];
+    post[t * N + n] = po[n];
+  }
+#pragma unroll
+  for (int e = 0; e < N * N; ++e) comb[t * N * N + e] = M[e];
+  if (logits_out) {
+#pragma unroll
+    for (int e = 0; e < N * N; ++e) logits_out[t * N * N + e] = lg[e];
+  }
+}
+
+size_t pre_fwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype);
+size_t pre_bwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype, int32_t iters);
+int pre_fwd_dispatch(const PreFwdArgs& a, cudaStream_t s);
+int pre_bwd_dispatch(const PreBwdArgs& a, cudaStream_t s);
+
+}  // namespace mhc

@@ -1,0 +1,139 @@
+/*
+ * mhc_b200.h -- C ABI of the B200 (sm_100a) mHC operator library.
+ *
+ * The reference (liuhycs/FlagOS-mhc) exposes these operators only as Python
+ * functions on torch tensors; it has no FFI.  Each entry point below is the
+ * device-side body of one of those Python functions, reduced to plain device
+ * pointers, sizes and a CUDA stream, so any host language can bind it
+ * (ctypes / cffi / cgo / JNI).  Tensor allocation stays with the caller.
+ *
+ * Conventions
+ *   - All pointers are device pointers of contiguous row-major tensors.
+ *     Tokens are flattened: a (B,S,N,D) tensor is passed as (T=B*S,N,D).
+ *   - `dtype` names the element type of x / h_out / out / grad_y / grad_x /
+ *     grad_h_out / y (MHC_F32, MHC_F16, MHC_BF16).  Every other tensor is fp32.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     stream-ordered, never synchronise the host and are safe to call
+ *     concurrently on different streams; the only process-wide state is a
+ *     per-device attribute cache and the launch counter below.
+ *   - Return value: 0 (MHC_OK) or an MHC_ERR_* code; mhc_status_string()
+ *     turns it into text.  Argument checks run before any launch, so a
+ *     non-zero return from a check leaves every output untouched.
+ */
+#ifndef MHC_B200_H_
+#define MHC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mhc_dtype { MHC_F32 = 0, MHC_F16 = 1, MHC_BF16 = 2 };
+
+enum mhc_status {
+  MHC_OK = 0,
+  MHC_ERR_INVALID_ARGUMENT = 1,  /* bad size, null pointer, bad scalar     */
+  MHC_ERR_UNSUPPORTED_N = 2,     /* hcMult outside 1..8                     */
+  MHC_ERR_UNSUPPORTED_DTYPE = 3, /* dtype not one of enum mhc_dtype         */
+  MHC_ERR_WORKSPACE = 4,         /* workspace null / too small / misaligned */
+  MHC_ERR_CUDA = 5,              /* a CUDA runtime call or launch failed    */
+  MHC_ERR_DEVICE = 6,            /* current device is not sm_100            */
+  MHC_ERR_TIMEOUT = 7            /* a bounded device-side wait gave up      */
+};
+
+/* Text for a status code (static storage). */
+const char* mhc_status_string(int status);
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int mhc_version(void);
+
+/* Running count of CUDA kernels this library has launched in this process
+ * (all devices, all threads).  Diagnostic: lets a caller verify that the
+ * device path ran.  No counterpart in the reference. */
+uint64_t mhc_kernel_launches(void);
+
+/*
+ * mhc_post forward.  Replaces the device work of `mhc_post`
+ * (src/mhc_post.py:296-341, kernels :24-96 and :207-271):
+ *   out[t,i,d] = sum_j h_res[t,j,i] * x[t,j,d] + h_post[t,i] * h_out[t,d]
+ * x, out: (T,N,D) dtype.  h_res: (T,N,N) fp32.  h_out: (T,D) dtype.
+ * h_post: (T,N) fp32.  Accumulation in fp32, one rounding on store.
+ */
+int mhc_post_fwd(const void* x, const float* h_res, const void* h_out,
+                 const float* h_post, void* out, int64_t T, int32_t N,
+                 int64_t D, int32_t dtype, void* stream);
+
+/*
+ * mhc_post backward.  Replaces `mhc_post_backward`
+ * (src/mhc_post_backward.py:593-621, kernel :293-421):
+ *   grad_x[t,j,d]    = sum_i h_res[t,j,i] * grad_y[t,i,d]     (dtype)
+ *   grad_h_res[t,j,i]= sum_d x[t,j,d] * grad_y[t,i,d]         (fp32)
+ *   grad_h_out[t,d]  = sum_i h_post[t,i] * grad_y[t,i,d]      (dtype)
+ *   grad_h_post[t,i] = sum_d h_out[t,d] * grad_y[t,i,d]       (fp32)
+ */
+int mhc_post_bwd(const void* grad_y, const void* x, const float* h_res,
+                 const void* h_out, const float* h_post, void* grad_x,
+                 float* grad_h_res, void* grad_h_out, float* grad_h_post,
+                 int64_t T, int32_t N, int64_t D, int32_t dtype,
+                 void* stream);
+
+/* Bytes of device workspace mhc_pre_fwd needs for these sizes. */
+size_t mhc_pre_fwd_workspace_bytes(int64_t T, int32_t N, int64_t D,
+                                   int32_t dtype);
+
+/*
+ * mhc_pre_clamp_sinkhorn forward.  Replaces `mhc_pre_clamp_sinkhorn`
+ * (src/mhc_pre_clamp_sinkhorn.py:857-971; semantics :974-1022):
+ *   inv = rsqrt(mean(x^2) + norm_eps) over N*D;  mixes = (x*inv) phi^T
+ *   pre = sigmoid(mixes[:N]*a0 + b[:N]) + hc_eps
+ *   post_out = 2*sigmoid(mixes[N:2N]*a1 + b[N:2N])
+ *   logits = mixes[2N:]*a2 + b[2N:]  (N,N), clamped iff clamp_min!=0||clamp_max!=0
+ *   comb = Sinkhorn(softmax_row(logits)), iter_times iterations
+ *   y[t,d] = sum_n x[t,n,d] * pre[t,n]
+ * x: (T,N,D) dtype; phi: (N*(N+2), N*D) fp32; alpha (3,); base (N*(N+2),).
+ * Outputs: y (T,D) dtype; post_out (T,N); comb_frag (T,N,N); inv_rms (T,);
+ * mixes (T,N*(N+2)); pre (T,N); optional (may be NULL): x_scaled (T,N*D),
+ * h_res_logits (T,N,N, pre-clamp).  workspace: >= mhc_pre_fwd_workspace_bytes,
+ * 256-byte aligned; its contents on entry do not matter.
+ */
+int mhc_pre_fwd(const void* x, const float* phi, const float* alpha,
+                const float* base, int64_t T, int32_t N, int64_t D,
+                int32_t dtype, float norm_eps, float hc_eps, float clamp_min,
+                float clamp_max, int32_t iter_times, void* y, float* post_out,
+                float* comb_frag, float* inv_rms, float* x_scaled,
+                float* mixes, float* h_res_logits, float* pre, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* Bytes of device workspace mhc_pre_bwd needs for these sizes. */
+size_t mhc_pre_bwd_workspace_bytes(int64_t T, int32_t N, int64_t D,
+                                   int32_t dtype, int32_t iter_times);
+
+/*
+ * mhc_pre_clamp_sinkhorn backward.  Replaces
+ * `mhc_pre_clamp_sinkhorn_backward`
+ * (src/mhc_pre_clamp_sinkhorn_backward.py:1292-1391; oracle :1397-1453).
+ * Inputs are the tensors the forward saved (x, phi, alpha, base, inv_rms,
+ * mixes, pre) and the upstream grads grad_y (T,D) dtype, grad_post_out (T,N),
+ * grad_comb_frag (T,N,N).  x_scaled and h_res_logits are not needed: the
+ * kernels recompute x*inv_rms on the fly and the logits from mixes.
+ * Outputs: grad_x (T,N,D) dtype; grad_phi (N*(N+2), N*D); grad_alpha (3,);
+ * grad_base (N*(N+2),).  All reductions run in a fixed order (no float
+ * atomics), so the result is bitwise reproducible run to run.
+ */
+int mhc_pre_bwd(const void* x, const float* phi, const float* alpha,
+                const float* base, const float* inv_rms, const float* mixes,
+                const float* pre, const void* grad_y,
+                const float* grad_post_out, const float* grad_comb_frag,
+                int64_t T, int32_t N, int64_t D, int32_t dtype,
+                float norm_eps, float hc_eps, float clamp_min, float clamp_max,
+                int32_t iter_times, void* grad_x, float* grad_phi,
+                float* grad_alpha, float* grad_base, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MHC_B200_H_ */

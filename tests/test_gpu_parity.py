@@ -1,0 +1,254 @@
+"""CUDA kernels vs the CPU oracle (and the reference goldens) on the same seeded
+inputs.  Tolerances: fp32 outputs <= 1e-5 normwise relative; bf16/fp16 outputs
+<= 2e-2 normwise relative; Sinkhorn matrices <= 1e-4 absolute."""
+import pytest
+import torch
+
+import FlagOS_mhc as M
+from oracle import mhc_oracle as O
+from tests._util import (TOL_BF16, TOL_FP32, TOL_SINKHORN_ABS, abs_err, golden_cases,
+                         load_golden, rel_err)
+from tests.gen import post_inputs, pre_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+F64 = torch.float64
+
+
+def _tol(dt):
+    return TOL_FP32 if dt == torch.float32 else TOL_BF16
+
+
+# ---------------------------------------------------------------- goldens
+@pytest.mark.parametrize("path", golden_cases("post"), ids=lambda p: p.split("/")[-1])
+def test_post_golden(path):
+    t, dt, _ = load_golden(path)
+    x, ho, gy = (t[k].to(dt).to(DEV) for k in ("x", "h_out", "grad_y"))
+    hr, hp = t["h_res"].to(DEV), t["h_post"].to(DEV)
+    y = M.mhc_post(x, hr, ho, hp)
+    assert y.dtype == dt and y.shape == x.shape
+    assert rel_err(y, t["y"]) <= _tol(dt)
+    gx, ghr, gho, ghp = M.mhc_post_backward(gy, x, hr, ho, hp)
+    assert rel_err(gx, t["grad_x"]) <= _tol(dt)
+    assert rel_err(gho, t["grad_h_out"]) <= _tol(dt)
+    assert rel_err(ghr, t["grad_h_res"]) <= TOL_FP32
+    assert rel_err(ghp, t["grad_h_post"]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("path", golden_cases("pre"), ids=lambda p: p.split("/")[-1])
+def test_pre_golden(path):
+    t, dt, sc = load_golden(path)
+    kw = dict(norm_eps=sc["norm_eps"], hc_eps=sc["hc_eps"], clamp_min=sc["clamp_min"],
+              clamp_max=sc["clamp_max"], iter_times=int(sc["iter_times"]))
+    x, gy = t["x"].to(dt).to(DEV), t["grad_y"].to(dt).to(DEV)
+    phi, alpha, base = (t[k].to(DEV) for k in ("phi", "alpha", "base"))
+    out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **kw)
+    assert rel_err(out["y"], t["y"]) <= _tol(dt)
+    for k in ("post_out", "inv_rms", "mixes", "h_res_logits", "pre"):
+        assert rel_err(out[k], t[k]) <= TOL_FP32, k
+    assert abs_err(out["comb_frag"], t["comb_frag"]) <= TOL_SINKHORN_ABS
+    gx, gphi, ga, gb = M.mhc_pre_clamp_sinkhorn_backward(
+        x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+        out["h_res_logits"], out["pre"], gy, t["grad_post_out"].to(DEV),
+        t["grad_comb_frag"].to(DEV), **kw)
+    assert rel_err(gx, t["grad_x"]) <= _tol(dt)
+    assert rel_err(gphi, t["grad_phi"]) <= TOL_FP32 * 4
+    assert rel_err(ga, t["grad_alpha"]) <= TOL_FP32 * 4
+    assert rel_err(gb, t["grad_base"]) <= TOL_FP32 * 4
+
+
+# ---------------------------------------------------------------- oracle sweeps
+POST_SHAPES = [(1, 4, 64), (3, 4, 7168), (63, 4, 200), (65, 4, 1000), (37, 8, 256),
+               (17, 1, 48), (9, 2, 24), (11, 3, 40), (7, 5, 72), (6, 6, 96), (5, 7, 80),
+               (40, 4, 1), (13, 4, 7)]
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("T,N,D", POST_SHAPES)
+def test_post_vs_oracle(T, N, D, dt):
+    x, hr, ho, hp, gy = post_inputs(T, N, D, dt, seed=T * 31 + N * 7 + D)
+    y = M.mhc_post(x.to(DEV), hr.to(DEV), ho.to(DEV), hp.to(DEV))
+    ref = O.post_fwd(x, hr, ho, hp, dtype=F64)
+    assert rel_err(y, ref) <= _tol(dt)
+    got = M.mhc_post_backward(gy.to(DEV), x.to(DEV), hr.to(DEV), ho.to(DEV), hp.to(DEV))
+    want = O.post_bwd(gy, x, hr, ho, hp, dtype=F64)
+    for a, b, tol in zip(got, want, (_tol(dt), TOL_FP32, _tol(dt), TOL_FP32)):
+        assert a.shape == b.shape
+        assert rel_err(a, b) <= tol
+
+
+def test_post_4d_and_unaligned_views():
+    B, S, N, D = 2, 5, 4, 136
+    x, hr, ho, hp, gy = post_inputs(B * S, N, D, torch.bfloat16, seed=11)
+    x4, hr4, ho4, hp4, gy4 = (x.reshape(B, S, N, D), hr.reshape(B, S, N, N),
+                              ho.reshape(B, S, D), hp.reshape(B, S, N), gy.reshape(B, S, N, D))
+    y = M.mhc_post(x4.to(DEV), hr4.to(DEV), ho4.to(DEV), hp4.to(DEV))
+    assert y.shape == (B, S, N, D)
+    assert rel_err(y, O.post_fwd(x4, hr4, ho4, hp4, dtype=F64)) <= TOL_BF16
+    # a non-contiguous x (every other token) goes through the flatten path
+    xs = torch.randn(2 * B * S, N, D).to(torch.bfloat16)[::2]
+    y2 = M.mhc_post(xs.to(DEV), hr.to(DEV), ho.to(DEV), hp.to(DEV))
+    assert rel_err(y2, O.post_fwd(xs.contiguous(), hr, ho, hp, dtype=F64)) <= TOL_BF16
+    g = M.mhc_post_backward(gy4.to(DEV), x4.to(DEV), hr4.to(DEV), ho4.to(DEV), hp4.to(DEV))
+    assert g[0].shape == (B, S, N, D) and g[2].shape == (B, S, D)
+
+
+PRE_SHAPES = [(1, 4, 64), (5, 4, 7168), (63, 4, 256), (130, 4, 64), (9, 8, 64), (7, 1, 32),
+              (11, 2, 40), (6, 3, 24), (5, 5, 16), (4, 6, 32), (3, 7, 24), (33, 4, 36)]
+
+
+@pytest.mark.parametrize("clamp", [(0.0, 0.0), (-1.0, 1.0)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T,N,D", PRE_SHAPES)
+def test_pre_vs_oracle(T, N, D, dt, clamp):
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, dt, seed=T * 13 + N * 5 + D,
+                                                       phi_std=2.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=clamp[0], clamp_max=clamp[1], iter_times=20)
+    out = M.mhc_pre_clamp_sinkhorn(x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV),
+                                   need_backward=True, **kw)
+    ref = O.pre_fwd(x, phi, alpha, base, dtype=F64, **kw)
+    assert rel_err(out["y"], ref["y"]) <= _tol(dt)
+    for k in ("post_out", "inv_rms", "mixes", "h_res_logits", "pre", "x_scaled"):
+        assert rel_err(out[k], ref[k]) <= TOL_FP32, k
+    assert abs_err(out["comb_frag"], ref["comb_frag"]) <= TOL_SINKHORN_ABS
+    got = M.mhc_pre_clamp_sinkhorn_backward(
+        x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV), out["inv_rms"], out["x_scaled"],
+        out["mixes"], out["h_res_logits"], out["pre"], gy.to(DEV), gpost.to(DEV),
+        gcomb.to(DEV), **kw)
+    # the backward mirrors the reference's: it starts from the saved forward tensors
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=clamp[0], clamp_max=clamp[1], iter_times=20,
+                                dtype=F64)
+    assert rel_err(got[0], want[0]) <= _tol(dt)
+    for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
+        assert rel_err(a, b) <= TOL_FP32, name
+
+
+@pytest.mark.parametrize("iters", [0, 1, 2, 7, 33])
+def test_pre_iteration_counts(iters):
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(40, 4, 64, torch.bfloat16, seed=iters)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-3.0, clamp_max=3.0, iter_times=iters)
+    out = M.mhc_pre_clamp_sinkhorn(x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV),
+                                   need_backward=True, **kw)
+    ref = O.pre_fwd(x, phi, alpha, base, dtype=F64, **kw)
+    assert abs_err(out["comb_frag"], ref["comb_frag"]) <= TOL_SINKHORN_ABS
+    got = M.mhc_pre_clamp_sinkhorn_backward(
+        x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV), out["inv_rms"], out["x_scaled"],
+        out["mixes"], out["h_res_logits"], out["pre"], gy.to(DEV), gpost.to(DEV),
+        gcomb.to(DEV), **kw)
+    want = O.pre_bwd(x, phi, alpha, base, gy, gpost, gcomb, dtype=F64, **kw)
+    assert rel_err(got[0], want[0]) <= TOL_BF16
+    for a, b in zip(got[1:], want[1:]):
+        assert rel_err(a, b) <= 1e-4
+
+
+def test_pre_need_backward_false_matches_ref_semantics():
+    """Unlike the reference fast path (which always clamps and runs 20 iterations
+    when need_backward=False), the result follows the _ref semantics."""
+    x, phi, alpha, base, *_ = pre_inputs(70, 4, 64, torch.bfloat16, seed=5, phi_std=0.3)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=0.0, clamp_max=0.0, iter_times=3)
+    out = M.mhc_pre_clamp_sinkhorn(x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV), **kw)
+    assert set(out) == {"y", "post_out", "comb_frag"}
+    ref = O.pre_fwd(x, phi, alpha, base, dtype=F64, **kw)
+    assert abs_err(out["comb_frag"], ref["comb_frag"]) <= TOL_SINKHORN_ABS
+
+
+def test_pre_empty_token_range():
+    x = torch.empty(0, 4, 64, dtype=torch.bfloat16, device=DEV)
+    phi = torch.randn(24, 256, device=DEV)
+    out = M.mhc_pre_clamp_sinkhorn(x, phi, torch.ones(3, device=DEV), torch.zeros(24, device=DEV),
+                                   need_backward=True)
+    assert out["y"].shape == (0, 64)
+    g = M.mhc_pre_clamp_sinkhorn_backward(
+        x, phi, torch.ones(3, device=DEV), torch.zeros(24, device=DEV), out["inv_rms"],
+        out["x_scaled"], out["mixes"], out["h_res_logits"], out["pre"],
+        torch.empty(0, 64, dtype=torch.bfloat16, device=DEV), torch.empty(0, 4, device=DEV),
+        torch.empty(0, 4, 4, device=DEV))
+    assert g[0].shape == (0, 4, 64) and float(g[1].abs().sum()) == 0.0
+
+
+# ---------------------------------------------------------------- autograd
+def test_autograd_wrappers_match_oracle():
+    T, N, D = 24, 4, 128
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=9)
+    xd = x.to(DEV).requires_grad_(True)
+    phid, ad, bd = (t.to(DEV).requires_grad_(True) for t in (phi, alpha, base))
+    y, post, comb = M.mhc_pre_clamp_sinkhorn_fn(xd, phid, ad, bd, clamp_min=-5.0, clamp_max=5.0)
+    loss = (y.float() * gy.to(DEV).float()).sum() + (post * gpost.to(DEV)).sum() + \
+        (comb * gcomb.to(DEV)).sum()
+    loss.backward()
+    want = O.pre_bwd(x, phi, alpha, base, gy, gpost, gcomb, clamp_min=-5.0, clamp_max=5.0,
+                     dtype=F64)
+    assert rel_err(xd.grad, want[0]) <= TOL_BF16
+    assert rel_err(phid.grad, want[1]) <= 1e-4
+    # mhc_post through autograd
+    x2, hr, ho, hp, gy2 = post_inputs(T, N, D, torch.bfloat16, seed=10)
+    leaves = [t.to(DEV).requires_grad_(True) for t in (x2, hr, ho, hp)]
+    out = M.mhc_post_fn(*leaves)
+    out.backward(gy2.to(DEV))
+    want = O.post_bwd(gy2, x2, hr, ho, hp, dtype=F64)
+    for leaf, w in zip(leaves, want):
+        assert rel_err(leaf.grad, w) <= TOL_BF16
+
+
+# ---------------------------------------------------------------- full-size properties
+def test_post_full_size_token_sample():
+    """Config C2 (T=32768, N=4, D=7168 bf16): tokens are independent, so a
+    random sample of tokens checked against the oracle covers the full launch."""
+    T, N, D = 32768, 4, 7168
+    x, hr, ho, hp, gy = post_inputs(T, N, D, torch.bfloat16, seed=2, device=DEV)
+    y = M.mhc_post(x, hr, ho, hp)
+    g = M.mhc_post_backward(gy, x, hr, ho, hp)
+    idx = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:48]
+    s = lambda t: t[idx.to(t.device)].cpu()  # noqa: E731
+    assert rel_err(s(y), O.post_fwd(s(x), s(hr), s(ho), s(hp), dtype=F64)) <= TOL_BF16
+    want = O.post_bwd(s(gy), s(x), s(hr), s(ho), s(hp), dtype=F64)
+    for a, b, tol in zip(g, want, (TOL_BF16, TOL_FP32, TOL_BF16, TOL_FP32)):
+        assert rel_err(s(a), b) <= tol
+
+
+def test_pre_full_size_sample_and_linearity():
+    """Config C3 shapes (N=4, D=7168).  Per-token outputs: a token sample against
+    the oracle.  grad_phi/alpha/base are sums over tokens: the full-range result
+    equals the sum of the results over two halves (linearity)."""
+    T, N, D = 8192, 4, 7168
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=3,
+                                                       device=DEV)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
+    out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **kw)
+    idx = torch.randperm(T, generator=torch.Generator().manual_seed(1))[:24].to(DEV)
+    ref = O.pre_fwd(x[idx].cpu(), phi.cpu(), alpha.cpu(), base.cpu(), dtype=F64, **kw)
+    for k in ("post_out", "mixes", "pre", "inv_rms"):
+        assert rel_err(out[k][idx], ref[k]) <= TOL_FP32, k
+    assert abs_err(out["comb_frag"][idx], ref["comb_frag"]) <= TOL_SINKHORN_ABS
+    assert rel_err(out["y"][idx], ref["y"]) <= TOL_BF16
+
+    def bwd(sl):
+        return M.mhc_pre_clamp_sinkhorn_backward(
+            x[sl], phi, alpha, base, out["inv_rms"][sl], out["x_scaled"][sl], out["mixes"][sl],
+            out["h_res_logits"][sl], out["pre"][sl], gy[sl], gpost[sl], gcomb[sl], **kw)
+    full = bwd(slice(0, T))
+    h1, h2 = bwd(slice(0, T // 2)), bwd(slice(T // 2, T))
+    for i in (1, 2, 3):
+        assert rel_err(full[i], h1[i].double() + h2[i].double()) <= 2e-5
+    assert torch.equal(full[0][: T // 2], h1[0])
+    want = O.pre_bwd_from_saved(x[idx].cpu(), phi.cpu(), alpha.cpu(), base.cpu(),
+                                out["inv_rms"][idx].cpu(), out["mixes"][idx].cpu(),
+                                out["pre"][idx].cpu(), gy[idx].cpu(), gpost[idx].cpu(),
+                                gcomb[idx].cpu(), hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0,
+                                iter_times=20, dtype=F64)
+    assert rel_err(full[0][idx], want[0]) <= TOL_BF16
+
+
+def test_deterministic_backward():
+    T, N, D = 4096, 4, 1024
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=12,
+                                                       device=DEV)
+    out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True)
+    args = (x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+            out["h_res_logits"], out["pre"], gy, gpost, gcomb)
+    a = M.mhc_pre_clamp_sinkhorn_backward(*args)
+    b = M.mhc_pre_clamp_sinkhorn_backward(*args)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
