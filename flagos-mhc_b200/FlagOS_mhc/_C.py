@@ -26,6 +26,7 @@ MHC_ERR_WORKSPACE = 4
 MHC_ERR_CUDA = 5
 MHC_ERR_DEVICE = 6
 MHC_ERR_TIMEOUT = 7
+MHC_ERR_SCRATCH_LIMIT = 8
 
 _vp, _fp = ctypes.c_void_p, ctypes.c_void_p
 _i64, _i32, _f32, _sz = ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_size_t
@@ -41,6 +42,9 @@ _SIGS = {
     "mhc_pre_fwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _i64, _i32, _i64, _i32, _f32, _f32, _f32,
                                    _f32, _i32, _vp, _fp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _sz,
                                    _vp]),
+    "mhc_pre_fwd_noalloc": (ctypes.c_int, [_vp, _fp, _fp, _fp, _i64, _i32, _i64, _i32, _f32, _f32,
+                                           _f32, _f32, _i32, _vp, _fp, _fp, _fp, _fp, _fp, _fp,
+                                           _fp, _vp]),
     "mhc_pre_bwd_workspace_bytes": (_sz, [_i64, _i32, _i64, _i32, _i32]),
     "mhc_pre_bwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp, _i64, _i32,
                                    _i64, _i32, _f32, _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp,

@@ -91,6 +91,8 @@ const char* mhc_status_string(int status) {
     case MHC_ERR_CUDA: return "CUDA error";
     case MHC_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
     case MHC_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    case MHC_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the static array of the no-alloc entry point holds";
     default: return "unknown status";
   }
 }

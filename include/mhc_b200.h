@@ -40,7 +40,8 @@ enum mhc_status {
   MHC_ERR_WORKSPACE = 4,         /* workspace null / too small / misaligned */
   MHC_ERR_CUDA = 5,              /* a CUDA runtime call or launch failed    */
   MHC_ERR_DEVICE = 6,            /* current device is not sm_100            */
-  MHC_ERR_TIMEOUT = 7            /* a bounded device-side wait gave up      */
+  MHC_ERR_TIMEOUT = 7,           /* a bounded device-side wait gave up      */
+  MHC_ERR_SCRATCH_LIMIT = 8      /* needs more than the static scratch holds */
 };
 
 /* Text for a status code (static storage). */
@@ -131,6 +132,30 @@ int mhc_pre_bwd(const void* x, const float* phi, const float* alpha,
                 int32_t iter_times, void* grad_x, float* grad_phi,
                 float* grad_alpha, float* grad_base, void* workspace,
                 size_t workspace_bytes, void* stream);
+
+/* Size of the static device scratch array used by mhc_pre_fwd_noalloc. */
+#define MHC_PRE_FWD_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/*
+ * mhc_pre_fwd_noalloc -- no counterpart in the reference.
+ * Same computation, arguments and outputs as mhc_pre_fwd, but without the
+ * workspace arguments: the scratch lives in a static 16 MiB device array of
+ * this library, so the call allocates no device memory.  For callers that may
+ * not call cudaMalloc where they run the operator (an arena or pooled
+ * allocator that owns the device budget; a cgo/JNI/C binding with no device
+ * allocator).  Returns MHC_ERR_SCRATCH_LIMIT when
+ * mhc_pre_fwd_workspace_bytes(T,N,D,dtype) exceeds the array.  All calls on a
+ * device share the array: calls that overlap on the GPU race.  The first call
+ * on each device looks up the array's address; make it before any stream
+ * capture begins.
+ */
+int mhc_pre_fwd_noalloc(const void* x, const float* phi, const float* alpha,
+                        const float* base, int64_t T, int32_t N, int64_t D,
+                        int32_t dtype, float norm_eps, float hc_eps,
+                        float clamp_min, float clamp_max, int32_t iter_times,
+                        void* y, float* post_out, float* comb_frag,
+                        float* inv_rms, float* x_scaled, float* mixes,
+                        float* h_res_logits, float* pre, void* stream);
 
 #ifdef __cplusplus
 }

@@ -34,7 +34,7 @@ def test_status_strings_and_version():
     from FlagOS_mhc import _C
     L = _C.lib()
     assert L.mhc_version() >= 100
-    for code in range(8):
+    for code in range(9):
         assert len(L.mhc_status_string(code)) > 0
 
 
