@@ -16,6 +16,9 @@ int post_bwd_dispatch(int32_t N, int32_t dtype, const void* gy, const void* x,
                       float* ghres, void* ghout, float* ghpost, int64_t T, int64_t D,
                       cudaStream_t s);
 
+int pre_fwd_tc_device_error();
+int pre_bwd_tc_device_error();
+
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
@@ -100,6 +103,13 @@ const char* mhc_status_string(int status) {
 int mhc_version(void) { return 100; }
 
 uint64_t mhc_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int mhc_device_status(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return MHC_ERR_CUDA;
+  const int a = pre_fwd_tc_device_error();
+  const int b = pre_bwd_tc_device_error();
+  return a != MHC_OK ? a : b;
+}
 
 int mhc_post_fwd(const void* x, const float* h_res, const void* h_out, const float* h_post,
                  void* out, int64_t T, int32_t N, int64_t D, int32_t dtype, void* stream) {

@@ -18,6 +18,8 @@
 #include "common.cuh"
 #include "pre_common.cuh"
 
+#include <type_traits>
+
 namespace mhc {
 
 template <typename E, int N, bool VEC>
@@ -53,6 +55,44 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
   }
 }
 
+// bf16 hi/lo operand rows of one token for the tensor-core main pass (N = 4):
+//   G' = [g_hi | g_lo | g_hi | 0] (K = 80: g0 holds 0..63, g1 holds 64..79)
+//   Gp = [(inv g)_hi | (inv g)_lo | 0] (64)
+__device__ __forceinline__ void write_tc_operand_rows(const float* g, float inv, int64_t t,
+                                                      __nv_bfloat16* g0, __nv_bfloat16* g1,
+                                                      __nv_bfloat16* gp) {
+  constexpr int HM = 24;
+  __nv_bfloat16 row[80], prow[64];
+#pragma unroll
+  for (int k = 0; k < HM; ++k) {
+    const __nv_bfloat16 hi = __float2bfloat16_rn(g[k]);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(g[k] - __bfloat162float(hi));
+    row[k] = hi;
+    row[HM + k] = lo;
+    row[2 * HM + k] = hi;
+    const float p = g[k] * inv;
+    const __nv_bfloat16 phi_ = __float2bfloat16_rn(p);
+    prow[k] = phi_;
+    prow[HM + k] = __float2bfloat16_rn(p - __bfloat162float(phi_));
+  }
+#pragma unroll
+  for (int k = 3 * HM; k < 80; ++k) row[k] = __float2bfloat16_rn(0.f);
+#pragma unroll
+  for (int k = 2 * HM; k < 64; ++k) prow[k] = __float2bfloat16_rn(0.f);
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  const uint4* pv = reinterpret_cast<const uint4*>(prow);
+  uint4* d0 = reinterpret_cast<uint4*>(g0 + t * 64);
+  uint4* d1 = reinterpret_cast<uint4*>(g1 + t * 16);
+  uint4* dp = reinterpret_cast<uint4*>(gp + t * 64);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    d0[j] = rv[j];
+    dp[j] = pv[j];
+  }
+  d1[0] = rv[8];
+  d1[1] = rv[9];
+}
+
 // Small-stage VJP of one token; thread per token.  The Sinkhorn iterates are kept in
 // `hist` ((iters-1) matrices, layout [iter][elem][T] so the stores coalesce).
 template <int N>
@@ -62,7 +102,9 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
                      const float* __restrict__ gpost, const float* __restrict__ gcomb,
                      const float* __restrict__ inv_rms, int64_t T, int64_t HC, SmallParams sp,
                      float* __restrict__ hist, float* __restrict__ gm_out,
-                     float* __restrict__ coef_out, float* __restrict__ partials) {
+                     float* __restrict__ coef_out, float* __restrict__ partials,
+                     __nv_bfloat16* __restrict__ g0, __nv_bfloat16* __restrict__ g1,
+                     __nv_bfloat16* __restrict__ gp) {
   constexpr int HM = hc_mix(N);
   constexpr int NN = N * N;
   constexpr int NP = 3 + HM;
@@ -170,11 +212,14 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
     float dot = 0.f;
 #pragma unroll
     for (int k = 0; k < HM; ++k) {
-      gm_out[t * HM + k] = gmx[k];
+      if (gm_out) gm_out[t * HM + k] = gmx[k];
       dot = fmaf(gmx[k], mix[k], dot);
     }
     const float inv = inv_rms[t];
     coef_out[t] = inv * inv / (float)HC * dot;
+    if constexpr (N == 4) {
+      if (g0) write_tc_operand_rows(gmx, inv, t, g0, g1, gp);
+    }
   }
 #pragma unroll
   for (int i = 0; i < NP; ++i) red[threadIdx.x][i] = contrib[i];
@@ -301,6 +346,13 @@ static int gphi_splits(int64_t T) {
   return (int)(s < 1 ? 1 : (s > 16 ? 16 : s));
 }
 
+bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
+                         const void* gy, const void* gx);
+size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D);
+void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
+                             __nv_bfloat16** g1, __nv_bfloat16** gp);
+int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream_t s);
+
 struct BwdWs {
   float *gpre, *gm, *coef, *partials, *hist, *gphi_part;
   size_t total;
@@ -324,9 +376,15 @@ static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t ite
   return w;
 }
 
+static bool tc_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
+  return dtype == MHC_BF16 && N == 4 && D % 128 == 0 && T > 0;
+}
+
+// generic region, then (bf16, N=4, D%128==0 only) the tensor-core region
 size_t pre_bwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype, int32_t iters) {
-  (void)dtype;
-  return bwd_layout(nullptr, T, N, D, iters).total;
+  size_t n = bwd_layout(nullptr, T, N, D, iters).total;
+  if (tc_shape(T, N, D, dtype)) n += align_up(pre_bwd_tc_ws_bytes(T, D));
+  return n;
 }
 
 template <typename E, int N>
@@ -335,6 +393,11 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const int64_t T = a.T, D = a.D, HC = (int64_t)N * D;
   BwdWs w = bwd_layout((char*)a.workspace, T, N, D, a.sp.iters);
   const int nblk = (int)cdiv(T, 128);
+  const bool use_tc = std::is_same<E, __nv_bfloat16>::value &&
+                      pre_bwd_tc_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
+  char* tc_ws = (char*)a.workspace + w.total;
+  __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr;
+  if (use_tc) pre_bwd_tc_operand_ptrs(tc_ws, T, D, &g0, &g1, &gp);
   if (T == 0) {
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_alpha, 0, 3 * sizeof(float), s));
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_base, 0, HM * sizeof(float), s));
@@ -353,10 +416,12 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   MHC_LAUNCH_CHECK();
   pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(a.mixes, a.alpha, a.base, w.gpre, a.grad_post,
                                                a.grad_comb, a.inv_rms, T, HC, a.sp, w.hist,
-                                               w.gm, w.coef, w.partials);
+                                               use_tc ? nullptr : w.gm, w.coef, w.partials,
+                                               g0, g1, gp);
   MHC_LAUNCH_CHECK();
   pre_reduce_ab_kernel<<<1, 128, 0, s>>>(w.partials, nblk, HM, a.grad_alpha, a.grad_base);
   MHC_LAUNCH_CHECK();
+  if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   pre_bwd_gx_kernel<E, N><<<ggrid, kGxCC, 0, s>>>((const E*)a.x, (const E*)a.grad_y, a.phi,
                                                   w.gm, a.inv_rms, w.coef, a.pre,

@@ -1,0 +1,511 @@
+// pre_bwd_tc.cu -- mhc_pre_clamp_sinkhorn backward, tensor-core main pass (bf16, N=4,
+// D % 128 == 0).
+//
+// After pass 1 (pre_bwd.cu: grad_pre dots + small-stage VJP, which also writes the
+// bf16 hi/lo operand rows below), one persistent kernel streams x once more and
+// produces grad_x and grad_phi together:
+//
+//   gxs[t,c]    = sum_k grad_mixes[t,k] phi[k,c]        (tcgen05, M=128 tokens, N=128
+//                 columns, K=80: A' = [g_hi|g_lo|g_hi], B' = [phi_hi;phi_hi;phi_lo])
+//   grad_x[t,c] = gy[t,d] pre[t,n] + inv[t] gxs[t,c] - coef[t] x[t,c]       (epilogue)
+//   grad_phi[k,c] += sum_t gp[t,k] x[t,c],  gp = inv*grad_mixes              (tcgen05,
+//                 M=128 columns, N=64 (hi 24 | lo 24 | 0), K=128 tokens; x is the
+//                 MN-major A operand straight from the staged x tile)
+//
+// Work: column group g = a 128-wide range of d, all N=4 sub-chunks n (512 columns of
+// HC); items (g, token tile i) in g-major order, split into equal contiguous runs, one
+// per CTA.  Each group's tiles are cut into cells of SUBT tiles; grad_phi stays in
+// TMEM (4 x 64 columns) for the part of a cell a CTA owns and is then flushed into a
+// partial buffer, so no accumulation chain exceeds SUBT*8 MMAs (the tensor core's
+// fp32 accumulation error grows with the chain length).  pre_bwd_gphi_reduce_kernel
+// sums the partials of each column in a fixed order (deterministic).  The per-group
+// phi operand (80 KB) stays in shared memory for the whole segment.
+//
+// Roles (320 threads): warp 0 TMA producer; warp 1 TMEM owner + MMA issuer; warps 2-9
+// epilogue (warp w reads TMEM lane quarter w%4, column half (w-2)/4).
+#include "pre_common.cuh"
+#include "tc.cuh"
+
+namespace mhc {
+
+namespace bwdtc {
+constexpr int N = 4;
+constexpr int HM = 24;
+constexpr int GC = 128;                     // columns of d per group
+constexpr int KG = 80;                      // gxs K (72 used)
+constexpr int SUBT = 32;                    // token tiles per grad_phi cell
+// shared memory (bytes, offsets from a 1024-aligned base)
+constexpr int P0_BYTES = 128 * 64 * 2;      // [128 cols][64 k] SW128
+constexpr int P1_BYTES = 128 * 16 * 2;      // [128 cols][16 k] SW32
+constexpr int G0_BYTES = 128 * 64 * 2;      // [128 tok][64 k]
+constexpr int G1_BYTES = 128 * 16 * 2;      // [128 tok][16 k]
+constexpr int GP_BYTES = 128 * 64 * 2;      // [128 tok][64 n]
+constexpr int X_BYTES = 2 * 128 * 64 * 2;   // two [128 tok][64 col] boxes
+constexpr int OFF_P0 = 0;
+constexpr int OFF_P1 = OFF_P0 + N * P0_BYTES;
+constexpr int OFF_G0 = OFF_P1 + N * P1_BYTES;
+constexpr int OFF_G1 = OFF_G0 + 2 * G0_BYTES;
+constexpr int OFF_GP = OFF_G1 + 2 * G1_BYTES;
+constexpr int OFF_X = OFF_GP + 2 * GP_BYTES;
+constexpr int OFF_BAR = OFF_X + 2 * X_BYTES;
+constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr int THREADS = 320;
+constexpr int EPI_WARPS = 8;
+// TMEM columns: D2[n] (grad_phi, 64 each) at n*64, D1[b] (gxs, 128 each) at 256 + b*128
+constexpr int TMEM_COLS = 512;
+}  // namespace bwdtc
+
+struct BwdTcMaps {
+  CUtensorMap x, g0, g1, gp, p0, p1;
+};
+
+struct BwdGeom {
+  int64_t ntiles;  // 128-token tiles
+  int64_t cpg;     // cells per group
+  int64_t items;   // groups * ntiles
+  int ncta;
+  int max_segs;    // partial slots per CTA
+};
+
+__host__ __device__ inline int64_t cell_of(int64_t item, int64_t ntiles, int64_t cpg) {
+  const int64_t g = item / ntiles, i = item - g * ntiles;
+  return g * cpg + i / bwdtc::SUBT;
+}
+
+__global__ void __launch_bounds__(bwdtc::THREADS, 1)
+pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
+                  const float* __restrict__ inv_rms, const float* __restrict__ coef,
+                  const float* __restrict__ pre, __nv_bfloat16* __restrict__ gx,
+                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo) {
+  using namespace bwdtc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
+  uint64_t* xfull = bar;          // [2]
+  uint64_t* xempty = bar + 2;     // [2]
+  uint64_t* gfull = bar + 4;      // [2]
+  uint64_t* gempty = bar + 6;     // [2]
+  uint64_t* pfull = bar + 8;
+  uint64_t* pempty = bar + 9;
+  uint64_t* d1full = bar + 10;    // [2]
+  uint64_t* d1empty = bar + 12;   // [2]
+  uint64_t* d2full = bar + 14;
+  uint64_t* d2empty = bar + 15;
+  uint64_t* tdone = bar + 16;
+  uint32_t* tmem_slot = (uint32_t*)(bar + 17);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t HC = N * D;
+  const int64_t ntiles = geo.ntiles;
+  const int64_t it0 = geo.items * blockIdx.x / gridDim.x;
+  const int64_t it1 = geo.items * (blockIdx.x + 1) / gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&xfull[b], 1);
+      tc::mbar_init(&xempty[b], 1 + EPI_WARPS);
+      tc::mbar_init(&gfull[b], 1);
+      tc::mbar_init(&gempty[b], 1);
+      tc::mbar_init(&d1full[b], 1);
+      tc::mbar_init(&d1empty[b], EPI_WARPS);
+    }
+    tc::mbar_init(pfull, 1);
+    tc::mbar_init(pempty, 1);
+    tc::mbar_init(d2full, 1);
+    tc::mbar_init(d2empty, EPI_WARPS);
+    tc::mbar_init(tdone, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&maps.x);
+    tc::prefetch_tmap(&maps.g0);
+    tc::prefetch_tmap(&maps.gp);
+    tc::prefetch_tmap(&maps.p0);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // segment = the part of one cell this CTA owns
+  auto seg_start_of = [&](int64_t item, int64_t i) { return item == it0 || i % SUBT == 0; };
+  auto seg_end_of = [&](int64_t item, int64_t i) {
+    return item == it1 - 1 || (i + 1) % SUBT == 0 || i == ntiles - 1;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t xi = 0, gi = 0, seg = 0;
+      bool ok = true;
+      for (int64_t item = it0; item < it1 && ok; ++item) {
+        const int64_t g = item / ntiles, i = item - g * ntiles;
+        const int d0 = (int)(g * GC);
+        if (seg_start_of(item, i)) {
+          if (!tc::mbar_wait(pempty, (seg & 1) ^ 1, abort_flag)) break;
+          tc::mbar_arrive_expect_tx(pfull, N * (P0_BYTES + P1_BYTES));
+          for (int n = 0; n < N; ++n) {
+            tc::tma_load_2d(sm + OFF_P0 + n * P0_BYTES, &maps.p0, pfull, 0, (int)(n * D + d0));
+            tc::tma_load_2d(sm + OFF_P1 + n * P1_BYTES, &maps.p1, pfull, 0, (int)(n * D + d0));
+          }
+        }
+        {
+          const int b = gi & 1;
+          if (!tc::mbar_wait(&gempty[b], ((gi >> 1) & 1) ^ 1, abort_flag)) break;
+          tc::mbar_arrive_expect_tx(&gfull[b], G0_BYTES + G1_BYTES + GP_BYTES);
+          tc::tma_load_2d(sm + OFF_G0 + b * G0_BYTES, &maps.g0, &gfull[b], 0, (int)(i * 128));
+          tc::tma_load_2d(sm + OFF_G1 + b * G1_BYTES, &maps.g1, &gfull[b], 0, (int)(i * 128));
+          tc::tma_load_2d(sm + OFF_GP + b * GP_BYTES, &maps.gp, &gfull[b], 0, (int)(i * 128));
+          ++gi;
+        }
+        for (int n = 0; n < N; ++n, ++xi) {
+          const int s = xi & 1;
+          if (!tc::mbar_wait(&xempty[s], ((xi >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          tc::mbar_arrive_expect_tx(&xfull[s], X_BYTES);
+          uint8_t* dst = sm + OFF_X + s * X_BYTES;
+          const int col = (int)(n * D + d0);
+          tc::tma_load_2d(dst, &maps.x, &xfull[s], col, (int)(i * 128));
+          tc::tma_load_2d(dst + X_BYTES / 2, &maps.x, &xfull[s], col + 64, (int)(i * 128));
+        }
+        if (seg_end_of(item, i)) ++seg;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_gxs = tc::idesc_bf16(128, 128, false, false);
+      constexpr uint32_t id_gphi = tc::idesc_bf16(128, 64, true, true);
+      uint32_t xi = 0, gi = 0, seg = 0, di = 0;
+      bool ok = true;
+      for (int64_t item = it0; item < it1 && ok; ++item) {
+        const int64_t i = item % ntiles;
+        const bool seg_start = seg_start_of(item, i);
+        if (seg_start) {
+          if (!tc::mbar_wait(pfull, seg & 1, abort_flag)) break;
+          if (!tc::mbar_wait(d2empty, (seg & 1) ^ 1, abort_flag)) break;
+        }
+        const int b = gi & 1;
+        if (!tc::mbar_wait(&gfull[b], (gi >> 1) & 1, abort_flag)) break;
+        tc::tc_fence_after();
+        const uint32_t sg0 = tc::smem_u32(sm + OFF_G0 + b * G0_BYTES);
+        const uint32_t sg1 = tc::smem_u32(sm + OFF_G1 + b * G1_BYTES);
+        const uint32_t sgp = tc::smem_u32(sm + OFF_GP + b * GP_BYTES);
+        for (int n = 0; n < N; ++n, ++xi, ++di) {
+          const int s = xi & 1, e = di & 1;
+          if (!tc::mbar_wait(&xfull[s], (xi >> 1) & 1, abort_flag)) { ok = false; break; }
+          if (!tc::mbar_wait(&d1empty[e], ((di >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          tc::tc_fence_after();
+          // gxs tile: D1[e] = G' * P'(n)^T, K = 64 (SW128) + 16 (SW32)
+          const uint32_t d1 = tmem + 256 + e * 128;
+          const uint32_t sp0 = tc::smem_u32(sm + OFF_P0 + n * P0_BYTES);
+          const uint32_t sp1 = tc::smem_u32(sm + OFF_P1 + n * P1_BYTES);
+          const uint64_t a0 = tc::smem_desc(sg0, 16, 1024, tc::kSwizzle128);
+          const uint64_t b0 = tc::smem_desc(sp0, 16, 1024, tc::kSwizzle128);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) tc::mma_bf16(d1, a0 + 2 * k, b0 + 2 * k, id_gxs, k != 0);
+          tc::mma_bf16(d1, tc::smem_desc(sg1, 16, 256, tc::kSwizzle32),
+                       tc::smem_desc(sp1, 16, 256, tc::kSwizzle32), id_gxs, 1);
+          tc::mma_commit(&d1full[e]);
+          // grad_phi: D2[n] (+)= x_tile^T (MN-major, M = 128 columns) * Gp (MN-major, N = 64)
+          const uint32_t d2 = tmem + n * 64;
+          const uint32_t sx = tc::smem_u32(sm + OFF_X + s * X_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ax = tc::smem_desc(sx + kk * 2048, X_BYTES / 2, 1024, tc::kSwizzle128);
+            const uint64_t bg = tc::smem_desc(sgp + kk * 2048, GP_BYTES, 1024, tc::kSwizzle128);
+            tc::mma_bf16(d2, ax, bg, id_gphi, (seg_start && kk == 0) ? 0u : 1u);
+          }
+          tc::mma_commit(&xempty[s]);
+        }
+        if (!ok) break;
+        tc::mma_commit(&gempty[b]);
+        ++gi;
+        if (seg_end_of(item, i)) {
+          tc::mma_commit(d2full);
+          tc::mma_commit(pempty);
+          ++seg;
+        }
+      }
+      tc::mma_commit(tdone);
+      volatile int never = 0;
+      tc::mbar_wait(tdone, 0, &never);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;                 // TMEM lane quarter
+    const int h = (warp - 2) >> 2;          // column half (0: cols 0-63, 1: 64-127)
+    const int r = q * 32 + lane;            // token row (D1) / column row (D2)
+    uint32_t xi = 0, di = 0, seg = 0;
+    const int64_t cell_first = cell_of(it0, ntiles, geo.cpg);
+    for (int64_t item = it0; item < it1; ++item) {
+      const int64_t g = item / ntiles, i = item - g * ntiles;
+      const int64_t d0 = g * GC;
+      const int64_t t = i * 128 + r;
+      const bool live = t < T;
+      float inv = 0.f, cf = 0.f, pr[N];
+      if (live) {
+        inv = inv_rms[t];
+        cf = coef[t];
+#pragma unroll
+        for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
+      } else {
+#pragma unroll
+        for (int n = 0; n < N; ++n) pr[n] = 0.f;
+      }
+      bool ok = true;
+      for (int n = 0; n < N; ++n, ++xi, ++di) {
+        const int s = xi & 1, e = di & 1;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        float acc[64];
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 64;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) tc::tmem_ld16(ta + m * 16, acc + m * 16);
+        tc::tmem_ld_wait();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&d1empty[e]);
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&xfull[s], (xi >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        // x row r, columns [64h, 64h+64) of the staged tile (128B-swizzled rows)
+        const uint8_t* xrow = sm + OFF_X + s * X_BYTES + h * (X_BYTES / 2) + r * 128;
+        uint4 xv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          xv[j] = *reinterpret_cast<const uint4*>(xrow + ((j ^ (r & 7)) << 4));
+        // the x stage is refilled by TMA (async proxy): order these reads before it
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&xempty[s]);
+        if (live) {
+          const __nv_bfloat16* gyr = gy + t * D + d0 + h * 64;
+          __nv_bfloat16* out = gx + t * HC + n * D + d0 + h * 64;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float xf[8], gf[8], o[8];
+            widen<__nv_bfloat16>(xv[j], xf);
+            widen<__nv_bfloat16>(ld_keep(gyr + 8 * j), gf);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);
+              o[u] = fmaf(gf[u], pr[n], rr);
+            }
+            st_stream(out + 8 * j, narrow<__nv_bfloat16>(o));
+          }
+        }
+      }
+      if (!ok) break;
+      if (seg_end_of(item, i)) {
+        // flush: D2[n] row r = column d0 + r; cols k: hi k, lo 24 + k
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(d2full, seg & 1, abort_flag))) break;
+        tc::tc_fence_after();
+        const int lseg = (int)(cell_of(item, ntiles, geo.cpg) - cell_first);
+        for (int nn = 2 * h; nn < 2 * h + 2; ++nn) {
+          float v[48];
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + nn * 64;
+#pragma unroll
+          for (int m = 0; m < 3; ++m) tc::tmem_ld16(ta + m * 16, v + m * 16);
+          tc::tmem_ld_wait();
+          float* dst =
+              gphi_part + (((int64_t)blockIdx.x * geo.max_segs + lseg) * N + nn) * HM * GC;
+#pragma unroll
+          for (int k = 0; k < HM; ++k) dst[k * GC + r] = v[k] + v[HM + k];
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(d2empty);
+        ++seg;
+      }
+    }
+  }
+  if (*abort_flag && threadIdx.x == 0) flag_timeout();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, bwdtc::TMEM_COLS);
+  }
+}
+
+// phi (fp32 [HM][HC]) -> per-column bf16 operand rows P' = [phi_hi | phi_hi | phi_lo | 0]
+// split into P0 [HC][64] and P1 [HC][16].
+__global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi,
+                                        __nv_bfloat16* __restrict__ p0,
+                                        __nv_bfloat16* __restrict__ p1, int64_t HC) {
+  using namespace bwdtc;
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= HC) return;
+  __nv_bfloat16 row[KG];
+#pragma unroll
+  for (int k = 0; k < HM; ++k) {
+    const float p = phi[(int64_t)k * HC + c];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(p);
+    row[k] = hi;
+    row[HM + k] = hi;
+    row[2 * HM + k] = __float2bfloat16_rn(p - __bfloat162float(hi));
+  }
+#pragma unroll
+  for (int k = 3 * HM; k < KG; ++k) row[k] = __float2bfloat16_rn(0.f);
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  uint4* d0 = reinterpret_cast<uint4*>(p0 + c * 64);
+  uint4* d1 = reinterpret_cast<uint4*>(p1 + c * 16);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) d0[j] = rv[j];
+  d1[0] = rv[8];
+  d1[1] = rv[9];
+}
+
+// grad_phi[k][n*D + g*128 + c] = sum over the cells of group g, and within a cell over
+// the CTAs that own part of it (in CTA order), of their partials.
+__global__ void pre_bwd_gphi_reduce_kernel(const float* __restrict__ part,
+                                           float* __restrict__ grad_phi, int64_t D,
+                                           BwdGeom geo) {
+  using namespace bwdtc;
+  const int64_t G = D / GC;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (g, n, k, c)
+  if (idx >= G * N * HM * GC) return;
+  const int c = (int)(idx % GC);
+  const int k = (int)((idx / GC) % HM);
+  const int n = (int)((idx / (GC * HM)) % N);
+  const int64_t g = idx / (GC * HM * N);
+  const int64_t items = geo.items, ntiles = geo.ntiles;
+  const int ncta = geo.ncta;
+  float s = 0.f;
+  for (int64_t ci = 0; ci < geo.cpg; ++ci) {
+    const int64_t lo_item = g * ntiles + ci * SUBT;
+    int64_t hi_item = lo_item + SUBT;
+    if (hi_item > (g + 1) * ntiles) hi_item = (g + 1) * ntiles;
+    // first CTA whose run [it0, it1) ends after lo_item
+    int b = (int)(lo_item * ncta / items);
+    while (b > 0 && items * b / ncta > lo_item) --b;
+    while (b < ncta - 1 && items * (b + 1) / ncta <= lo_item) ++b;
+    for (; b < ncta; ++b) {
+      const int64_t it0 = items * b / ncta, it1 = items * (b + 1) / ncta;
+      if (it0 >= hi_item) break;
+      if (it1 <= lo_item || it1 <= it0) continue;
+      const int64_t lseg = g * geo.cpg + ci - cell_of(it0, ntiles, geo.cpg);
+      s += part[((((int64_t)b * geo.max_segs + lseg) * N + n) * HM + k) * GC + c];
+    }
+  }
+  grad_phi[(int64_t)k * (N * D) + n * D + g * GC + c] = s;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
+                         const void* gy, const void* gx) {
+  return dtype == MHC_BF16 && N == 4 && D % bwdtc::GC == 0 && T > 0 &&
+         T <= (int64_t)INT32_MAX - 256 && (int64_t)N * D <= INT32_MAX && aligned16(x) &&
+         aligned16(gy) && aligned16(gx);
+}
+
+static BwdGeom bwd_tc_geometry(int64_t T, int64_t D) {
+  BwdGeom g;
+  g.ntiles = cdiv(T, 128);
+  g.cpg = cdiv(g.ntiles, bwdtc::SUBT);
+  g.items = (D / bwdtc::GC) * g.ntiles;
+  int n = sm_count();
+  if (g.items < n) n = (int)g.items;
+  g.ncta = n < 1 ? 1 : n;
+  int64_t ms = 1;
+  for (int b = 0; b < g.ncta; ++b) {
+    const int64_t i0 = g.items * b / g.ncta, i1 = g.items * (b + 1) / g.ncta;
+    if (i1 > i0) {
+      const int64_t c = cell_of(i1 - 1, g.ntiles, g.cpg) - cell_of(i0, g.ntiles, g.cpg) + 1;
+      if (c > ms) ms = c;
+    }
+  }
+  g.max_segs = (int)ms;
+  return g;
+}
+
+struct BwdTcWs {
+  __nv_bfloat16 *g0, *g1, *gp, *p0, *p1;
+  float* part;
+  size_t total;
+};
+
+static BwdTcWs bwd_tc_layout(char* base, int64_t T, int64_t D) {
+  using namespace bwdtc;
+  const BwdGeom geo = bwd_tc_geometry(T, D);
+  const int64_t Tp = geo.ntiles * 128, HC = N * D;
+  BwdTcWs w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { char* p = base + off; off += align_up(bytes); return p; };
+  w.g0 = (__nv_bfloat16*)take((size_t)Tp * 64 * 2);
+  w.g1 = (__nv_bfloat16*)take((size_t)Tp * 16 * 2);
+  w.gp = (__nv_bfloat16*)take((size_t)Tp * 64 * 2);
+  w.p0 = (__nv_bfloat16*)take((size_t)HC * 64 * 2);
+  w.p1 = (__nv_bfloat16*)take((size_t)HC * 16 * 2);
+  w.part = (float*)take((size_t)geo.ncta * geo.max_segs * N * HM * GC * 4);
+  w.total = off;
+  return w;
+}
+
+size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D) { return bwd_tc_layout(nullptr, T, D).total; }
+
+// Pointers to the bf16 operand rows pass 1 writes (inside the tc workspace region).
+void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
+                             __nv_bfloat16** g1, __nv_bfloat16** gp) {
+  BwdTcWs w = bwd_tc_layout((char*)ws, T, D);
+  *g0 = w.g0;
+  *g1 = w.g1;
+  *gp = w.gp;
+}
+
+int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream_t s) {
+  using namespace bwdtc;
+  const int64_t T = a.T, D = a.D, HC = N * D;
+  const BwdGeom geo = bwd_tc_geometry(T, D);
+  BwdTcWs w = bwd_tc_layout((char*)ws, T, D);
+  pre_bwd_phi_prep_kernel<<<(unsigned)cdiv(HC, 256), 256, 0, s>>>(a.phi, w.p0, w.p1, HC);
+  MHC_LAUNCH_CHECK();
+  BwdTcMaps m;
+  const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  int st;
+  // operand rows: row extent T, so rows of the last tile beyond T read as zeros
+  if ((st = make_tmap_2d(&m.x, a.x, bf, 2, HC, T, HC * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tmap_2d(&m.g0, w.g0, bf, 2, 64, T, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tmap_2d(&m.g1, w.g1, bf, 2, 16, T, 32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B)))
+    return st;
+  if ((st = make_tmap_2d(&m.gp, w.gp, bf, 2, 64, T, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tmap_2d(&m.p0, w.p0, bf, 2, 64, HC, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tmap_2d(&m.p1, w.p1, bf, 2, 16, HC, 32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B)))
+    return st;
+  static bool attr_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    attr_set[dev] = true;
+  }
+  pre_bwd_tc_kernel<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
+                                                    a.inv_rms, coef, a.pre,
+                                                    (__nv_bfloat16*)a.grad_x, w.part, T, D, geo);
+  MHC_LAUNCH_CHECK();
+  const int64_t n = (D / GC) * N * HM * GC;
+  pre_bwd_gphi_reduce_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.part, a.grad_phi, D, geo);
+  MHC_LAUNCH_CHECK();
+  return MHC_OK;
+}
+
+int pre_bwd_tc_device_error() { return read_and_clear_tu_error(); }
+
+}  // namespace mhc

@@ -11,6 +11,8 @@
 #include "common.cuh"
 #include "pre_common.cuh"
 
+#include <type_traits>
+
 namespace mhc {
 
 constexpr int kMixTT = 32;   // tokens per CTA
@@ -140,10 +142,16 @@ pre_apply_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+bool pre_fwd_tc_eligible(const PreFwdArgs& a);
+size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D);
+int pre_fwd_tc_mix(const PreFwdArgs& a, cudaStream_t s);
+
+// the generic path and the tensor-core path use the workspace differently; size for both
 size_t pre_fwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype) {
-  (void)D; (void)dtype;
   const int HM = hc_mix(N);
-  return align_up((size_t)T * HM * 4) + align_up((size_t)T * 4);
+  const size_t generic = align_up((size_t)T * HM * 4) + align_up((size_t)T * 4);
+  const size_t tc = (dtype == MHC_BF16 && (N == 4 || N == 8)) ? pre_fwd_tc_ws_bytes(T, N, D) : 0;
+  return generic > tc ? generic : tc;
 }
 
 template <typename E, int N>
@@ -153,7 +161,10 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
   char* ws = (char*)a.workspace;
   float* raw = (float*)ws;
   float* sumsq = (float*)(ws + align_up((size_t)T * HM * 4));
-  if (T > 0) {
+  if (T > 0 && std::is_same<E, __nv_bfloat16>::value && pre_fwd_tc_eligible(a)) {
+    const int st = pre_fwd_tc_mix(a, s);
+    if (st != MHC_OK) return st;
+  } else if (T > 0) {
     const size_t smem = (size_t)(kMixTT * (kMixKC + 1) + HM * kMixKC) * sizeof(float);
     MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_kernel<E, N>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -164,6 +175,8 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
         raw, sumsq, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
         a.post_out, a.comb_frag, a.h_res_logits);
     MHC_LAUNCH_CHECK();
+  }
+  if (T > 0) {
     const bool vec = (D % Pack<E>::n == 0) && aligned16(a.x) && aligned16(a.y) &&
                      (a.x_scaled == nullptr || aligned16(a.x_scaled));
     const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;

@@ -1,0 +1,308 @@
+// pre_fwd_tc.cu -- mhc_pre_clamp_sinkhorn forward, tensor-core path (bf16 x).
+//
+// pre_phi_split_kernel   phi (fp32) -> phi_hl (bf16) [NP x HC]: rows [0,HM) = hi,
+//                        rows [HM,2HM) = lo = phi - hi, rows beyond = 0.  x is exact in
+//                        bf16, so x.phi^T = x.hi^T + x.lo^T in fp32 accumulation
+//                        reproduces the fp32 contraction to ~2^-17 per product.
+// pre_mix_tc_kernel      persistent, one 128-token tile at a time:
+//                          warp 0     TMA producer: x tile [128 x 64] + phi_hl [NP x 64]
+//                                     per K step into an S-stage ring (128B swizzle)
+//                          warp 1     TMEM owner + MMA issuer: tcgen05.mma M=128 N=NP
+//                                     K=16 x4 per stage; accumulation in K segments of
+//                                     KSEG stages, double-buffered in TMEM
+//                          warps 2-5  sum of squares of their token row from the staged
+//                                     x tile (same pass over x), the fp32 sum of the
+//                                     segment partials (hi+lo) from TMEM, then inv_rms,
+//                                     mixes, heads, clamp, softmax, Sinkhorn and the
+//                                     stores of the per-token outputs
+// x is read from HBM once here; pre_apply_kernel (pre_fwd.cu) reads it once more for
+// y and x_scaled, which need inv_rms / pre of the whole row first.
+#include "pre_common.cuh"
+#include "tc.cuh"
+
+namespace mhc {
+
+template <int N>
+struct MixCfg {
+  static constexpr int HM = hc_mix(N);
+  static constexpr int NP = (2 * HM + 15) / 16 * 16;            // MMA N (hi + lo rows)
+  static constexpr int BUFCOL = (NP + 16 + 31) / 32 * 32;       // TMEM columns per buffer
+  static constexpr int TMEM_COLS = (2 * BUFCOL <= 32) ? 32 : (2 * BUFCOL <= 64) ? 64
+                                   : (2 * BUFCOL <= 128) ? 128 : (2 * BUFCOL <= 256) ? 256 : 512;
+  static constexpr int KC = 64;                                  // K per stage (128 B rows)
+  // Stages per TMEM segment.  The tensor core's fp32 accumulation loses precision
+  // roughly in proportion to the number of chained MMAs; folding every 64 MMAs into
+  // fp32 registers keeps x.phi^T within a few 1e-6 of the fp32 contraction at any K.
+  static constexpr int KSEG = 16;
+  static constexpr int A_BYTES = 128 * KC * 2;                   // 16 KB
+  static constexpr int B_BYTES = NP * KC * 2;
+  static constexpr int B_STRIDE = (B_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGES = (200 * 1024) / (A_BYTES + B_STRIDE) > 8
+                                    ? 8 : (200 * 1024) / (A_BYTES + B_STRIDE);
+  static constexpr int SMEM = 1024 /*align slack*/ + STAGES * (A_BYTES + B_STRIDE) + 256;
+  static constexpr int THREADS = 192;
+};
+
+__global__ void pre_phi_split_kernel(const float* __restrict__ phi, __nv_bfloat16* __restrict__ hl,
+                                     int HM, int NP, int64_t HC) {
+  const int64_t n = (int64_t)NP * HC;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / HC, c = i - r * HC;
+    float v = 0.f;
+    if (r < HM) {
+      v = phi[r * HC + c];
+    } else if (r < 2 * HM) {
+      const float p = phi[(r - HM) * HC + c];
+      v = p - __bfloat162float(__float2bfloat16_rn(p));
+    }
+    hl[i] = __float2bfloat16_rn(v);
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(MixCfg<N>::THREADS, 1)
+pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
+                  const __grid_constant__ CUtensorMap tm_phi, const float* __restrict__ alpha,
+                  const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
+                  SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
+                  float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
+                  float* __restrict__ logits_out) {
+  using C = MixCfg<N>;
+  constexpr int HM = C::HM, S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * C::A_BYTES;
+  uint64_t* full = (uint64_t*)(sB + S * C::B_STRIDE);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* tdone = tempty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tdone + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  __shared__ float sbase[HM];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t ntiles = (T + 127) / 128;
+  const int nk = (int)((HC + C::KC - 1) / C::KC);
+
+  for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1 + 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&tfull[b], 1);
+      tc::mbar_init(&tempty[b], 4);
+    }
+    tc::mbar_init(tdone, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tm_x);
+    tc::prefetch_tmap(&tm_phi);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int kc = 0; kc < nk; ++kc, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          tc::mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+          tc::tma_load_2d(sA + s * C::A_BYTES, &tm_x, &full[s], kc * C::KC, (int)(tile * 128));
+          tc::tma_load_2d(sB + s * C::B_STRIDE, &tm_phi, &full[s], kc * C::KC, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16(128, C::NP, false, false);
+      uint32_t it = 0, j = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int kc0 = 0; kc0 < nk && ok; kc0 += C::KSEG, ++j) {
+          const int buf = j & 1;
+          if (!tc::mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t d = tmem + buf * C::BUFCOL;
+          const int kc1 = kc0 + C::KSEG < nk ? kc0 + C::KSEG : nk;
+          for (int kc = kc0; kc < kc1; ++kc, ++it) {
+            const int s = it % S;
+            if (!tc::mbar_wait(&full[s], (it / S) & 1, abort_flag)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint64_t a0 = tc::smem_desc(tc::smem_u32(sA + s * C::A_BYTES), 16, 1024,
+                                              tc::kSwizzle128);
+            const uint64_t b0 = tc::smem_desc(tc::smem_u32(sB + s * C::B_STRIDE), 16, 1024,
+                                              tc::kSwizzle128);
+#pragma unroll
+            for (int k = 0; k < C::KC / 16; ++k)
+              tc::mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (kc != kc0 || k != 0) ? 1u : 0u);
+            tc::mma_commit(&empty[s]);
+          }
+          if (!ok) break;
+          tc::mma_commit(&tfull[buf]);
+        }
+      }
+      // all MMAs of this CTA have completed before TMEM is released
+      tc::mma_commit(tdone);
+      volatile int never = 0;
+      tc::mbar_wait(tdone, 0, &never);
+    }
+  } else {
+    // ------------------------------------------------------------ sumsq + epilogue
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;        // token row within the tile
+    sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t it = 0, j = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      float sq = 0.f;
+      float mix[HM];
+#pragma unroll
+      for (int k = 0; k < HM; ++k) mix[k] = 0.f;
+      bool ok = true;
+      for (int kc = 0; kc < nk; ++kc, ++it) {
+        const int s = it % S;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (it / S) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const uint4* row = reinterpret_cast<const uint4*>(sA + s * C::A_BYTES + r * 128);
+        float csq = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float f[8];
+          widen<__nv_bfloat16>(row[c], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) csq = fmaf(f[e], f[e], csq);
+        }
+        sq += csq;
+        // the stage is refilled by TMA (async proxy): order these generic-proxy reads
+        // before that write, then release the stage
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[s]);
+        if ((kc + 1) % C::KSEG == 0 || kc + 1 == nk) {
+          // end of a K segment: fold its TMEM partial (hi + lo rows) into registers
+          const int buf = j & 1;
+          if (!__all_sync(0xffffffffu, tc::mbar_wait(&tfull[buf], (j >> 1) & 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t taddr = tq + buf * C::BUFCOL;
+#pragma unroll
+          for (int k0 = 0; k0 < HM; k0 += 16) {
+            float hi[16], lo[16];
+            tc::tmem_ld16(taddr + k0, hi);
+            tc::tmem_ld16(taddr + HM + k0, lo);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (k0 + e < HM) mix[k0 + e] += hi[e] + lo[e];
+          }
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&tempty[buf]);
+          ++j;
+        }
+      }
+      if (!ok) break;
+      const int64_t t = tile * 128 + r;
+      if (t < T) {
+        const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
+#pragma unroll
+        for (int k = 0; k < HM; ++k) mix[k] *= inv;
+        small_outputs<N>(mix, sbase, sp, t, inv, inv_rms, mixes, pre, post, comb, logits_out);
+      }
+    }
+  }
+  if (*abort_flag && threadIdx.x == 0) flag_timeout();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+bool pre_fwd_tc_eligible(const PreFwdArgs& a) {
+  const int64_t HC = (int64_t)a.N * a.D;
+  return a.dtype == MHC_BF16 && (a.N == 4 || a.N == 8) && HC % 8 == 0 && aligned16(a.x) &&
+         a.T > 0 && a.T <= (int64_t)INT32_MAX - 256;
+}
+
+size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D) {
+  (void)T;
+  const int HM = hc_mix(N);
+  const int NP = (2 * HM + 15) / 16 * 16;
+  return align_up((size_t)NP * N * D * 2);
+}
+
+template <int N>
+static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
+  using C = MixCfg<N>;
+  const int64_t T = a.T, HC = (int64_t)N * a.D;
+  __nv_bfloat16* phi_hl = (__nv_bfloat16*)a.workspace;
+  {
+    const int64_t n = (int64_t)C::NP * HC;
+    const int grid = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 8);
+    pre_phi_split_kernel<<<grid, 256, 0, s>>>(a.phi, phi_hl, C::HM, C::NP, HC);
+    MHC_LAUNCH_CHECK();
+  }
+  CUtensorMap tx, tp;
+  int st = make_tmap_2d(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, T, HC * 2, C::KC, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != MHC_OK) return st;
+  st = make_tmap_2d(&tp, phi_hl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, C::NP, HC * 2, C::KC,
+                    C::NP, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st != MHC_OK) return st;
+  static bool attr_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_tc_kernel<N>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set[dev] = true;
+  }
+  const int64_t ntiles = cdiv(T, 128);
+  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  pre_mix_tc_kernel<N><<<grid, C::THREADS, C::SMEM, s>>>(
+      tx, tp, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
+      a.comb_frag, a.h_res_logits);
+  MHC_LAUNCH_CHECK();
+  return MHC_OK;
+}
+
+// Runs the tensor-core mix (+ fused small stage); the caller then runs pre_apply.
+int pre_fwd_tc_mix(const PreFwdArgs& a, cudaStream_t s) {
+  switch (a.N) {
+    case 4: return pre_fwd_tc_n<4>(a, s);
+    case 8: return pre_fwd_tc_n<8>(a, s);
+    default: return MHC_ERR_UNSUPPORTED_N;
+  }
+}
+
+int pre_fwd_tc_device_error() { return read_and_clear_tu_error(); }
+
+}  // namespace mhc

@@ -55,6 +55,13 @@ int mhc_version(void);
  * device path ran.  No counterpart in the reference. */
 uint64_t mhc_kernel_launches(void);
 
+/* Synchronises the current device, then returns (and clears) the status a
+ * tensor-core kernel recorded when one of its bounded device-side waits gave
+ * up (MHC_ERR_TIMEOUT), MHC_ERR_CUDA if the device reports an error, else
+ * MHC_OK.  Diagnostic; the operators themselves never synchronise.  No
+ * counterpart in the reference. */
+int mhc_device_status(void);
+
 /*
  * mhc_post forward.  Replaces the device work of `mhc_post`
  * (src/mhc_post.py:296-341, kernels :24-96 and :207-271):

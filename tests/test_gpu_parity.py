@@ -252,3 +252,41 @@ def test_deterministic_backward():
     b = M.mhc_pre_clamp_sinkhorn_backward(*args)
     for u, v in zip(a, b):
         assert torch.equal(u, v)
+
+
+@pytest.mark.parametrize("N", [4, 8])
+def test_pre_many_tiles_ragged(N):
+    """More 128-token tiles than SMs (each persistent CTA runs several tiles,
+    alternating TMEM buffers) and a ragged last tile."""
+    T, D = 148 * 128 * 2 + 77, 64
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=N,
+                                                       phi_std=2.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-4.0, clamp_max=4.0, iter_times=20)
+    out = M.mhc_pre_clamp_sinkhorn(x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV),
+                                   need_backward=True, **kw)
+    ref = O.pre_fwd(x, phi, alpha, base, dtype=F64, **kw)
+    for k in ("post_out", "inv_rms", "mixes", "h_res_logits", "pre"):
+        assert rel_err(out[k], ref[k]) <= TOL_FP32, k
+    assert abs_err(out["comb_frag"], ref["comb_frag"]) <= TOL_SINKHORN_ABS
+    assert rel_err(out["y"], ref["y"]) <= TOL_BF16
+    from FlagOS_mhc import _C
+    assert _C.lib().mhc_device_status() == 0
+
+
+def test_pre_bwd_full_grad_phi_vs_oracle():
+    """Config-3 widths (N=4, D=7168) at T=8192: grad_phi / grad_alpha / grad_base
+    (sums over every token) against the fp64 oracle run on the same saved tensors."""
+    T, N, D = 8192, 4, 7168
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=33)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    out = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True, **kw)
+    got = M.mhc_pre_clamp_sinkhorn_backward(
+        d[0], d[1], d[2], d[3], out["inv_rms"], out["x_scaled"], out["mixes"],
+        out["h_res_logits"], out["pre"], d[4], d[5], d[6], **kw)
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=-10.0, clamp_max=10.0, iter_times=20, dtype=F64)
+    for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
+        assert rel_err(a, b) <= TOL_FP32, name
+    assert rel_err(got[0], want[0]) <= TOL_BF16
