@@ -55,7 +55,7 @@ post_fwd_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
 // grad_x[j]   = sum_i h_res[j,i] gy[i]      grad_h_out  = sum_i h_post[i] gy[i]
 // grad_hres[j,i] = <x[j], gy[i]>            grad_h_post[i] = <h_out, gy[i]>
 template <typename E, int N, bool VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 post_bwd_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                 const float* __restrict__ h_res, const E* __restrict__ h_out,
                 const float* __restrict__ h_post, E* __restrict__ gx,

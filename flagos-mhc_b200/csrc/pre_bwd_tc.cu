@@ -258,6 +258,14 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 #pragma unroll
         for (int n = 0; n < N; ++n) pr[n] = 0.f;
       }
+      // this thread's 64 grad_y values serve all N sub-chunks of the item: load them once,
+      // ahead of the TMEM waits
+      uint4 gyv[8];
+      if (live) {
+        const __nv_bfloat16* gyr = gy + t * D + d0 + h * 64;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) gyv[j] = ld_stream(gyr + 8 * j);
+      }
       bool ok = true;
       for (int n = 0; n < N; ++n, ++xi, ++di) {
         const int s = xi & 1, e = di & 1;
@@ -289,13 +297,12 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&xempty[s]);
         if (live) {
-          const __nv_bfloat16* gyr = gy + t * D + d0 + h * 64;
           __nv_bfloat16* out = gx + t * HC + n * D + d0 + h * 64;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float xf[8], gf[8], o[8];
             widen<__nv_bfloat16>(xv[j], xf);
-            widen<__nv_bfloat16>(ld_keep(gyr + 8 * j), gf);
+            widen<__nv_bfloat16>(gyv[j], gf);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);

@@ -188,8 +188,10 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
         float csq = 0.f;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
+          // visit the row's 16-byte chunks in swizzled order: the 8 rows of an atom then
+          // hit 8 different bank groups (a plain c order is a 32-way bank conflict)
           float f[8];
-          widen<__nv_bfloat16>(row[c], f);
+          widen<__nv_bfloat16>(row[c ^ (r & 7)], f);
 #pragma unroll
           for (int e = 0; e < 8; ++e) csq = fmaf(f[e], f[e], csq);
         }
