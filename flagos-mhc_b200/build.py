@@ -54,6 +54,7 @@ def build(jobs=None, debug=False, verbose=False):
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(LIB_DIR, exist_ok=True)
     extra = ["-DMHC_DEBUG"] if debug else []
+    extra += os.environ.get("MHC_EXTRA_NVCC_FLAGS", "").split()
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count()) as ex:
         results = list(ex.map(lambda s: _compile(s, extra, verbose), srcs))

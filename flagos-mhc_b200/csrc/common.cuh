@@ -112,6 +112,25 @@ __device__ __forceinline__ void store_pack(E* p, const float* f) {
   }
 }
 
+// 32-byte global accesses (sm_100): a thread that owns one row writes whole 32-byte
+// sectors, halving the memory requests of row-per-thread epilogues.
+struct alignas(32) U8 {
+  uint4 a, b;
+};
+__device__ __forceinline__ void st_global_32B(void* p, const uint4& a, const uint4& b) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a.x),
+               "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+__device__ __forceinline__ U8 ld_global_32B(const void* p) {
+  U8 v;
+  asm volatile("ld.global.cs.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.a.x), "=r"(v.a.y), "=r"(v.a.z), "=r"(v.a.w), "=r"(v.b.x), "=r"(v.b.y),
+                 "=r"(v.b.z), "=r"(v.b.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -21,10 +21,25 @@
 // sums the partials of each column in a fixed order (deterministic).  The per-group
 // phi operand (80 KB) stays in shared memory for the whole segment.
 //
-// Roles (320 threads): warp 0 TMA producer; warp 1 TMEM owner + MMA issuer; warps 2-9
-// epilogue (warp w reads TMEM lane quarter w%4, column half (w-2)/4).
+// Roles (576 threads): warp 0 TMA producer; warp 1 TMEM owner + MMA issuer; warps 2-17
+// epilogue (warp w reads TMEM lane quarter w%4, column quarter (w-2)/4).
 #include "pre_common.cuh"
 #include "tc.cuh"
+
+#include <stdlib.h>
+
+#ifdef MHC_PROFILE_WAITS
+// debug-only: accumulate the cycles each role spends in each barrier wait
+#define TW(slot, expr)                                   \
+  ([&]() {                                               \
+    const long long _t0 = clock64();                     \
+    const bool _r = (expr);                              \
+    wcyc[slot] += clock64() - _t0;                       \
+    return _r;                                           \
+  }())
+#else
+#define TW(slot, expr) (expr)
+#endif
 
 namespace mhc {
 
@@ -33,7 +48,7 @@ constexpr int N = 4;
 constexpr int HM = 24;
 constexpr int GC = 128;                     // columns of d per group
 constexpr int KG = 80;                      // gxs K (72 used)
-constexpr int SUBT = 32;                    // token tiles per grad_phi cell
+constexpr int SUBT = 32;                    // max token tiles per grad_phi cell
 // shared memory (bytes, offsets from a 1024-aligned base)
 constexpr int P0_BYTES = 128 * 64 * 2;      // [128 cols][64 k] SW128
 constexpr int P1_BYTES = 128 * 16 * 2;      // [128 cols][16 k] SW32
@@ -49,34 +64,41 @@ constexpr int OFF_GP = OFF_G1 + 2 * G1_BYTES;
 constexpr int OFF_X = OFF_GP + 2 * GP_BYTES;
 constexpr int OFF_BAR = OFF_X + 2 * X_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr int THREADS = 320;
-constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 576;
+constexpr int EPI_WARPS = 16;
 // TMEM columns: D2[n] (grad_phi, 64 each) at n*64, D1[b] (gxs, 128 each) at 256 + b*128
 constexpr int TMEM_COLS = 512;
 }  // namespace bwdtc
 
 struct BwdTcMaps {
-  CUtensorMap x, g0, g1, gp, p0, p1;
+  CUtensorMap x, g0, g1, gp, p0, p1, gx;
 };
 
+// A cell is `subt` consecutive token tiles of one column group; subt never exceeds the
+// shortest CTA run, so every cell is split across at most two CTAs: slot 0 belongs to
+// the CTA holding the cell's first tile, slot 1 to a CTA whose run starts inside it.
 struct BwdGeom {
   int64_t ntiles;  // 128-token tiles
+  int64_t subt;    // tiles per cell
   int64_t cpg;     // cells per group
   int64_t items;   // groups * ntiles
   int ncta;
-  int max_segs;    // partial slots per CTA
 };
 
-__host__ __device__ inline int64_t cell_of(int64_t item, int64_t ntiles, int64_t cpg) {
+__host__ __device__ inline int64_t cell_of(int64_t item, int64_t ntiles, int64_t subt,
+                                           int64_t cpg) {
   const int64_t g = item / ntiles, i = item - g * ntiles;
-  return g * cpg + i / bwdtc::SUBT;
+  return g * cpg + i / subt;
 }
 
 __global__ void __launch_bounds__(bwdtc::THREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, __nv_bfloat16* __restrict__ gx,
-                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo) {
+                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
+                  long long* __restrict__ wdbg) {
+  long long wcyc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const long long tstart = clock64();
   using namespace bwdtc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -92,7 +114,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   uint64_t* d2full = bar + 14;
   uint64_t* d2empty = bar + 15;
   uint64_t* tdone = bar + 16;
-  uint32_t* tmem_slot = (uint32_t*)(bar + 17);
+  uint64_t* xmma = bar + 17;      // [2] the grad_phi MMAs are done reading the x stage
+  uint64_t* ostage = bar + 19;    // [2] all epilogue warps wrote grad_x into the stage
+  uint32_t* tmem_slot = (uint32_t*)(bar + 21);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -104,7 +128,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&xfull[b], 1);
-      tc::mbar_init(&xempty[b], 1 + EPI_WARPS);
+      tc::mbar_init(&xempty[b], 1);  // the thread that TMA-stores the stage's grad_x
+      tc::mbar_init(&xmma[b], 1);
+      tc::mbar_init(&ostage[b], EPI_WARPS);
       tc::mbar_init(&gfull[b], 1);
       tc::mbar_init(&gempty[b], 1);
       tc::mbar_init(&d1full[b], 1);
@@ -123,6 +149,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     tc::prefetch_tmap(&maps.g0);
     tc::prefetch_tmap(&maps.gp);
     tc::prefetch_tmap(&maps.p0);
+    tc::prefetch_tmap(&maps.gx);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -134,9 +161,10 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   const uint32_t tmem = *tmem_slot;
 
   // segment = the part of one cell this CTA owns
-  auto seg_start_of = [&](int64_t item, int64_t i) { return item == it0 || i % SUBT == 0; };
+  const int64_t subt = geo.subt;
+  auto seg_start_of = [&](int64_t item, int64_t i) { return item == it0 || i % subt == 0; };
   auto seg_end_of = [&](int64_t item, int64_t i) {
-    return item == it1 - 1 || (i + 1) % SUBT == 0 || i == ntiles - 1;
+    return item == it1 - 1 || (i + 1) % subt == 0 || i == ntiles - 1;
   };
 
   if (warp == 0) {
@@ -148,7 +176,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         const int64_t g = item / ntiles, i = item - g * ntiles;
         const int d0 = (int)(g * GC);
         if (seg_start_of(item, i)) {
-          if (!tc::mbar_wait(pempty, (seg & 1) ^ 1, abort_flag)) break;
+          if (!TW(0, tc::mbar_wait(pempty, (seg & 1) ^ 1, abort_flag))) break;
           tc::mbar_arrive_expect_tx(pfull, N * (P0_BYTES + P1_BYTES));
           for (int n = 0; n < N; ++n) {
             tc::tma_load_2d(sm + OFF_P0 + n * P0_BYTES, &maps.p0, pfull, 0, (int)(n * D + d0));
@@ -157,7 +185,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         }
         {
           const int b = gi & 1;
-          if (!tc::mbar_wait(&gempty[b], ((gi >> 1) & 1) ^ 1, abort_flag)) break;
+          if (!TW(1, tc::mbar_wait(&gempty[b], ((gi >> 1) & 1) ^ 1, abort_flag))) break;
           tc::mbar_arrive_expect_tx(&gfull[b], G0_BYTES + G1_BYTES + GP_BYTES);
           tc::tma_load_2d(sm + OFF_G0 + b * G0_BYTES, &maps.g0, &gfull[b], 0, (int)(i * 128));
           tc::tma_load_2d(sm + OFF_G1 + b * G1_BYTES, &maps.g1, &gfull[b], 0, (int)(i * 128));
@@ -166,7 +194,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         }
         for (int n = 0; n < N; ++n, ++xi) {
           const int s = xi & 1;
-          if (!tc::mbar_wait(&xempty[s], ((xi >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          if (!TW(2, tc::mbar_wait(&xempty[s], ((xi >> 1) & 1) ^ 1, abort_flag))) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&xfull[s], X_BYTES);
           uint8_t* dst = sm + OFF_X + s * X_BYTES;
           const int col = (int)(n * D + d0);
@@ -178,58 +206,75 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Software-pipelined by one step: iteration st issues the gxs MMAs of step st (they
+    // need only the per-item G and the stationary P, never x) and then the grad_phi MMAs
+    // of step st-1 (which need the x tile).  D1 therefore never waits on an x load.
     if (lane == 0) {
       constexpr uint32_t id_gxs = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_gphi = tc::idesc_bf16(128, 64, true, true);
-      uint32_t xi = 0, gi = 0, seg = 0, di = 0;
+      const int64_t nsteps = (it1 - it0) * N;
+      uint32_t seg_a = 0, seg_b = 0;
       bool ok = true;
-      for (int64_t item = it0; item < it1 && ok; ++item) {
-        const int64_t i = item % ntiles;
-        const bool seg_start = seg_start_of(item, i);
-        if (seg_start) {
-          if (!tc::mbar_wait(pfull, seg & 1, abort_flag)) break;
-          if (!tc::mbar_wait(d2empty, (seg & 1) ^ 1, abort_flag)) break;
-        }
-        const int b = gi & 1;
-        if (!tc::mbar_wait(&gfull[b], (gi >> 1) & 1, abort_flag)) break;
-        tc::tc_fence_after();
-        const uint32_t sg0 = tc::smem_u32(sm + OFF_G0 + b * G0_BYTES);
-        const uint32_t sg1 = tc::smem_u32(sm + OFF_G1 + b * G1_BYTES);
-        const uint32_t sgp = tc::smem_u32(sm + OFF_GP + b * GP_BYTES);
-        for (int n = 0; n < N; ++n, ++xi, ++di) {
-          const int s = xi & 1, e = di & 1;
-          if (!tc::mbar_wait(&xfull[s], (xi >> 1) & 1, abort_flag)) { ok = false; break; }
-          if (!tc::mbar_wait(&d1empty[e], ((di >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+      for (int64_t st = 0; st <= nsteps && ok; ++st) {
+        if (st < nsteps) {
+          // ---- gxs of step st
+          const int64_t item = it0 + st / N, i = item % ntiles;
+          const int n = (int)(st % N);
+          const uint32_t gi = (uint32_t)(item - it0);
+          const int b = gi & 1, e = (int)(st & 1);
+          if (n == 0) {
+            if (seg_start_of(item, i) && !TW(0, tc::mbar_wait(pfull, seg_a & 1, abort_flag))) break;
+            if (!TW(0, tc::mbar_wait(&gfull[b], (gi >> 1) & 1, abort_flag))) break;
+          }
+          if (!TW(1, tc::mbar_wait(&d1empty[e], ((st >> 1) & 1) ^ 1, abort_flag))) break;
           tc::tc_fence_after();
-          // gxs tile: D1[e] = G' * P'(n)^T, K = 64 (SW128) + 16 (SW32)
           const uint32_t d1 = tmem + 256 + e * 128;
-          const uint32_t sp0 = tc::smem_u32(sm + OFF_P0 + n * P0_BYTES);
-          const uint32_t sp1 = tc::smem_u32(sm + OFF_P1 + n * P1_BYTES);
-          const uint64_t a0 = tc::smem_desc(sg0, 16, 1024, tc::kSwizzle128);
-          const uint64_t b0 = tc::smem_desc(sp0, 16, 1024, tc::kSwizzle128);
+          const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + OFF_G0 + b * G0_BYTES), 16, 1024,
+                                            tc::kSwizzle128);
+          const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + OFF_P0 + n * P0_BYTES), 16, 1024,
+                                            tc::kSwizzle128);
 #pragma unroll
           for (int k = 0; k < 4; ++k) tc::mma_bf16(d1, a0 + 2 * k, b0 + 2 * k, id_gxs, k != 0);
-          tc::mma_bf16(d1, tc::smem_desc(sg1, 16, 256, tc::kSwizzle32),
-                       tc::smem_desc(sp1, 16, 256, tc::kSwizzle32), id_gxs, 1);
+          tc::mma_bf16(d1,
+                       tc::smem_desc(tc::smem_u32(sm + OFF_G1 + b * G1_BYTES), 16, 256,
+                                     tc::kSwizzle32),
+                       tc::smem_desc(tc::smem_u32(sm + OFF_P1 + n * P1_BYTES), 16, 256,
+                                     tc::kSwizzle32),
+                       id_gxs, 1);
           tc::mma_commit(&d1full[e]);
-          // grad_phi: D2[n] (+)= x_tile^T (MN-major, M = 128 columns) * Gp (MN-major, N = 64)
+          if (n == N - 1 && seg_end_of(item, i)) {
+            tc::mma_commit(pempty);  // last use of this segment's P
+            ++seg_a;
+          }
+        }
+        if (st >= 1) {
+          // ---- grad_phi of step sb = st - 1: D2[n] (+)= x_tile^T * Gp
+          const int64_t sb = st - 1;
+          const int64_t item = it0 + sb / N, i = item % ntiles;
+          const int n = (int)(sb % N);
+          const uint32_t gi = (uint32_t)(item - it0);
+          const int b = gi & 1, s = (int)(sb & 1);
+          const bool seg_start = seg_start_of(item, i);
+          if (n == 0 && seg_start && !TW(2, tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag))) break;
+          if (!TW(3, tc::mbar_wait(&xfull[s], (sb >> 1) & 1, abort_flag))) break;
+          tc::tc_fence_after();
           const uint32_t d2 = tmem + n * 64;
           const uint32_t sx = tc::smem_u32(sm + OFF_X + s * X_BYTES);
+          const uint32_t sgp = tc::smem_u32(sm + OFF_GP + b * GP_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t ax = tc::smem_desc(sx + kk * 2048, X_BYTES / 2, 1024, tc::kSwizzle128);
             const uint64_t bg = tc::smem_desc(sgp + kk * 2048, GP_BYTES, 1024, tc::kSwizzle128);
             tc::mma_bf16(d2, ax, bg, id_gphi, (seg_start && kk == 0) ? 0u : 1u);
           }
-          tc::mma_commit(&xempty[s]);
-        }
-        if (!ok) break;
-        tc::mma_commit(&gempty[b]);
-        ++gi;
-        if (seg_end_of(item, i)) {
-          tc::mma_commit(d2full);
-          tc::mma_commit(pempty);
-          ++seg;
+          tc::mma_commit(&xmma[s]);
+          if (n == N - 1) {
+            tc::mma_commit(&gempty[b]);
+            if (seg_end_of(item, i)) {
+              tc::mma_commit(d2full);
+              ++seg_b;
+            }
+          }
         }
       }
       tc::mma_commit(tdone);
@@ -238,97 +283,125 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     }
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int q = warp & 3;                 // TMEM lane quarter
-    const int h = (warp - 2) >> 2;          // column half (0: cols 0-63, 1: 64-127)
+    // 16 warps: lane quarter q = warp % 4 (the TMEM lanes this warp may read), column
+    // quarter h = (warp - 2) / 4 (32 of the group's 128 columns).
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;            // token row (D1) / column row (D2)
-    uint32_t xi = 0, di = 0, seg = 0;
-    const int64_t cell_first = cell_of(it0, ntiles, geo.cpg);
+    uint32_t di = 0, seg = 0;
+    bool first_seg = true;
     for (int64_t item = it0; item < it1; ++item) {
       const int64_t g = item / ntiles, i = item - g * ntiles;
       const int64_t d0 = g * GC;
       const int64_t t = i * 128 + r;
       const bool live = t < T;
       float inv = 0.f, cf = 0.f, pr[N];
+      uint4 gyv[4];
       if (live) {
         inv = inv_rms[t];
         cf = coef[t];
 #pragma unroll
         for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
+        const __nv_bfloat16* gyr = gy + t * D + d0 + h * 32;
+        const U8 g01 = ld_global_32B(gyr), g23 = ld_global_32B(gyr + 16);
+        gyv[0] = g01.a; gyv[1] = g01.b; gyv[2] = g23.a; gyv[3] = g23.b;
       } else {
 #pragma unroll
         for (int n = 0; n < N; ++n) pr[n] = 0.f;
-      }
-      // this thread's 64 grad_y values serve all N sub-chunks of the item: load them once,
-      // ahead of the TMEM waits
-      uint4 gyv[8];
-      if (live) {
-        const __nv_bfloat16* gyr = gy + t * D + d0 + h * 64;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) gyv[j] = ld_stream(gyr + 8 * j);
+        for (int j = 0; j < 4; ++j) gyv[j] = make_uint4(0, 0, 0, 0);
       }
       bool ok = true;
-      for (int n = 0; n < N; ++n, ++xi, ++di) {
-        const int s = xi & 1, e = di & 1;
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag))) {
+      for (int n = 0; n < N; ++n, ++di) {
+        const int e = di & 1, s = di & 1;
+        if (!__all_sync(0xffffffffu, TW(0, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag)))) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        float acc[64];
-        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 64;
-#pragma unroll
-        for (int m = 0; m < 4; ++m) tc::tmem_ld16(ta + m * 16, acc + m * 16);
+        float acc[32];
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 32;
+#ifdef MHC_PROFILE_WAITS
+        long long _p0 = clock64();
+#endif
+        tc::tmem_ld16(ta, acc);
+        tc::tmem_ld16(ta + 16, acc + 16);
         tc::tmem_ld_wait();
+#ifdef MHC_PROFILE_WAITS
+        wcyc[3] += clock64() - _p0;
+#endif
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&d1empty[e]);
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&xfull[s], (xi >> 1) & 1, abort_flag))) {
+        if (!__all_sync(0xffffffffu, TW(1, tc::mbar_wait(&xfull[s], (di >> 1) & 1, abort_flag)))) {
           ok = false;
           break;
         }
-        // x row r, columns [64h, 64h+64) of the staged tile (128B-swizzled rows)
-        const uint8_t* xrow = sm + OFF_X + s * X_BYTES + h * (X_BYTES / 2) + r * 128;
-        uint4 xv[8];
+        // x row r, columns [32h, 32h+32): box h/2, 16-byte chunks 4(h%2)..+3 (swizzled)
+        uint8_t* stage = sm + OFF_X + s * X_BYTES;
+        uint8_t* xrow = stage + (h >> 1) * (X_BYTES / 2) + r * 128;
+        uint4 xv[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          xv[j] = *reinterpret_cast<const uint4*>(xrow + ((j ^ (r & 7)) << 4));
-        // the x stage is refilled by TMA (async proxy): order these reads before it
-        tc::fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&xempty[s]);
-        if (live) {
-          __nv_bfloat16* out = gx + t * HC + n * D + d0 + h * 64;
+        for (int j = 0; j < 4; ++j)
+          xv[j] = *reinterpret_cast<const uint4*>(xrow + ((((h & 1) * 4 + j) ^ (r & 7)) << 4));
+#ifdef MHC_PROFILE_WAITS
+        long long _p2 = clock64();
+#endif
+        uint4 ov[4];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float xf[8], gf[8], o[8];
-            widen<__nv_bfloat16>(xv[j], xf);
-            widen<__nv_bfloat16>(gyv[j], gf);
+        for (int j = 0; j < 4; ++j) {
+          float xf[8], gf[8], o[8];
+          widen<__nv_bfloat16>(xv[j], xf);
+          widen<__nv_bfloat16>(gyv[j], gf);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);
-              o[u] = fmaf(gf[u], pr[n], rr);
-            }
-            st_stream(out + 8 * j, narrow<__nv_bfloat16>(o));
+          for (int u = 0; u < 8; ++u) {
+            const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);
+            o[u] = fmaf(gf[u], pr[n], rr);
           }
+          ov[j] = narrow<__nv_bfloat16>(o);
         }
+        // grad_x goes back into the x stage (same swizzled bytes this thread just read)
+        // once the grad_phi MMAs are done with it; then one thread TMA-stores the tile
+        if (!__all_sync(0xffffffffu, TW(6, tc::mbar_wait(&xmma[s], (di >> 1) & 1, abort_flag)))) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(xrow + ((((h & 1) * 4 + j) ^ (r & 7)) << 4)) = ov[j];
+        tc::fence_proxy_async();        // generic smem writes -> async-proxy (TMA) reads
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ostage[s]);
+        if (warp == 2 && lane == 0) {
+          if (!tc::mbar_wait(&ostage[s], (di >> 1) & 1, abort_flag)) { ok = false; break; }
+          const int col = (int)(n * D + d0);
+          tc::tma_store_2d(&maps.gx, stage, col, (int)(i * 128));
+          tc::tma_store_2d(&maps.gx, stage + X_BYTES / 2, col + 64, (int)(i * 128));
+          tc::bulk_commit_group();
+          tc::bulk_wait_read<0>();       // the store has read the stage: refill it
+          tc::mbar_arrive(&xempty[s]);
+        }
+#ifdef MHC_PROFILE_WAITS
+        wcyc[5] += clock64() - _p2;
+#endif
       }
       if (!ok) break;
       if (seg_end_of(item, i)) {
-        // flush: D2[n] row r = column d0 + r; cols k: hi k, lo 24 + k
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(d2full, seg & 1, abort_flag))) break;
+        // flush: D2[h] row r = column d0 + r; cols k: hi k, lo 24 + k
+        if (!__all_sync(0xffffffffu, TW(2, tc::mbar_wait(d2full, seg & 1, abort_flag)))) break;
         tc::tc_fence_after();
-        const int lseg = (int)(cell_of(item, ntiles, geo.cpg) - cell_first);
-        for (int nn = 2 * h; nn < 2 * h + 2; ++nn) {
-          float v[48];
-          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + nn * 64;
+        // slot 1 iff this CTA's run began inside the cell
+        const int64_t slot = cell_of(item, ntiles, subt, geo.cpg) * 2 +
+                             ((first_seg && (it0 % ntiles) % subt != 0) ? 1 : 0);
+        first_seg = false;
+        float v[48];
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * 64;
 #pragma unroll
-          for (int m = 0; m < 3; ++m) tc::tmem_ld16(ta + m * 16, v + m * 16);
-          tc::tmem_ld_wait();
-          float* dst =
-              gphi_part + (((int64_t)blockIdx.x * geo.max_segs + lseg) * N + nn) * HM * GC;
+        for (int m = 0; m < 3; ++m) tc::tmem_ld16(ta + m * 16, v + m * 16);
+        tc::tmem_ld_wait();
+        float* dst = gphi_part + (slot * N + h) * HM * GC;
 #pragma unroll
-          for (int k = 0; k < HM; ++k) dst[k * GC + r] = v[k] + v[HM + k];
-        }
+        for (int k = 0; k < HM; ++k) dst[k * GC + r] = v[k] + v[HM + k];
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(d2empty);
@@ -336,7 +409,18 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       }
     }
   }
+  if (warp == 2 && lane == 0) tc::bulk_wait_all<0>();  // grad_x stores have landed
   if (*abort_flag && threadIdx.x == 0) flag_timeout();
+#ifdef MHC_PROFILE_WAITS
+  // row per CTA: [total, producer x4, mma x4, epilogue warp 2 x4]
+  if (wdbg != nullptr && lane == 0 && (warp <= 2)) {
+    long long* row = wdbg + (int64_t)blockIdx.x * 32;
+    if (warp == 0) row[0] = clock64() - tstart;
+    for (int k = 0; k < 8; ++k) row[1 + warp * 8 + k] = wcyc[k];
+  }
+#else
+  (void)wdbg; (void)tstart; (void)wcyc;
+#endif
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -373,8 +457,8 @@ __global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi,
   d1[1] = rv[9];
 }
 
-// grad_phi[k][n*D + g*128 + c] = sum over the cells of group g, and within a cell over
-// the CTAs that own part of it (in CTA order), of their partials.
+// grad_phi[k][n*D + g*128 + c] = sum over the cells of group g (in order) of slot 0,
+// plus slot 1 where a CTA run boundary falls strictly inside the cell.
 __global__ void pre_bwd_gphi_reduce_kernel(const float* __restrict__ part,
                                            float* __restrict__ grad_phi, int64_t D,
                                            BwdGeom geo) {
@@ -382,28 +466,22 @@ __global__ void pre_bwd_gphi_reduce_kernel(const float* __restrict__ part,
   const int64_t G = D / GC;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (g, n, k, c)
   if (idx >= G * N * HM * GC) return;
-  const int c = (int)(idx % GC);
-  const int k = (int)((idx / GC) % HM);
-  const int n = (int)((idx / (GC * HM)) % N);
-  const int64_t g = idx / (GC * HM * N);
-  const int64_t items = geo.items, ntiles = geo.ntiles;
-  const int ncta = geo.ncta;
+  const int64_t inner = idx % (N * HM * GC);   // (n, k, c) inside a slot
+  const int n = (int)(inner / (HM * GC));
+  const int k = (int)((inner / GC) % HM);
+  const int c = (int)(inner % GC);
+  const int64_t g = idx / (N * HM * GC);
   float s = 0.f;
   for (int64_t ci = 0; ci < geo.cpg; ++ci) {
-    const int64_t lo_item = g * ntiles + ci * SUBT;
-    int64_t hi_item = lo_item + SUBT;
-    if (hi_item > (g + 1) * ntiles) hi_item = (g + 1) * ntiles;
-    // first CTA whose run [it0, it1) ends after lo_item
-    int b = (int)(lo_item * ncta / items);
-    while (b > 0 && items * b / ncta > lo_item) --b;
-    while (b < ncta - 1 && items * (b + 1) / ncta <= lo_item) ++b;
-    for (; b < ncta; ++b) {
-      const int64_t it0 = items * b / ncta, it1 = items * (b + 1) / ncta;
-      if (it0 >= hi_item) break;
-      if (it1 <= lo_item || it1 <= it0) continue;
-      const int64_t lseg = g * geo.cpg + ci - cell_of(it0, ntiles, geo.cpg);
-      s += part[((((int64_t)b * geo.max_segs + lseg) * N + n) * HM + k) * GC + c];
-    }
+    const int64_t cell = g * geo.cpg + ci;
+    s += part[(cell * 2) * (N * HM * GC) + inner];
+    const int64_t lo = g * geo.ntiles + ci * geo.subt;
+    int64_t hi = lo + geo.subt;
+    if (hi > (g + 1) * geo.ntiles) hi = (g + 1) * geo.ntiles;
+    // first run boundary items*b/ncta above lo
+    int64_t b = lo * geo.ncta / geo.items;
+    while (geo.items * b / geo.ncta <= lo) ++b;
+    if (b < geo.ncta && geo.items * b / geo.ncta < hi) s += part[(cell * 2 + 1) * (N * HM * GC) + inner];
   }
   grad_phi[(int64_t)k * (N * D) + n * D + g * GC + c] = s;
 }
@@ -421,20 +499,14 @@ bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const v
 static BwdGeom bwd_tc_geometry(int64_t T, int64_t D) {
   BwdGeom g;
   g.ntiles = cdiv(T, 128);
-  g.cpg = cdiv(g.ntiles, bwdtc::SUBT);
   g.items = (D / bwdtc::GC) * g.ntiles;
   int n = sm_count();
   if (g.items < n) n = (int)g.items;
   g.ncta = n < 1 ? 1 : n;
-  int64_t ms = 1;
-  for (int b = 0; b < g.ncta; ++b) {
-    const int64_t i0 = g.items * b / g.ncta, i1 = g.items * (b + 1) / g.ncta;
-    if (i1 > i0) {
-      const int64_t c = cell_of(i1 - 1, g.ntiles, g.cpg) - cell_of(i0, g.ntiles, g.cpg) + 1;
-      if (c > ms) ms = c;
-    }
-  }
-  g.max_segs = (int)ms;
+  const int64_t shortest_run = g.items / g.ncta;  // >= 1
+  g.subt = shortest_run < bwdtc::SUBT ? shortest_run : bwdtc::SUBT;
+  if (g.subt < 1) g.subt = 1;
+  g.cpg = cdiv(g.ntiles, g.subt);
   return g;
 }
 
@@ -456,7 +528,7 @@ static BwdTcWs bwd_tc_layout(char* base, int64_t T, int64_t D) {
   w.gp = (__nv_bfloat16*)take((size_t)Tp * 64 * 2);
   w.p0 = (__nv_bfloat16*)take((size_t)HC * 64 * 2);
   w.p1 = (__nv_bfloat16*)take((size_t)HC * 16 * 2);
-  w.part = (float*)take((size_t)geo.ncta * geo.max_segs * N * HM * GC * 4);
+  w.part = (float*)take((size_t)(D / GC) * geo.cpg * 2 * N * HM * GC * 4);
   w.total = off;
   return w;
 }
@@ -495,6 +567,9 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
     return st;
   if ((st = make_tmap_2d(&m.p1, w.p1, bf, 2, 16, HC, 32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B)))
     return st;
+  if ((st = make_tmap_2d(&m.gx, a.grad_x, bf, 2, HC, T, HC * 2, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -505,7 +580,15 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
   }
   pre_bwd_tc_kernel<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
-                                                    (__nv_bfloat16*)a.grad_x, w.part, T, D, geo);
+                                                    (__nv_bfloat16*)a.grad_x, w.part, T, D, geo,
+#ifdef MHC_PROFILE_WAITS
+                                                    getenv("MHC_WAIT_DBG")
+                                                        ? (long long*)strtoull(getenv("MHC_WAIT_DBG"), nullptr, 10)
+                                                        : nullptr
+#else
+                                                    nullptr
+#endif
+  );
   MHC_LAUNCH_CHECK();
   const int64_t n = (D / GC) * N * HM * GC;
   pre_bwd_gphi_reduce_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.part, a.grad_phi, D, geo);
