@@ -59,10 +59,11 @@ constexpr int X_BYTES = 2 * 128 * 64 * 2;   // two [128 tok][64 col] boxes
 constexpr int OFF_P0 = 0;
 constexpr int OFF_P1 = OFF_P0 + N * P0_BYTES;
 constexpr int OFF_G0 = OFF_P1 + N * P1_BYTES;
-constexpr int OFF_G1 = OFF_G0 + 2 * G0_BYTES;
-constexpr int OFF_GP = OFF_G1 + 2 * G1_BYTES;
-constexpr int OFF_X = OFF_GP + 2 * GP_BYTES;
-constexpr int OFF_BAR = OFF_X + 2 * X_BYTES;
+constexpr int XS = 3;                       // x stages (G is single-buffered)
+constexpr int OFF_G1 = OFF_G0 + G0_BYTES;
+constexpr int OFF_GP = OFF_G1 + G1_BYTES;
+constexpr int OFF_X = OFF_GP + GP_BYTES;
+constexpr int OFF_BAR = OFF_X + XS * X_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
 constexpr int THREADS = 576;
 constexpr int EPI_WARPS = 16;
@@ -103,39 +104,40 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
-  uint64_t* xfull = bar;          // [2]
-  uint64_t* xempty = bar + 2;     // [2]
-  uint64_t* gfull = bar + 4;      // [2]
-  uint64_t* gempty = bar + 6;     // [2]
-  uint64_t* pfull = bar + 8;
-  uint64_t* pempty = bar + 9;
-  uint64_t* d1full = bar + 10;    // [2]
-  uint64_t* d1empty = bar + 12;   // [2]
-  uint64_t* d2full = bar + 14;
-  uint64_t* d2empty = bar + 15;
-  uint64_t* tdone = bar + 16;
-  uint64_t* xmma = bar + 17;      // [2] the grad_phi MMAs are done reading the x stage
-  uint64_t* ostage = bar + 19;    // [2] all epilogue warps wrote grad_x into the stage
-  uint32_t* tmem_slot = (uint32_t*)(bar + 21);
+  uint64_t* xfull = bar;             // [XS] x tile landed
+  uint64_t* xempty = bar + XS;       // [XS] its grad_x store has read the stage
+  uint64_t* xmma = bar + 2 * XS;     // [XS] the grad_phi MMAs are done reading the x tile
+  uint64_t* ostage = bar + 3 * XS;   // [XS] all epilogue warps wrote grad_x into the stage
+  uint64_t* gfull = bar + 4 * XS;
+  uint64_t* gempty = gfull + 1;
+  uint64_t* pfull = gfull + 2;
+  uint64_t* pempty = gfull + 3;
+  uint64_t* d1full = gfull + 4;      // [2]
+  uint64_t* d1empty = gfull + 6;     // [2]
+  uint64_t* d2full = gfull + 8;
+  uint64_t* d2empty = gfull + 9;
+  uint64_t* tdone = gfull + 10;
+  uint32_t* tmem_slot = (uint32_t*)(gfull + 11);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t HC = N * D;
   const int64_t ntiles = geo.ntiles;
   const int64_t it0 = geo.items * blockIdx.x / gridDim.x;
   const int64_t it1 = geo.items * (blockIdx.x + 1) / gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < XS; ++b) {
       tc::mbar_init(&xfull[b], 1);
       tc::mbar_init(&xempty[b], 1);  // the thread that TMA-stores the stage's grad_x
       tc::mbar_init(&xmma[b], 1);
       tc::mbar_init(&ostage[b], EPI_WARPS);
-      tc::mbar_init(&gfull[b], 1);
-      tc::mbar_init(&gempty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&d1full[b], 1);
       tc::mbar_init(&d1empty[b], EPI_WARPS);
     }
+    tc::mbar_init(gfull, 1);
+    tc::mbar_init(gempty, 1);
     tc::mbar_init(pfull, 1);
     tc::mbar_init(pempty, 1);
     tc::mbar_init(d2full, 1);
@@ -183,23 +185,23 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             tc::tma_load_2d(sm + OFF_P1 + n * P1_BYTES, &maps.p1, pfull, 0, (int)(n * D + d0));
           }
         }
-        {
-          const int b = gi & 1;
-          if (!TW(1, tc::mbar_wait(&gempty[b], ((gi >> 1) & 1) ^ 1, abort_flag))) break;
-          tc::mbar_arrive_expect_tx(&gfull[b], G0_BYTES + G1_BYTES + GP_BYTES);
-          tc::tma_load_2d(sm + OFF_G0 + b * G0_BYTES, &maps.g0, &gfull[b], 0, (int)(i * 128));
-          tc::tma_load_2d(sm + OFF_G1 + b * G1_BYTES, &maps.g1, &gfull[b], 0, (int)(i * 128));
-          tc::tma_load_2d(sm + OFF_GP + b * GP_BYTES, &maps.gp, &gfull[b], 0, (int)(i * 128));
-          ++gi;
-        }
         for (int n = 0; n < N; ++n, ++xi) {
-          const int s = xi & 1;
-          if (!TW(2, tc::mbar_wait(&xempty[s], ((xi >> 1) & 1) ^ 1, abort_flag))) { ok = false; break; }
+          const int s = xi % XS;
+          if (!TW(2, tc::mbar_wait(&xempty[s], ((xi / XS) & 1) ^ 1, abort_flag))) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&xfull[s], X_BYTES);
           uint8_t* dst = sm + OFF_X + s * X_BYTES;
           const int col = (int)(n * D + d0);
           tc::tma_load_2d(dst, &maps.x, &xfull[s], col, (int)(i * 128));
           tc::tma_load_2d(dst + X_BYTES / 2, &maps.x, &xfull[s], col + 64, (int)(i * 128));
+          if (n == 0) {
+            // the item's G operands (single buffer) once the previous item's MMAs are done
+            if (!TW(1, tc::mbar_wait(gempty, (gi & 1) ^ 1, abort_flag))) { ok = false; break; }
+            tc::mbar_arrive_expect_tx(gfull, G0_BYTES + G1_BYTES + GP_BYTES);
+            tc::tma_load_2d(sm + OFF_G0, &maps.g0, gfull, 0, (int)(i * 128));
+            tc::tma_load_2d(sm + OFF_G1, &maps.g1, gfull, 0, (int)(i * 128));
+            tc::tma_load_2d(sm + OFF_GP, &maps.gp, gfull, 0, (int)(i * 128));
+            ++gi;
+          }
         }
         if (seg_end_of(item, i)) ++seg;
       }
@@ -207,8 +209,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // Software-pipelined by one step: iteration st issues the gxs MMAs of step st (they
-    // need only the per-item G and the stationary P, never x) and then the grad_phi MMAs
-    // of step st-1 (which need the x tile).  D1 therefore never waits on an x load.
+    // need only the per-item G and the stationary P, never x) and the grad_phi MMAs of
+    // step st-1 (which need the x tile), so D1 does not wait on the x load of its step.
     if (lane == 0) {
       constexpr uint32_t id_gxs = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_gphi = tc::idesc_bf16(128, 64, true, true);
@@ -216,27 +218,27 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       uint32_t seg_a = 0, seg_b = 0;
       bool ok = true;
       for (int64_t st = 0; st <= nsteps && ok; ++st) {
-        if (st < nsteps) {
+        auto issue_gxs = [&](int64_t st) -> bool {
           // ---- gxs of step st
           const int64_t item = it0 + st / N, i = item % ntiles;
           const int n = (int)(st % N);
           const uint32_t gi = (uint32_t)(item - it0);
-          const int b = gi & 1, e = (int)(st & 1);
+          const int e = (int)(st & 1);
           if (n == 0) {
-            if (seg_start_of(item, i) && !TW(0, tc::mbar_wait(pfull, seg_a & 1, abort_flag))) break;
-            if (!TW(0, tc::mbar_wait(&gfull[b], (gi >> 1) & 1, abort_flag))) break;
+            if (seg_start_of(item, i) && !TW(0, tc::mbar_wait(pfull, seg_a & 1, abort_flag))) return false;
+            if (!TW(0, tc::mbar_wait(gfull, gi & 1, abort_flag))) return false;
           }
-          if (!TW(1, tc::mbar_wait(&d1empty[e], ((st >> 1) & 1) ^ 1, abort_flag))) break;
+          if (!TW(1, tc::mbar_wait(&d1empty[e], ((st >> 1) & 1) ^ 1, abort_flag))) return false;
           tc::tc_fence_after();
           const uint32_t d1 = tmem + 256 + e * 128;
-          const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + OFF_G0 + b * G0_BYTES), 16, 1024,
+          const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + OFF_G0), 16, 1024,
                                             tc::kSwizzle128);
           const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + OFF_P0 + n * P0_BYTES), 16, 1024,
                                             tc::kSwizzle128);
 #pragma unroll
           for (int k = 0; k < 4; ++k) tc::mma_bf16(d1, a0 + 2 * k, b0 + 2 * k, id_gxs, k != 0);
           tc::mma_bf16(d1,
-                       tc::smem_desc(tc::smem_u32(sm + OFF_G1 + b * G1_BYTES), 16, 256,
+                       tc::smem_desc(tc::smem_u32(sm + OFF_G1), 16, 256,
                                      tc::kSwizzle32),
                        tc::smem_desc(tc::smem_u32(sm + OFF_P1 + n * P1_BYTES), 16, 256,
                                      tc::kSwizzle32),
@@ -246,21 +248,20 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             tc::mma_commit(pempty);  // last use of this segment's P
             ++seg_a;
           }
-        }
-        if (st >= 1) {
+          return true;
+        };
+        auto issue_gphi = [&](int64_t sb) -> bool {
           // ---- grad_phi of step sb = st - 1: D2[n] (+)= x_tile^T * Gp
-          const int64_t sb = st - 1;
           const int64_t item = it0 + sb / N, i = item % ntiles;
           const int n = (int)(sb % N);
-          const uint32_t gi = (uint32_t)(item - it0);
-          const int b = gi & 1, s = (int)(sb & 1);
+          const int s = (int)(sb % XS);
           const bool seg_start = seg_start_of(item, i);
-          if (n == 0 && seg_start && !TW(2, tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag))) break;
-          if (!TW(3, tc::mbar_wait(&xfull[s], (sb >> 1) & 1, abort_flag))) break;
+          if (n == 0 && seg_start && !TW(2, tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag))) return false;
+          if (!TW(3, tc::mbar_wait(&xfull[s], (sb / XS) & 1, abort_flag))) return false;
           tc::tc_fence_after();
           const uint32_t d2 = tmem + n * 64;
           const uint32_t sx = tc::smem_u32(sm + OFF_X + s * X_BYTES);
-          const uint32_t sgp = tc::smem_u32(sm + OFF_GP + b * GP_BYTES);
+          const uint32_t sgp = tc::smem_u32(sm + OFF_GP);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t ax = tc::smem_desc(sx + kk * 2048, X_BYTES / 2, 1024, tc::kSwizzle128);
@@ -269,12 +270,22 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
           }
           tc::mma_commit(&xmma[s]);
           if (n == N - 1) {
-            tc::mma_commit(&gempty[b]);
+            tc::mma_commit(gempty);
             if (seg_end_of(item, i)) {
               tc::mma_commit(d2full);
               ++seg_b;
             }
           }
+          return true;
+        };
+        // At an item boundary the previous item's last grad_phi MMAs go first: they
+        // release the single G buffer that the next item's gxs MMAs wait for.
+        if (st % N == 0) {
+          if (st >= 1 && !issue_gphi(st - 1)) { ok = false; break; }
+          if (st < nsteps && !issue_gxs(st)) { ok = false; break; }
+        } else {
+          if (st < nsteps && !issue_gxs(st)) { ok = false; break; }
+          if (st >= 1 && !issue_gphi(st - 1)) { ok = false; break; }
         }
       }
       tc::mma_commit(tdone);
@@ -313,7 +324,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       }
       bool ok = true;
       for (int n = 0; n < N; ++n, ++di) {
-        const int e = di & 1, s = di & 1;
+        const int e = di & 1, s = di % XS;
+        const uint32_t xph = (di / XS) & 1;
         if (!__all_sync(0xffffffffu, TW(0, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag)))) {
           ok = false;
           break;
@@ -333,7 +345,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&d1empty[e]);
-        if (!__all_sync(0xffffffffu, TW(1, tc::mbar_wait(&xfull[s], (di >> 1) & 1, abort_flag)))) {
+        if (!__all_sync(0xffffffffu, TW(1, tc::mbar_wait(&xfull[s], xph, abort_flag)))) {
           ok = false;
           break;
         }
@@ -362,7 +374,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         }
         // grad_x goes back into the x stage (same swizzled bytes this thread just read)
         // once the grad_phi MMAs are done with it; then one thread TMA-stores the tile
-        if (!__all_sync(0xffffffffu, TW(6, tc::mbar_wait(&xmma[s], (di >> 1) & 1, abort_flag)))) {
+        if (!__all_sync(0xffffffffu, TW(6, tc::mbar_wait(&xmma[s], xph, abort_flag)))) {
           ok = false;
           break;
         }
@@ -373,7 +385,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ostage[s]);
         if (warp == 2 && lane == 0) {
-          if (!tc::mbar_wait(&ostage[s], (di >> 1) & 1, abort_flag)) { ok = false; break; }
+          if (!tc::mbar_wait(&ostage[s], xph, abort_flag)) { ok = false; break; }
           const int col = (int)(n * D + d0);
           tc::tma_store_2d(&maps.gx, stage, col, (int)(i * 128));
           tc::tma_store_2d(&maps.gx, stage + X_BYTES / 2, col + 64, (int)(i * 128));
