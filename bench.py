@@ -70,50 +70,72 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms by a reader thread;
+    stop() keeps the samples taken between mark_start() and mark_stop()."""
     Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, uuid):
         self.uuid = (uuid or "").lower()
         self.proc = None
+        self.rows = []          # (time, fields)
+        self.t0 = self.t1 = None
 
-    def start(self):
+    def _reader(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.rows.append((time.perf_counter(), [c.strip() for c in ln.split(",")]))
+
+    def start(self, wait_s=5.0):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return
+        threading.Thread(target=self._reader, daemon=True).start()
+        t = time.perf_counter()
+        while not self.rows and time.perf_counter() - t < wait_s:
+            time.sleep(0.01)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_stop(self):
+        self.t1 = time.perf_counter()
 
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.25)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-            out, _ = self.proc.communicate()
-        rows = [[c.strip() for c in ln.split(",")] for ln in out.splitlines() if ln.strip()]
+        rows = [f for t, f in self.rows if self.t0 is not None and self.t0 <= t <= (self.t1 or t)]
+        window = "timed region"
+        if not rows:  # region shorter than one sample period: nearest samples after its start
+            rows = [f for t, f in self.rows if self.t0 is not None and t >= self.t0][:3]
+            window = "first samples after the timed region began"
         mine = [r for r in rows if self.uuid and self.uuid in r[0].lower()] or rows
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in mine:
             try:
                 sm.append(float(r[1]))
                 mx.append(float(r[2]))
             except (ValueError, IndexError):
                 continue
-            for n, v in zip(names, r[5:9]):
+            for n, v in zip(self.NAMES, r[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 def make_inputs(T, N, D, seed, dev):
@@ -290,11 +312,13 @@ def main():
     torch.cuda.synchronize()
     clocks.start()
     n0 = _C.lib().mhc_kernel_launches()
+    clocks.mark_start()
     start.record()
     for k in range(K):
         run_step(M, inp, world, evs[k])
     stop.record()
     torch.cuda.synchronize()
+    clocks.mark_stop()
     launches = _C.lib().mhc_kernel_launches() - n0
     if world > 1:
         dist.barrier()

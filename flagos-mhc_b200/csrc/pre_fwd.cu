@@ -139,6 +139,55 @@ pre_apply_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
   }
 }
 
+// bf16 x, D % 16 == 0: a lane handles 16 consecutive d per row with 32-byte accesses
+// (one load per row of x, one store of y, two stores of x_scaled per row).
+template <int N>
+__global__ void __launch_bounds__(256)
+pre_apply_bf16x16_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ inv_rms,
+                         const float* __restrict__ pre, __nv_bfloat16* __restrict__ y,
+                         float* __restrict__ x_scaled, int64_t T, int64_t D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t nchunk = D / 16;
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
+       t += nwarps) {
+    const float inv = inv_rms[t];
+    float pr[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
+    const __nv_bfloat16* xt = x + t * N * D;
+    float* xst = x_scaled ? x_scaled + t * N * D : nullptr;
+    for (int64_t c = lane; c < nchunk; c += 32) {
+      U8 xv[N];
+#pragma unroll
+      for (int n = 0; n < N; ++n) xv[n] = ld_global_32B(xt + n * D + c * 16);
+      float o[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) o[e] = 0.f;
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        float f[16];
+        widen<__nv_bfloat16>(xv[n].a, f);
+        widen<__nv_bfloat16>(xv[n].b, f + 8);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) o[e] = fmaf(f[e], pr[n], o[e]);
+        if (xst) {
+          float* dst = xst + n * D + c * 16;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint4 a = make_uint4(__float_as_uint(f[8 * h] * inv), __float_as_uint(f[8 * h + 1] * inv),
+                                 __float_as_uint(f[8 * h + 2] * inv), __float_as_uint(f[8 * h + 3] * inv));
+            uint4 b = make_uint4(__float_as_uint(f[8 * h + 4] * inv), __float_as_uint(f[8 * h + 5] * inv),
+                                 __float_as_uint(f[8 * h + 6] * inv), __float_as_uint(f[8 * h + 7] * inv));
+            st_global_32B(dst + 8 * h, a, b);
+          }
+        }
+      }
+      st_global_32B(y + t * D + c * 16, narrow<__nv_bfloat16>(o), narrow<__nv_bfloat16>(o + 8));
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -181,7 +230,14 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
                      (a.x_scaled == nullptr || aligned16(a.x_scaled));
     const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;
     dim3 grid((unsigned)(want < cap ? want : cap));
-    if (vec)
+    const bool v16 = std::is_same<E, __nv_bfloat16>::value && D % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.x) & 31) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.y) & 31) == 0 &&
+                     (a.x_scaled == nullptr || (reinterpret_cast<uintptr_t>(a.x_scaled) & 31) == 0);
+    if (v16)
+      pre_apply_bf16x16_kernel<N><<<grid, 256, 0, s>>>((const __nv_bfloat16*)a.x, a.inv_rms, a.pre,
+                                                       (__nv_bfloat16*)a.y, a.x_scaled, T, D);
+    else if (vec)
       pre_apply_kernel<E, N, true><<<grid, 256, 0, s>>>((const E*)a.x, a.inv_rms, a.pre,
                                                         (E*)a.y, a.x_scaled, T, D);
     else
