@@ -231,15 +231,20 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
   }
 }
 
+// One warp per output value: lanes take strided partials, then a fixed-shape tree
+// (warp_sum) -- deterministic for a given number of blocks.
 __global__ void pre_reduce_ab_kernel(const float* __restrict__ partials, int nblk, int HM,
                                      float* __restrict__ grad_alpha,
                                      float* __restrict__ grad_base) {
   const int NP = 3 + HM;
-  for (int i = threadIdx.x; i < NP; i += blockDim.x) {
-    float s = 0.f;
-    for (int b = 0; b < nblk; ++b) s += partials[(int64_t)b * NP + i];
-    if (i < 3) grad_alpha[i] = s;
-    else grad_base[i - 3] = s;
+  const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (w >= NP) return;
+  float acc = 0.f;
+  for (int b = lane; b < nblk; b += 32) acc += partials[(int64_t)b * NP + w];
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    if (w < 3) grad_alpha[w] = acc;
+    else grad_base[w - 3] = acc;
   }
 }
 
@@ -419,7 +424,8 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
                                                use_tc ? nullptr : w.gm, w.coef, w.partials,
                                                g0, g1, gp);
   MHC_LAUNCH_CHECK();
-  pre_reduce_ab_kernel<<<1, 128, 0, s>>>(w.partials, nblk, HM, a.grad_alpha, a.grad_base);
+  pre_reduce_ab_kernel<<<(unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s>>>(w.partials, nblk, HM,
+                                                                       a.grad_alpha, a.grad_base);
   MHC_LAUNCH_CHECK();
   if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));

@@ -470,30 +470,41 @@ __global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi,
 }
 
 // grad_phi[k][n*D + g*128 + c] = sum over the cells of group g (in order) of slot 0,
-// plus slot 1 where a CTA run boundary falls strictly inside the cell.
-__global__ void pre_bwd_gphi_reduce_kernel(const float* __restrict__ part,
-                                           float* __restrict__ grad_phi, int64_t D,
-                                           BwdGeom geo) {
+// plus slot 1 where a CTA run boundary falls strictly inside the cell.  A block of 256
+// outputs lies inside one group (N*HM*GC is a multiple of 256); the group's split flags
+// are computed once per block.
+constexpr int kMaxCellsPerGroup = 4096;
+__global__ void __launch_bounds__(256)
+pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ grad_phi,
+                           int64_t D, BwdGeom geo) {
   using namespace bwdtc;
-  const int64_t G = D / GC;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (g, n, k, c)
-  if (idx >= G * N * HM * GC) return;
-  const int64_t inner = idx % (N * HM * GC);   // (n, k, c) inside a slot
-  const int n = (int)(inner / (HM * GC));
-  const int k = (int)((inner / GC) % HM);
-  const int c = (int)(inner % GC);
-  const int64_t g = idx / (N * HM * GC);
-  float s = 0.f;
-  for (int64_t ci = 0; ci < geo.cpg; ++ci) {
-    const int64_t cell = g * geo.cpg + ci;
-    s += part[(cell * 2) * (N * HM * GC) + inner];
+  constexpr int64_t SLOT = (int64_t)N * HM * GC;
+  static_assert(SLOT % 256 == 0, "a block must not straddle two groups");
+  __shared__ unsigned char split[kMaxCellsPerGroup];
+  const int64_t idx0 = (int64_t)blockIdx.x * blockDim.x;
+  const int64_t g = idx0 / SLOT;
+  auto cell_split = [&](int64_t ci) -> bool {
     const int64_t lo = g * geo.ntiles + ci * geo.subt;
     int64_t hi = lo + geo.subt;
     if (hi > (g + 1) * geo.ntiles) hi = (g + 1) * geo.ntiles;
     // first run boundary items*b/ncta above lo
     int64_t b = lo * geo.ncta / geo.items;
     while (geo.items * b / geo.ncta <= lo) ++b;
-    if (b < geo.ncta && geo.items * b / geo.ncta < hi) s += part[(cell * 2 + 1) * (N * HM * GC) + inner];
+    return b < geo.ncta && geo.items * b / geo.ncta < hi;
+  };
+  const bool table = geo.cpg <= kMaxCellsPerGroup;
+  if (table)
+    for (int64_t ci = threadIdx.x; ci < geo.cpg; ci += blockDim.x) split[ci] = cell_split(ci);
+  __syncthreads();
+  const int64_t inner = idx0 - g * SLOT + threadIdx.x;  // (n, k, c) inside a slot
+  const int n = (int)(inner / (HM * GC));
+  const int k = (int)((inner / GC) % HM);
+  const int c = (int)(inner % GC);
+  float s = 0.f;
+  for (int64_t ci = 0; ci < geo.cpg; ++ci) {
+    const int64_t cell = g * geo.cpg + ci;
+    s += part[(cell * 2) * SLOT + inner];
+    if (table ? split[ci] != 0 : cell_split(ci)) s += part[(cell * 2 + 1) * SLOT + inner];
   }
   grad_phi[(int64_t)k * (N * D) + n * D + g * GC + c] = s;
 }
@@ -504,6 +515,7 @@ __global__ void pre_bwd_gphi_reduce_kernel(const float* __restrict__ part,
 bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
                          const void* gy, const void* gx) {
   return dtype == MHC_BF16 && N == 4 && D % bwdtc::GC == 0 && T > 0 &&
+
          T <= (int64_t)INT32_MAX - 256 && (int64_t)N * D <= INT32_MAX && aligned16(x) &&
          aligned16(gy) && aligned16(gx);
 }
