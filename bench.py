@@ -307,10 +307,12 @@ def main():
     except Exception:
         pass
     clocks = ClockSampler(uuid)
+    clocks.start()
+    # the barrier comes after each rank's sampler is up, right before the timed region:
+    # otherwise a rank that starts early waits for the others inside its first all-reduce
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
     n0 = _C.lib().mhc_kernel_launches()
     clocks.mark_start()
     start.record()

@@ -169,36 +169,40 @@ __device__ __forceinline__ void softmax_rows(const float* l, float* P) {
       P[i * N + j] = expf(l[i * N + j] - m);
       s += P[i * N + j];
     }
+    const float rs = 1.0f / s;
 #pragma unroll
-    for (int j = 0; j < N; ++j) P[i * N + j] = P[i * N + j] / s;
+    for (int j = 0; j < N; ++j) P[i * N + j] *= rs;
   }
 }
 
+// Normalisations divide by (sum + eps) through one reciprocal per row / column, as the
+// reference's own kernels do (`inv_s = 1/(s+eps)` then multiply); rc_out receives the
+// reciprocals when the caller needs them for the backward.
 template <int N>
-__device__ __forceinline__ void col_norm(float* M, float eps, float* cs_out = nullptr) {
+__device__ __forceinline__ void col_norm(float* M, float eps, float* rc_out = nullptr) {
 #pragma unroll
   for (int j = 0; j < N; ++j) {
     float c = 0.f;
 #pragma unroll
     for (int i = 0; i < N; ++i) c += M[i * N + j];
-    c += eps;
-    if (cs_out) cs_out[j] = c;
+    const float rc = 1.0f / (c + eps);
+    if (rc_out) rc_out[j] = rc;
 #pragma unroll
-    for (int i = 0; i < N; ++i) M[i * N + j] = M[i * N + j] / c;
+    for (int i = 0; i < N; ++i) M[i * N + j] *= rc;
   }
 }
 
 template <int N>
-__device__ __forceinline__ void row_norm(float* M, float eps, float* rs_out = nullptr) {
+__device__ __forceinline__ void row_norm(float* M, float eps, float* rr_out = nullptr) {
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     float r = 0.f;
 #pragma unroll
     for (int j = 0; j < N; ++j) r += M[i * N + j];
-    r += eps;
-    if (rs_out) rs_out[i] = r;
+    const float rr = 1.0f / (r + eps);
+    if (rr_out) rr_out[i] = rr;
 #pragma unroll
-    for (int j = 0; j < N; ++j) M[i * N + j] = M[i * N + j] / r;
+    for (int j = 0; j < N; ++j) M[i * N + j] *= rr;
   }
 }
 

@@ -137,14 +137,14 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
 #pragma unroll
     for (int e = 0; e < NN; ++e) g[e] = gcomb[t * NN + e];
     for (int it = sp.iters - 1; it >= 1; --it) {
-      float Q[NN], rs[N], cs[N];
+      float Q[NN], rs[N], cs[N];  // reciprocals of the row / column divisors
 #pragma unroll
       for (int e = 0; e < NN; ++e) Q[e] = hist[((int64_t)(it - 1) * NN + e) * T + t];
-      row_norm<N>(Q, sp.hc_eps, rs);       // Q = M_in / rs
+      row_norm<N>(Q, sp.hc_eps, rs);       // Q = M_in / (rowsum + eps)
       float U[NN];
 #pragma unroll
       for (int e = 0; e < NN; ++e) U[e] = Q[e];
-      col_norm<N>(U, sp.hc_eps, cs);       // U = Q / cs
+      col_norm<N>(U, sp.hc_eps, cs);       // U = Q / (colsum + eps)
       // col-norm VJP: dQ = (g - sum_i g*U) / cs
 #pragma unroll
       for (int j = 0; j < N; ++j) {
@@ -152,7 +152,7 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
 #pragma unroll
         for (int i = 0; i < N; ++i) s += g[i * N + j] * U[i * N + j];
 #pragma unroll
-        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - s) / cs[j];
+        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - s) * cs[j];
       }
       // row-norm VJP: dM = (dQ - sum_j dQ*Q) / rs
 #pragma unroll
@@ -161,7 +161,7 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
 #pragma unroll
         for (int j = 0; j < N; ++j) s += g[i * N + j] * Q[i * N + j];
 #pragma unroll
-        for (int j = 0; j < N; ++j) g[i * N + j] = (g[i * N + j] - s) / rs[i];
+        for (int j = 0; j < N; ++j) g[i * N + j] = (g[i * N + j] - s) * rs[i];
       }
     }
     // iteration 0: U0 = M0 / cs0, M0 = P + eps
@@ -176,7 +176,7 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
 #pragma unroll
         for (int i = 0; i < N; ++i) s += g[i * N + j] * U[i * N + j];
 #pragma unroll
-        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - s) / cs[j];
+        for (int i = 0; i < N; ++i) g[i * N + j] = (g[i * N + j] - s) * cs[j];
       }
     }
     // softmax VJP: dl = P * (dP - sum_j dP*P); clamp passes where min <= l <= max
