@@ -5,8 +5,9 @@
 //                        bf16, so x.phi^T = x.hi^T + x.lo^T in fp32 accumulation
 //                        reproduces the fp32 contraction to ~2^-17 per product.
 // pre_mix_tc_kernel      persistent, one 128-token tile at a time:
-//                          warp 0     TMA producer: x tile [128 x 64] + phi_hl [NP x 64]
-//                                     per K step into an S-stage ring (128B swizzle)
+//                          warp 0     TMA producer: x tile [128 x 64*NB] + phi_hl
+//                                     [NP x 64*NB] per stage into an S-stage ring (NB
+//                                     adjacent 128B-swizzled boxes per stage)
 //                          warp 1     TMEM owner + MMA issuer: tcgen05.mma M=128 N=NP
 //                                     K=16 x4 per stage; accumulation in K segments of
 //                                     KSEG stages, double-buffered in TMEM
@@ -22,21 +23,25 @@
 
 namespace mhc {
 
-template <int N>
+template <int N, int NB>
 struct MixCfg {
   static constexpr int HM = hc_mix(N);
   static constexpr int NP = (2 * HM + 15) / 16 * 16;            // MMA N (hi + lo rows)
   static constexpr int BUFCOL = (NP + 16 + 31) / 32 * 32;       // TMEM columns per buffer
   static constexpr int TMEM_COLS = (2 * BUFCOL <= 32) ? 32 : (2 * BUFCOL <= 64) ? 64
                                    : (2 * BUFCOL <= 128) ? 128 : (2 * BUFCOL <= 256) ? 256 : 512;
-  static constexpr int KC = 64;                                  // K per stage (128 B rows)
+  static constexpr int BOX = 64;                                 // columns per TMA box (128 B)
+  static constexpr int KC = BOX * NB;                            // K per stage: NB adjacent boxes
   // Stages per TMEM segment.  The tensor core's fp32 accumulation loses precision
   // roughly in proportion to the number of chained MMAs; folding every 64 MMAs into
   // fp32 registers keeps x.phi^T within a few 1e-6 of the fp32 contraction at any K.
-  static constexpr int KSEG = 16;
-  static constexpr int A_BYTES = 128 * KC * 2;                   // 16 KB
-  static constexpr int B_BYTES = NP * KC * 2;
-  static constexpr int B_STRIDE = (B_BYTES + 1023) / 1024 * 1024;
+  static constexpr int KSEG = 16 / NB;                           // stages per segment (64 MMAs)
+  static constexpr int A_BOX = 128 * BOX * 2;                   // 16 KB
+  static constexpr int A_BYTES = A_BOX * NB;
+  static constexpr int B_BOX = NP * BOX * 2;
+  static constexpr int B_BOX_STRIDE = (B_BOX + 1023) / 1024 * 1024;
+  static constexpr int B_BYTES = B_BOX * NB;                     // TMA bytes per stage
+  static constexpr int B_STRIDE = B_BOX_STRIDE * NB;
   static constexpr int STAGES = (200 * 1024) / (A_BYTES + B_STRIDE) > 8
                                     ? 8 : (200 * 1024) / (A_BYTES + B_STRIDE);
   static constexpr int SMEM = 1024 /*align slack*/ + STAGES * (A_BYTES + B_STRIDE) + 256;
@@ -60,15 +65,15 @@ __global__ void pre_phi_split_kernel(const float* __restrict__ phi, __nv_bfloat1
   }
 }
 
-template <int N>
-__global__ void __launch_bounds__(MixCfg<N>::THREADS, 1)
+template <int N, int NB>
+__global__ void __launch_bounds__(MixCfg<N, NB>::THREADS, 1)
 pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                   const __grid_constant__ CUtensorMap tm_phi, const float* __restrict__ alpha,
                   const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
                   SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
                   float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
                   float* __restrict__ logits_out) {
-  using C = MixCfg<N>;
+  using C = MixCfg<N, NB>;
   constexpr int HM = C::HM, S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -125,8 +130,14 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
           const uint32_t ph = (it / S) & 1;
           if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
-          tc::tma_load_2d(sA + s * C::A_BYTES, &tm_x, &full[s], kc * C::KC, (int)(tile * 128));
-          tc::tma_load_2d(sB + s * C::B_STRIDE, &tm_phi, &full[s], kc * C::KC, 0);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const int col = kc * C::KC + b * C::BOX;
+            tc::tma_load_2d(sA + s * C::A_BYTES + b * C::A_BOX, &tm_x, &full[s], col,
+                            (int)(tile * 128));
+            tc::tma_load_2d(sB + s * C::B_STRIDE + b * C::B_BOX_STRIDE, &tm_phi, &full[s], col,
+                            0);
+          }
         }
       }
     }
@@ -147,13 +158,18 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
             const int s = it % S;
             if (!tc::mbar_wait(&full[s], (it / S) & 1, abort_flag)) { ok = false; break; }
             tc::tc_fence_after();
-            const uint64_t a0 = tc::smem_desc(tc::smem_u32(sA + s * C::A_BYTES), 16, 1024,
-                                              tc::kSwizzle128);
-            const uint64_t b0 = tc::smem_desc(tc::smem_u32(sB + s * C::B_STRIDE), 16, 1024,
-                                              tc::kSwizzle128);
 #pragma unroll
-            for (int k = 0; k < C::KC / 16; ++k)
-              tc::mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc, (kc != kc0 || k != 0) ? 1u : 0u);
+            for (int b = 0; b < NB; ++b) {
+              const uint64_t a0 = tc::smem_desc(
+                  tc::smem_u32(sA + s * C::A_BYTES + b * C::A_BOX), 16, 1024, tc::kSwizzle128);
+              const uint64_t b0 = tc::smem_desc(
+                  tc::smem_u32(sB + s * C::B_STRIDE + b * C::B_BOX_STRIDE), 16, 1024,
+                  tc::kSwizzle128);
+#pragma unroll
+              for (int k = 0; k < C::BOX / 16; ++k)
+                tc::mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc,
+                             (kc != kc0 || b != 0 || k != 0) ? 1u : 0u);
+            }
             tc::mma_commit(&empty[s]);
           }
           if (!ok) break;
@@ -184,10 +200,12 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
           ok = false;
           break;
         }
-        const uint4* row = reinterpret_cast<const uint4*>(sA + s * C::A_BYTES + r * 128);
         float csq = 0.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int bc = 0; bc < 8 * NB; ++bc) {
+          const uint4* row =
+              reinterpret_cast<const uint4*>(sA + s * C::A_BYTES + (bc >> 3) * C::A_BOX + r * 128);
+          const int c = bc & 7;
           // visit the row's 16-byte chunks in swizzled order: the 8 rows of an atom then
           // hit 8 different bank groups (a plain c order is a 32-way bank conflict)
           float f[8];
@@ -261,9 +279,9 @@ size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D) {
   return align_up((size_t)NP * N * D * 2);
 }
 
-template <int N>
-static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
-  using C = MixCfg<N>;
+template <int N, int NB>
+static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
+  using C = MixCfg<N, NB>;
   const int64_t T = a.T, HC = (int64_t)N * a.D;
   __nv_bfloat16* phi_hl = (__nv_bfloat16*)a.workspace;
   {
@@ -273,27 +291,36 @@ static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
     MHC_LAUNCH_CHECK();
   }
   CUtensorMap tx, tp;
-  int st = make_tmap_2d(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, T, HC * 2, C::KC, 128,
+  int st = make_tmap_2d(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, T, HC * 2, C::BOX, 128,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
-  st = make_tmap_2d(&tp, phi_hl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, C::NP, HC * 2, C::KC,
+  st = make_tmap_2d(&tp, phi_hl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, C::NP, HC * 2, C::BOX,
                     C::NP, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_tc_kernel<N>,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_tc_kernel<N, NB>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev] = true;
   }
   const int64_t ntiles = cdiv(T, 128);
   const int grid = (int)std::min<int64_t>(ntiles, sm_count());
-  pre_mix_tc_kernel<N><<<grid, C::THREADS, C::SMEM, s>>>(
+  pre_mix_tc_kernel<N, NB><<<grid, C::THREADS, C::SMEM, s>>>(
       tx, tp, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
       a.comb_frag, a.h_res_logits);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
+}
+
+// Two adjacent 64-column boxes per stage: each DRAM row visit then fetches 256 B of a
+// token row instead of 128 B (measured: the mix pass 0.36 -> 0.31 ms at T=32768, D=7168;
+// four boxes gain nothing more).  N=8's larger phi operand keeps one box per stage so the
+// ring still holds several stages.
+template <int N>
+static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
+  return pre_fwd_tc_nb<N, (N <= 4 ? 2 : 1)>(a, s);
 }
 
 // Runs the tensor-core mix (+ fused small stage); the caller then runs pre_apply.
