@@ -39,12 +39,13 @@ WORKLOAD = "pre_clamp_sinkhorn fwd(need_backward)+bwd and post fwd+bwd, T=32768 
 
 
 # ----------------------------------------------------------------------------- helpers
-def algorithmic_bytes(T, N, D, e=2):
+def algorithmic_bytes(T, N, D, e=2, x_scaled=True):
     """Compulsory HBM bytes per op (each input read once, each output written once)."""
     HM, HC = N * (N + 2), N * D
+    xs = HC * 4 if x_scaled else 0
     post_fwd = T * (2 * N * D * e + D * e + N * N * 4 + N * 4)
     post_bwd = T * (3 * N * D * e + 2 * D * e + 2 * (N * N * 4 + N * 4))
-    pre_fwd = T * (N * D * e + D * e + N * 4 + N * N * 4 + 4 + HC * 4 + HM * 4 + N * N * 4
+    pre_fwd = T * (N * D * e + D * e + N * 4 + N * N * 4 + 4 + xs + HM * 4 + N * N * 4
                    + N * 4) + HM * HC * 4
     pre_bwd = T * (2 * N * D * e + D * e + N * 4 + N * N * 4 + 4 + HM * 4 + N * 4) \
         + 2 * HM * HC * 4 + (3 + HM) * 4
@@ -166,12 +167,12 @@ def make_inputs(T, N, D, seed, dev):
 KW = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
 
 
-def run_step(M, inp, world, ev=None):
+def run_step(M, inp, world, ev=None, x_scaled=True):
     """The four operators (+ the gradient all-reduce). Returns the small results."""
     if ev is not None:
         ev[0].record()
     out = M.mhc_pre_clamp_sinkhorn(inp["x_pre"], inp["phi"], inp["alpha"], inp["base"],
-                                   need_backward=True, **KW)
+                                   need_backward=True, materialize_x_scaled=x_scaled, **KW)
     if ev is not None:
         ev[1].record()
     y = M.mhc_post(inp["x_post"], inp["h_res"], inp["h_out"], inp["h_post"])
@@ -273,6 +274,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_TOK, help="tokens per GPU")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-x-scaled", action="store_true",
+                    help="opt-in variant: the forward does not write the fp32 x_scaled "
+                         "(not the reference contract; the default keeps it)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -291,11 +295,12 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
 
     T, N, D = args.tokens, N_HC, D_HID
+    xs_on = not args.skip_x_scaled
     inp = make_inputs(T, N, D, seed=1000 + rank, dev=dev)
     torch.cuda.synchronize()
 
     for _ in range(max(args.warmup, 0)):
-        run_step(M, inp, world)
+        run_step(M, inp, world, x_scaled=xs_on)
     torch.cuda.synchronize()
 
     K = args.steps
@@ -317,7 +322,7 @@ def main():
     clocks.mark_start()
     start.record()
     for k in range(K):
-        run_step(M, inp, world, evs[k])
+        run_step(M, inp, world, evs[k], x_scaled=xs_on)
     stop.record()
     torch.cuda.synchronize()
     clocks.mark_stop()
@@ -336,7 +341,7 @@ def main():
     names = ["pre_fwd", "post_fwd", "post_bwd", "pre_bwd", "allreduce"]
     op_ms = {n: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K))
              for i, n in enumerate(names)}
-    ab = algorithmic_bytes(T, N, D)
+    ab = algorithmic_bytes(T, N, D, x_scaled=xs_on)
     peak, peak_kind = hbm_peak()
     step_bytes = sum(ab.values())
     ops = {n: {"ms": op_ms[n], "GB/s": ab[n] / (op_ms[n] / 1e3) / 1e9,
@@ -367,7 +372,7 @@ def main():
         for _ in range(args.e2e_steps):
             for k in big:
                 inp[k].copy_(host[k], non_blocking=True)
-            out, y, pg, grads = run_step(M, inp, world)
+            out, y, pg, grads = run_step(M, inp, world, x_scaled=xs_on)
             res = [grads[1], grads[2], grads[3], pg[1], pg[3], out["post_out"], out["comb_frag"]]
             cpu_res = [r.to("cpu", non_blocking=False) for r in res]
             d2h = sum(r.numel() * r.element_size() for r in cpu_res)
@@ -400,7 +405,10 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "global_tokens": world * T,
                        "N": N, "D": D, "hcMix": N * (N + 2), "clamp": [-10.0, 10.0],
-                       "iter_times": 20, "parallelism": f"dp{world} token-sharded"
+                       "iter_times": 20,
+                       "x_scaled": "written (reference contract)" if xs_on
+                       else "skipped (opt-in materialize_x_scaled=False)",
+                       "parallelism": f"dp{world} token-sharded"
                        + (", packed grad_phi NCCL all-reduce" if world > 1 else ""),
                        "l2": "no flush: every step streams ~21 GB, x alone is 1.88 GB > 126 MB L2"},
             "hbm_frac_step": step_bytes / (ms_step / 1e3) / 1e9 / peak,

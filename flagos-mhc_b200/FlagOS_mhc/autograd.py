@@ -38,10 +38,12 @@ class MhcPreClampSinkhornFn(torch.autograd.Function):
     (x, phi, alpha, base, inv_rms, x_scaled, mixes, h_res_logits, pre)."""
 
     @staticmethod
-    def forward(ctx, x, phi, alpha, base, norm_eps, hc_eps, clamp_min, clamp_max, iter_times):
+    def forward(ctx, x, phi, alpha, base, norm_eps, hc_eps, clamp_min, clamp_max, iter_times,
+                materialize_x_scaled=True):
         out = mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=norm_eps, hc_eps=hc_eps,
                                      clamp_min=clamp_min, clamp_max=clamp_max,
-                                     iter_times=iter_times, need_backward=True)
+                                     iter_times=iter_times, need_backward=True,
+                                     materialize_x_scaled=materialize_x_scaled)
         ctx.save_for_backward(x, phi, alpha, base, out["inv_rms"], out["x_scaled"],
                               out["mixes"], out["h_res_logits"], out["pre"])
         ctx.norm_eps = norm_eps
@@ -67,11 +69,14 @@ class MhcPreClampSinkhornFn(torch.autograd.Function):
             norm_eps=ctx.norm_eps, hc_eps=ctx.hc_eps, clamp_min=ctx.clamp_min,
             clamp_max=ctx.clamp_max, iter_times=ctx.iter_times)
         return (gx, gphi.to(phi.dtype), galpha.to(alpha.dtype), gbase.to(base.dtype),
-                None, None, None, None, None)
+                None, None, None, None, None, None)
 
 
 def mhc_pre_clamp_sinkhorn_fn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clamp_min=0.0,
-                              clamp_max=0.0, iter_times=20):
-    """Autograd-aware mhc_pre_clamp_sinkhorn. Returns (y, post_out, comb_frag)."""
+                              clamp_max=0.0, iter_times=20, materialize_x_scaled=True):
+    """Autograd-aware mhc_pre_clamp_sinkhorn. Returns (y, post_out, comb_frag).
+
+    ``materialize_x_scaled=False`` (opt-in, not in the reference API) saves an empty
+    x_scaled instead of the fp32 copy of x; the backward does not need it."""
     return MhcPreClampSinkhornFn.apply(x, phi, alpha, base, norm_eps, hc_eps, clamp_min,
-                                       clamp_max, iter_times)
+                                       clamp_max, iter_times, materialize_x_scaled)

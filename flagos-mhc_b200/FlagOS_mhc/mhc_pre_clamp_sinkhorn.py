@@ -34,7 +34,8 @@ def _check_params(N, D, phi, alpha, base):
 
 
 def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clamp_min=0.0,
-                           clamp_max=0.0, iter_times=20, need_backward=False):
+                           clamp_max=0.0, iter_times=20, need_backward=False,
+                           materialize_x_scaled=True):
     """Fused RMSNorm + x.phi^T + heads + clamp + softmax + Sinkhorn + y.
 
     Reference: ``mhc_pre_clamp_sinkhorn`` (src/mhc_pre_clamp_sinkhorn.py:857-971).
@@ -44,6 +45,10 @@ def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clam
     pre-clamp) and ``pre`` (T,N), all fp32.  The clamp is applied iff
     ``clamp_min != 0 or clamp_max != 0`` and the Sinkhorn runs ``iter_times``
     iterations in both modes.
+
+    ``materialize_x_scaled=False`` (an addition to the reference API, opt-in) skips
+    writing the fp32 ``x_scaled`` (4*N*D bytes per token, the largest output) and
+    returns an empty tensor in its place; the backward of this package never reads it.
     """
     xf, y_shape = _flatten(x)
     T, N, D = xf.shape
@@ -60,7 +65,7 @@ def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clam
     inv_rms = torch.empty(T, **f32)
     mixes = torch.empty(T, hc_mix, **f32)
     pre = torch.empty(T, N, **f32)
-    x_scaled = torch.empty(T, hc_d, **f32) if need_backward else None
+    x_scaled = torch.empty(T, hc_d, **f32) if (need_backward and materialize_x_scaled) else None
     h_res_logits = torch.empty(T, N, N, **f32) if need_backward else None
     L = _C.lib()
     code = _C.dtype_code(xf.dtype)
@@ -76,6 +81,8 @@ def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clam
     _C.check(st, "mhc_pre_clamp_sinkhorn")
     result = {"y": y.reshape(y_shape), "post_out": post_out, "comb_frag": comb_frag}
     if need_backward:
+        if x_scaled is None:
+            x_scaled = torch.empty(0, hc_d, **f32)
         result.update(inv_rms=inv_rms, x_scaled=x_scaled, mixes=mixes,
                       h_res_logits=h_res_logits, pre=pre)
     return result

@@ -72,7 +72,7 @@ constexpr int TMEM_COLS = 512;
 }  // namespace bwdtc
 
 struct BwdTcMaps {
-  CUtensorMap x, g0, g1, gp, p0, p1, gx;
+  CUtensorMap x, g0, g1, gp, p0, p1;
 };
 
 // A cell is `subt` consecutive token tiles of one column group; subt never exceeds the
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(bwdtc::THREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, __nv_bfloat16* __restrict__ gx,
-                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
+                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo, bool gx32,
                   long long* __restrict__ wdbg) {
   long long wcyc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const long long tstart = clock64();
@@ -105,10 +105,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
   uint64_t* xfull = bar;             // [XS] x tile landed
-  uint64_t* xempty = bar + XS;       // [XS] its grad_x store has read the stage
-  uint64_t* xmma = bar + 2 * XS;     // [XS] the grad_phi MMAs are done reading the x tile
-  uint64_t* ostage = bar + 3 * XS;   // [XS] all epilogue warps wrote grad_x into the stage
-  uint64_t* gfull = bar + 4 * XS;
+  uint64_t* xempty = bar + XS;       // [XS] epilogue warps and grad_phi MMAs read the tile
+  uint64_t* gfull = bar + 2 * XS;
   uint64_t* gempty = gfull + 1;
   uint64_t* pfull = gfull + 2;
   uint64_t* pempty = gfull + 3;
@@ -128,9 +126,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   if (threadIdx.x == 0) {
     for (int b = 0; b < XS; ++b) {
       tc::mbar_init(&xfull[b], 1);
-      tc::mbar_init(&xempty[b], 1);  // the thread that TMA-stores the stage's grad_x
-      tc::mbar_init(&xmma[b], 1);
-      tc::mbar_init(&ostage[b], EPI_WARPS);
+      tc::mbar_init(&xempty[b], EPI_WARPS + 1);  // 16 epilogue warps + 1 MMA commit
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&d1full[b], 1);
@@ -151,7 +147,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     tc::prefetch_tmap(&maps.g0);
     tc::prefetch_tmap(&maps.gp);
     tc::prefetch_tmap(&maps.p0);
-    tc::prefetch_tmap(&maps.gx);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -268,7 +263,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             const uint64_t bg = tc::smem_desc(sgp + kk * 2048, GP_BYTES, 1024, tc::kSwizzle128);
             tc::mma_bf16(d2, ax, bg, id_gphi, (seg_start && kk == 0) ? 0u : 1u);
           }
-          tc::mma_commit(&xmma[s]);
+          tc::mma_commit(&xempty[s]);
           if (n == N - 1) {
             tc::mma_commit(gempty);
             if (seg_end_of(item, i)) {
@@ -359,39 +354,37 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 #ifdef MHC_PROFILE_WAITS
         long long _p2 = clock64();
 #endif
-        uint4 ov[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float xf[8], gf[8], o[8];
-          widen<__nv_bfloat16>(xv[j], xf);
-          widen<__nv_bfloat16>(gyv[j], gf);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);
-            o[u] = fmaf(gf[u], pr[n], rr);
-          }
-          ov[j] = narrow<__nv_bfloat16>(o);
-        }
-        // grad_x goes back into the x stage (same swizzled bytes this thread just read)
-        // once the grad_phi MMAs are done with it; then one thread TMA-stores the tile
-        if (!__all_sync(0xffffffffu, TW(6, tc::mbar_wait(&xmma[s], xph, abort_flag)))) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(xrow + ((((h & 1) * 4 + j) ^ (r & 7)) << 4)) = ov[j];
-        tc::fence_proxy_async();        // generic smem writes -> async-proxy (TMA) reads
+        // the stage is free once every epilogue warp has read its x and the grad_phi
+        // MMAs are done (their commit is the barrier's last arrival); grad_x goes
+        // straight from registers to global memory, 64 contiguous bytes per thread
+        tc::fence_proxy_async();        // generic smem reads before the TMA refill
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&ostage[s]);
-        if (warp == 2 && lane == 0) {
-          if (!tc::mbar_wait(&ostage[s], xph, abort_flag)) { ok = false; break; }
-          const int col = (int)(n * D + d0);
-          tc::tma_store_2d(&maps.gx, stage, col, (int)(i * 128));
-          tc::tma_store_2d(&maps.gx, stage + X_BYTES / 2, col + 64, (int)(i * 128));
-          tc::bulk_commit_group();
-          tc::bulk_wait_read<0>();       // the store has read the stage: refill it
-          tc::mbar_arrive(&xempty[s]);
+        if (lane == 0) tc::mbar_arrive(&xempty[s]);
+        __nv_bfloat16* dst = gx + t * (N * D) + n * D + d0 + h * 32;
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+          uint4 ov[2];
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * jp + jj;
+            float xf[8], gf[8], o[8];
+            widen<__nv_bfloat16>(xv[j], xf);
+            widen<__nv_bfloat16>(gyv[j], gf);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);
+              o[u] = fmaf(gf[u], pr[n], rr);
+            }
+            ov[jj] = narrow<__nv_bfloat16>(o);
+          }
+          if (live) {
+            if (gx32) {
+              st_global_32B(dst + 16 * jp, ov[0], ov[1]);
+            } else {
+              st_stream(dst + 16 * jp, ov[0]);
+              st_stream(dst + 16 * jp + 8, ov[1]);
+            }
+          }
         }
 #ifdef MHC_PROFILE_WAITS
         wcyc[5] += clock64() - _p2;
@@ -421,7 +414,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       }
     }
   }
-  if (warp == 2 && lane == 0) tc::bulk_wait_all<0>();  // grad_x stores have landed
   if (*abort_flag && threadIdx.x == 0) flag_timeout();
 #ifdef MHC_PROFILE_WAITS
   // row per CTA: [total, producer x4, mma x4, epilogue warp 2 x4]
@@ -591,9 +583,6 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
     return st;
   if ((st = make_tmap_2d(&m.p1, w.p1, bf, 2, 16, HC, 32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B)))
     return st;
-  if ((st = make_tmap_2d(&m.gx, a.grad_x, bf, 2, HC, T, HC * 2, 64, 128,
-                         CU_TENSOR_MAP_SWIZZLE_128B)))
-    return st;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -605,6 +594,7 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
   pre_bwd_tc_kernel<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
                                                     (__nv_bfloat16*)a.grad_x, w.part, T, D, geo,
+                                                    (reinterpret_cast<uintptr_t>(a.grad_x) & 31) == 0,
 #ifdef MHC_PROFILE_WAITS
                                                     getenv("MHC_WAIT_DBG")
                                                         ? (long long*)strtoull(getenv("MHC_WAIT_DBG"), nullptr, 10)

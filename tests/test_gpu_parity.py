@@ -290,3 +290,28 @@ def test_pre_bwd_full_grad_phi_vs_oracle():
     for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
         assert rel_err(a, b) <= TOL_FP32, name
     assert rel_err(got[0], want[0]) <= TOL_BF16
+
+
+def test_pre_skip_x_scaled_opt_in():
+    """materialize_x_scaled=False: same outputs and gradients, no fp32 copy of x."""
+    T, N, D = 300, 4, 256
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=21)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    a = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True)
+    b = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True,
+                                 materialize_x_scaled=False)
+    assert b["x_scaled"].numel() == 0
+    for k in ("y", "post_out", "comb_frag", "mixes", "pre", "inv_rms", "h_res_logits"):
+        assert torch.equal(a[k], b[k]), k
+    ga = M.mhc_pre_clamp_sinkhorn_backward(d[0], d[1], d[2], d[3], a["inv_rms"], a["x_scaled"],
+                                           a["mixes"], a["h_res_logits"], a["pre"], d[4], d[5],
+                                           d[6])
+    gb = M.mhc_pre_clamp_sinkhorn_backward(d[0], d[1], d[2], d[3], b["inv_rms"], b["x_scaled"],
+                                           b["mixes"], b["h_res_logits"], b["pre"], d[4], d[5],
+                                           d[6])
+    for u, v in zip(ga, gb):
+        assert torch.equal(u, v)
+    xd = d[0].clone().requires_grad_(True)
+    y, post, comb = M.mhc_pre_clamp_sinkhorn_fn(xd, d[1], d[2], d[3], materialize_x_scaled=False)
+    (y.float().sum() + comb.sum()).backward()
+    assert xd.grad is not None and torch.isfinite(xd.grad.float()).all()
