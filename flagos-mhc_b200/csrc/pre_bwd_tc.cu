@@ -326,43 +326,40 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
           break;
         }
         tc::tc_fence_after();
-        float acc[32];
-        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 32;
-#ifdef MHC_PROFILE_WAITS
-        long long _p0 = clock64();
-#endif
-        tc::tmem_ld16(ta, acc);
-        tc::tmem_ld16(ta + 16, acc + 16);
-        tc::tmem_ld_wait();
-#ifdef MHC_PROFILE_WAITS
-        wcyc[3] += clock64() - _p0;
-#endif
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&d1empty[e]);
         if (!__all_sync(0xffffffffu, TW(1, tc::mbar_wait(&xfull[s], xph, abort_flag)))) {
           ok = false;
           break;
         }
         // x row r, columns [32h, 32h+32): box h/2, 16-byte chunks 4(h%2)..+3 (swizzled)
-        uint8_t* stage = sm + OFF_X + s * X_BYTES;
-        uint8_t* xrow = stage + (h >> 1) * (X_BYTES / 2) + r * 128;
+        const uint8_t* xrow = sm + OFF_X + s * X_BYTES + (h >> 1) * (X_BYTES / 2) + r * 128;
         uint4 xv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           xv[j] = *reinterpret_cast<const uint4*>(xrow + ((((h & 1) * 4 + j) ^ (r & 7)) << 4));
-#ifdef MHC_PROFILE_WAITS
-        long long _p2 = clock64();
-#endif
         // the stage is free once every epilogue warp has read its x and the grad_phi
-        // MMAs are done (their commit is the barrier's last arrival); grad_x goes
-        // straight from registers to global memory, 64 contiguous bytes per thread
+        // MMAs are done (their commit is the barrier's last arrival)
         tc::fence_proxy_async();        // generic smem reads before the TMA refill
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&xempty[s]);
+#ifdef MHC_PROFILE_WAITS
+        long long _p2 = clock64();
+#endif
+        // gxs in two halves of 16 columns (keeps the live registers under the 96 that
+        // 18 warps per CTA allow); grad_x goes straight from registers to global memory,
+        // 64 contiguous bytes per thread
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 32;
         __nv_bfloat16* dst = gx + t * (N * D) + n * D + d0 + h * 32;
+        const float prn = pr[n];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
+          float acc[16];
+          tc::tmem_ld16(ta + 16 * jp, acc);
+          tc::tmem_ld_wait();
+          if (jp == 1) {
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&d1empty[e]);
+          }
           uint4 ov[2];
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
@@ -372,8 +369,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             widen<__nv_bfloat16>(gyv[j], gf);
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-              const float rr = fmaf(inv, acc[8 * j + u], -cf * xf[u]);
-              o[u] = fmaf(gf[u], pr[n], rr);
+              const float rr = fmaf(inv, acc[8 * jj + u], -cf * xf[u]);
+              o[u] = fmaf(gf[u], prn, rr);
             }
             ov[jj] = narrow<__nv_bfloat16>(o);
           }
@@ -389,6 +386,11 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 #ifdef MHC_PROFILE_WAITS
         wcyc[5] += clock64() - _p2;
 #endif
+        if (n == 0 && item + 1 < it1) {
+          // pull the next item's grad_y row segment into L2 while this item runs
+          const int64_t gn = (item + 1) / ntiles, tn = ((item + 1) - gn * ntiles) * 128 + r;
+          if (tn < T) prefetch_l2(gy + tn * D + gn * GC + h * 32);
+        }
       }
       if (!ok) break;
       if (seg_end_of(item, i)) {
