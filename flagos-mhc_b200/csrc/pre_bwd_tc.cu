@@ -350,6 +350,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 32;
         __nv_bfloat16* dst = gx + t * (N * D) + n * D + d0 + h * 32;
         const float prn = pr[n];
+        const float2 pr2 = make_float2(prn, prn), inv2 = make_float2(inv, inv),
+                     ncf2 = make_float2(-cf, -cf);
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
           float acc[16];
@@ -367,10 +369,14 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             float xf[8], gf[8], o[8];
             widen<__nv_bfloat16>(xv[j], xf);
             widen<__nv_bfloat16>(gyv[j], gf);
+            // packed fp32 pairs (each lane rounds exactly like fmaf / a plain multiply)
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float rr = fmaf(inv, acc[8 * jj + u], -cf * xf[u]);
-              o[u] = fmaf(gf[u], prn, rr);
+            for (int u = 0; u < 8; u += 2) {
+              const float2 cx = __fmul2_rn(ncf2, make_float2(xf[u], xf[u + 1]));
+              const float2 rr = __ffma2_rn(inv2, make_float2(acc[8 * jj + u], acc[8 * jj + u + 1]), cx);
+              const float2 oo = __ffma2_rn(make_float2(gf[u], gf[u + 1]), pr2, rr);
+              o[u] = oo.x;
+              o[u + 1] = oo.y;
             }
             ov[jj] = narrow<__nv_bfloat16>(o);
           }
