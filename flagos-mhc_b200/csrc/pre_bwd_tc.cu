@@ -86,11 +86,31 @@ struct BwdGeom {
   int ncta;
 };
 
-__host__ __device__ inline int64_t cell_of(int64_t item, int64_t ntiles, int64_t subt,
-                                           int64_t cpg) {
-  const int64_t g = item / ntiles, i = item - g * ntiles;
-  return g * cpg + i / subt;
-}
+// Walks a CTA's items in order with counters only (no 64-bit division on the issue
+// paths): column group g, token tile i in the group, position of i in its grad_phi
+// cell, and whether the item starts / ends the CTA's segment of that cell.
+struct ItemCursor {
+  int64_t item, it0, it1, g;
+  int i, isub, ntiles, subt;
+  bool seg_start, seg_end;
+  __device__ void flags() {
+    seg_start = item == it0 || isub == 0;
+    seg_end = item == it1 - 1 || isub == subt - 1 || i == ntiles - 1;
+  }
+  __device__ void init(int64_t a, int64_t b, int64_t nt, int64_t st) {
+    item = a; it0 = a; it1 = b; ntiles = (int)nt; subt = (int)st;
+    g = a / nt;
+    i = (int)(a - g * nt);
+    isub = i % subt;
+    flags();
+  }
+  __device__ void next() {
+    ++item;
+    if (++i == ntiles) { i = 0; isub = 0; ++g; }
+    else if (++isub == subt) isub = 0;
+    flags();
+  }
+};
 
 __global__ void __launch_bounds__(bwdtc::THREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
@@ -106,8 +126,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   uint64_t* bar = (uint64_t*)(sm + OFF_BAR);
   uint64_t* xfull = bar;             // [XS] x tile landed
   uint64_t* xempty = bar + XS;       // [XS] epilogue warps and grad_phi MMAs read the tile
-  uint64_t* gfull = bar + 2 * XS;
-  uint64_t* gempty = gfull + 1;
+  uint64_t* gfull = bar + 2 * XS;    // G0/G1 (gxs operand) of an item landed
+  uint64_t* gempty = gfull + 1;      // the item's gxs MMAs are done with G0/G1
   uint64_t* pfull = gfull + 2;
   uint64_t* pempty = gfull + 3;
   uint64_t* d1full = gfull + 4;      // [2]
@@ -115,7 +135,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   uint64_t* d2full = gfull + 8;
   uint64_t* d2empty = gfull + 9;
   uint64_t* tdone = gfull + 10;
-  uint32_t* tmem_slot = (uint32_t*)(gfull + 11);
+  uint64_t* gpfull = gfull + 11;     // GP (grad_phi operand) of an item landed
+  uint64_t* gpempty = gfull + 12;    // the item's grad_phi MMAs are done with GP
+  uint32_t* tmem_slot = (uint32_t*)(gfull + 13);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,6 +156,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     }
     tc::mbar_init(gfull, 1);
     tc::mbar_init(gempty, 1);
+    tc::mbar_init(gpfull, 1);
+    tc::mbar_init(gpempty, 1);
     tc::mbar_init(pfull, 1);
     tc::mbar_init(pempty, 1);
     tc::mbar_init(d2full, 1);
@@ -159,20 +183,18 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 
   // segment = the part of one cell this CTA owns
   const int64_t subt = geo.subt;
-  auto seg_start_of = [&](int64_t item, int64_t i) { return item == it0 || i % subt == 0; };
-  auto seg_end_of = [&](int64_t item, int64_t i) {
-    return item == it1 - 1 || (i + 1) % subt == 0 || i == ntiles - 1;
-  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t xi = 0, gi = 0, seg = 0;
       bool ok = true;
-      for (int64_t item = it0; item < it1 && ok; ++item) {
-        const int64_t g = item / ntiles, i = item - g * ntiles;
-        const int d0 = (int)(g * GC);
-        if (seg_start_of(item, i)) {
+      ItemCursor cur;
+      cur.init(it0, it1, ntiles, subt);
+      for (; cur.item < it1 && ok; cur.next()) {
+        const int i = cur.i;
+        const int d0 = (int)(cur.g * GC);
+        if (cur.seg_start) {
           if (!TW(0, tc::mbar_wait(pempty, (seg & 1) ^ 1, abort_flag))) break;
           tc::mbar_arrive_expect_tx(pfull, N * (P0_BYTES + P1_BYTES));
           for (int n = 0; n < N; ++n) {
@@ -189,16 +211,19 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
           tc::tma_load_2d(dst, &maps.x, &xfull[s], col, (int)(i * 128));
           tc::tma_load_2d(dst + X_BYTES / 2, &maps.x, &xfull[s], col + 64, (int)(i * 128));
           if (n == 0) {
-            // the item's G operands (single buffer) once the previous item's MMAs are done
+            // the item's G operands (single buffers): G0/G1 once the previous item's
+            // gxs MMAs are done, GP once its grad_phi MMAs are done (one step later)
             if (!TW(1, tc::mbar_wait(gempty, (gi & 1) ^ 1, abort_flag))) { ok = false; break; }
-            tc::mbar_arrive_expect_tx(gfull, G0_BYTES + G1_BYTES + GP_BYTES);
+            tc::mbar_arrive_expect_tx(gfull, G0_BYTES + G1_BYTES);
             tc::tma_load_2d(sm + OFF_G0, &maps.g0, gfull, 0, (int)(i * 128));
             tc::tma_load_2d(sm + OFF_G1, &maps.g1, gfull, 0, (int)(i * 128));
-            tc::tma_load_2d(sm + OFF_GP, &maps.gp, gfull, 0, (int)(i * 128));
+            if (!TW(1, tc::mbar_wait(gpempty, (gi & 1) ^ 1, abort_flag))) { ok = false; break; }
+            tc::mbar_arrive_expect_tx(gpfull, GP_BYTES);
+            tc::tma_load_2d(sm + OFF_GP, &maps.gp, gpfull, 0, (int)(i * 128));
             ++gi;
           }
         }
-        if (seg_end_of(item, i)) ++seg;
+        if (cur.seg_end) ++seg;
       }
     }
   } else if (warp == 1) {
@@ -209,78 +234,88 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     if (lane == 0) {
       constexpr uint32_t id_gxs = tc::idesc_bf16(128, 128, false, false);
       constexpr uint32_t id_gphi = tc::idesc_bf16(128, 64, true, true);
+      // step = (item, n); A runs one step ahead of B (the grad_phi step)
+      struct StepPos {
+        ItemCursor c;
+        int n, s;          // sub-chunk, x stage
+        uint32_t gi, xph;  // item index in the run, x stage phase
+        __device__ void next() {
+          if (++s == XS) { s = 0; xph ^= 1; }
+          if (++n == N) { n = 0; ++gi; c.next(); }
+        }
+      };
+      StepPos A, B;
+      A.c.init(it0, it1, ntiles, subt);
+      A.n = 0; A.s = 0; A.gi = 0; A.xph = 0;
+      B = A;
       const int64_t nsteps = (it1 - it0) * N;
       uint32_t seg_a = 0, seg_b = 0;
+      const uint32_t sg0 = tc::smem_u32(sm + OFF_G0), sg1 = tc::smem_u32(sm + OFF_G1);
+      const uint32_t sp0 = tc::smem_u32(sm + OFF_P0), sp1 = tc::smem_u32(sm + OFF_P1);
+      const uint32_t sx0 = tc::smem_u32(sm + OFF_X), sgp = tc::smem_u32(sm + OFF_GP);
       bool ok = true;
+      auto issue_gxs = [&](int64_t st) -> bool {
+        // ---- gxs of step st (position A)
+        const int n = A.n;
+        const int e = (int)(st & 1);
+        if (n == 0) {
+          if (A.c.seg_start && !TW(0, tc::mbar_wait(pfull, seg_a & 1, abort_flag))) return false;
+          if (!TW(0, tc::mbar_wait(gfull, A.gi & 1, abort_flag))) return false;
+        }
+        if (!TW(1, tc::mbar_wait(&d1empty[e], ((uint32_t)(st >> 1) & 1) ^ 1, abort_flag))) return false;
+        tc::tc_fence_after();
+        const uint32_t d1 = tmem + 256 + e * 128;
+        const uint64_t a0 = tc::smem_desc(sg0, 16, 1024, tc::kSwizzle128);
+        const uint64_t b0 = tc::smem_desc(sp0 + n * P0_BYTES, 16, 1024, tc::kSwizzle128);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc::mma_bf16(d1, a0 + 2 * k, b0 + 2 * k, id_gxs, k != 0);
+        tc::mma_bf16(d1, tc::smem_desc(sg1, 16, 256, tc::kSwizzle32),
+                     tc::smem_desc(sp1 + n * P1_BYTES, 16, 256, tc::kSwizzle32), id_gxs, 1);
+        tc::mma_commit(&d1full[e]);
+        if (n == N - 1) tc::mma_commit(gempty);  // last gxs use of this item's G0/G1
+        if (n == N - 1 && A.c.seg_end) {
+          tc::mma_commit(pempty);  // last use of this segment's P
+          ++seg_a;
+        }
+        A.next();
+        return true;
+      };
+      auto issue_gphi = [&]() -> bool {
+        // ---- grad_phi of the step at position B: D2[n] (+)= x_tile^T * Gp
+        const int n = B.n, s = B.s;
+        const bool seg_start = B.c.seg_start;
+        if (n == 0 && seg_start && !TW(2, tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag))) return false;
+        if (n == 0 && !TW(0, tc::mbar_wait(gpfull, B.gi & 1, abort_flag))) return false;
+        if (!TW(3, tc::mbar_wait(&xfull[s], B.xph, abort_flag))) return false;
+        tc::tc_fence_after();
+        const uint32_t d2 = tmem + n * 64;
+        const uint32_t sx = sx0 + s * X_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ax = tc::smem_desc(sx + kk * 2048, X_BYTES / 2, 1024, tc::kSwizzle128);
+          const uint64_t bg = tc::smem_desc(sgp + kk * 2048, GP_BYTES, 1024, tc::kSwizzle128);
+          tc::mma_bf16(d2, ax, bg, id_gphi, (seg_start && kk == 0) ? 0u : 1u);
+        }
+        tc::mma_commit(&xempty[s]);
+        if (n == N - 1) {
+          tc::mma_commit(gpempty);
+          if (B.c.seg_end) {
+            tc::mma_commit(d2full);
+            ++seg_b;
+          }
+        }
+        B.next();
+        return true;
+      };
       for (int64_t st = 0; st <= nsteps && ok; ++st) {
-        auto issue_gxs = [&](int64_t st) -> bool {
-          // ---- gxs of step st
-          const int64_t item = it0 + st / N, i = item % ntiles;
-          const int n = (int)(st % N);
-          const uint32_t gi = (uint32_t)(item - it0);
-          const int e = (int)(st & 1);
-          if (n == 0) {
-            if (seg_start_of(item, i) && !TW(0, tc::mbar_wait(pfull, seg_a & 1, abort_flag))) return false;
-            if (!TW(0, tc::mbar_wait(gfull, gi & 1, abort_flag))) return false;
-          }
-          if (!TW(1, tc::mbar_wait(&d1empty[e], ((st >> 1) & 1) ^ 1, abort_flag))) return false;
-          tc::tc_fence_after();
-          const uint32_t d1 = tmem + 256 + e * 128;
-          const uint64_t a0 = tc::smem_desc(tc::smem_u32(sm + OFF_G0), 16, 1024,
-                                            tc::kSwizzle128);
-          const uint64_t b0 = tc::smem_desc(tc::smem_u32(sm + OFF_P0 + n * P0_BYTES), 16, 1024,
-                                            tc::kSwizzle128);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) tc::mma_bf16(d1, a0 + 2 * k, b0 + 2 * k, id_gxs, k != 0);
-          tc::mma_bf16(d1,
-                       tc::smem_desc(tc::smem_u32(sm + OFF_G1), 16, 256,
-                                     tc::kSwizzle32),
-                       tc::smem_desc(tc::smem_u32(sm + OFF_P1 + n * P1_BYTES), 16, 256,
-                                     tc::kSwizzle32),
-                       id_gxs, 1);
-          tc::mma_commit(&d1full[e]);
-          if (n == N - 1 && seg_end_of(item, i)) {
-            tc::mma_commit(pempty);  // last use of this segment's P
-            ++seg_a;
-          }
-          return true;
-        };
-        auto issue_gphi = [&](int64_t sb) -> bool {
-          // ---- grad_phi of step sb = st - 1: D2[n] (+)= x_tile^T * Gp
-          const int64_t item = it0 + sb / N, i = item % ntiles;
-          const int n = (int)(sb % N);
-          const int s = (int)(sb % XS);
-          const bool seg_start = seg_start_of(item, i);
-          if (n == 0 && seg_start && !TW(2, tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag))) return false;
-          if (!TW(3, tc::mbar_wait(&xfull[s], (sb / XS) & 1, abort_flag))) return false;
-          tc::tc_fence_after();
-          const uint32_t d2 = tmem + n * 64;
-          const uint32_t sx = tc::smem_u32(sm + OFF_X + s * X_BYTES);
-          const uint32_t sgp = tc::smem_u32(sm + OFF_GP);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ax = tc::smem_desc(sx + kk * 2048, X_BYTES / 2, 1024, tc::kSwizzle128);
-            const uint64_t bg = tc::smem_desc(sgp + kk * 2048, GP_BYTES, 1024, tc::kSwizzle128);
-            tc::mma_bf16(d2, ax, bg, id_gphi, (seg_start && kk == 0) ? 0u : 1u);
-          }
-          tc::mma_commit(&xempty[s]);
-          if (n == N - 1) {
-            tc::mma_commit(gempty);
-            if (seg_end_of(item, i)) {
-              tc::mma_commit(d2full);
-              ++seg_b;
-            }
-          }
-          return true;
-        };
         // At an item boundary the previous item's last grad_phi MMAs go first: they
-        // release the single G buffer that the next item's gxs MMAs wait for.
-        if (st % N == 0) {
-          if (st >= 1 && !issue_gphi(st - 1)) { ok = false; break; }
+        // release GP, which the producer waits for before the item's next x tiles.
+        if (A.n == 0) {
+          if (st >= 1 && !issue_gphi()) { ok = false; break; }
           if (st < nsteps && !issue_gxs(st)) { ok = false; break; }
         } else {
           if (st < nsteps && !issue_gxs(st)) { ok = false; break; }
-          if (st >= 1 && !issue_gphi(st - 1)) { ok = false; break; }
+          if (st >= 1 && !issue_gphi()) { ok = false; break; }
         }
       }
       tc::mma_commit(tdone);
@@ -296,9 +331,12 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     const int r = q * 32 + lane;            // token row (D1) / column row (D2)
     uint32_t di = 0, seg = 0;
     bool first_seg = true;
-    for (int64_t item = it0; item < it1; ++item) {
-      const int64_t g = item / ntiles, i = item - g * ntiles;
-      const int64_t d0 = g * GC;
+    ItemCursor cur;
+    cur.init(it0, it1, ntiles, subt);
+    const bool starts_inside = cur.isub != 0;  // this CTA's run began inside a cell
+    for (; cur.item < it1; cur.next()) {
+      const int64_t item = cur.item, i = cur.i;
+      const int64_t d0 = cur.g * GC;
       const int64_t t = i * 128 + r;
       const bool live = t < T;
       float inv = 0.f, cf = 0.f, pr[N];
@@ -394,18 +432,19 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 #endif
         if (n == 0 && item + 1 < it1) {
           // pull the next item's grad_y row segment into L2 while this item runs
-          const int64_t gn = (item + 1) / ntiles, tn = ((item + 1) - gn * ntiles) * 128 + r;
+          const bool wrap = cur.i + 1 == ntiles;
+          const int64_t gn = wrap ? cur.g + 1 : cur.g, tn = (wrap ? 0 : i + 1) * 128 + r;
           if (tn < T) prefetch_l2(gy + tn * D + gn * GC + h * 32);
         }
       }
       if (!ok) break;
-      if (seg_end_of(item, i)) {
+      if (cur.seg_end) {
         // flush: D2[h] row r = column d0 + r; cols k: hi k, lo 24 + k
         if (!__all_sync(0xffffffffu, TW(2, tc::mbar_wait(d2full, seg & 1, abort_flag)))) break;
         tc::tc_fence_after();
         // slot 1 iff this CTA's run began inside the cell
-        const int64_t slot = cell_of(item, ntiles, subt, geo.cpg) * 2 +
-                             ((first_seg && (it0 % ntiles) % subt != 0) ? 1 : 0);
+        const int64_t slot = (cur.g * geo.cpg + cur.i / cur.subt) * 2 +
+                             ((first_seg && starts_inside) ? 1 : 0);
         first_seg = false;
         float v[48];
         const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + h * 64;
