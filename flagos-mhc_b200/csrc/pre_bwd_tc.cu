@@ -18,8 +18,10 @@
 // TMEM (4 x 64 columns) for the part of a cell a CTA owns and is then flushed into a
 // partial buffer, so no accumulation chain exceeds SUBT*8 MMAs (the tensor core's
 // fp32 accumulation error grows with the chain length).  pre_bwd_gphi_reduce_kernel
-// sums the partials of each column in a fixed order (deterministic).  The per-group
-// phi operand (80 KB) stays in shared memory for the whole segment.
+// sums the partials of each column in a fixed order (deterministic).  The phi operand
+// of each step (20 KB of the 4.6 MB operand rows, which stay in L2) is streamed into a
+// double buffer; grad_x leaves through per-warp shared-memory boxes and TMA stores, so
+// an x stage is released as soon as the epilogue and the grad_phi MMAs have read it.
 //
 // Roles (576 threads): warp 0 TMA producer; warp 1 TMEM owner + MMA issuer; warps 2-17
 // epilogue (warp w reads TMEM lane quarter w%4, column quarter (w-2)/4).
@@ -56,23 +58,28 @@ constexpr int G0_BYTES = 128 * 64 * 2;      // [128 tok][64 k]
 constexpr int G1_BYTES = 128 * 16 * 2;      // [128 tok][16 k]
 constexpr int GP_BYTES = 128 * 64 * 2;      // [128 tok][64 n]
 constexpr int X_BYTES = 2 * 128 * 64 * 2;   // two [128 tok][64 col] boxes
-constexpr int OFF_P0 = 0;
-constexpr int OFF_P1 = OFF_P0 + N * P0_BYTES;
-constexpr int OFF_G0 = OFF_P1 + N * P1_BYTES;
+constexpr int P_BYTES = P0_BYTES + P1_BYTES;  // phi operand of one sub-chunk (20 KB)
+constexpr int OUT_BYTES = 32 * 32 * 2;      // per epilogue warp: [32 tok][32 col], 64B swizzle
+constexpr int THREADS = 576;
+constexpr int EPI_WARPS = 16;
+constexpr int PS = 2;                       // phi operand buffers (streamed from L2 per step)
 constexpr int XS = 3;                       // x stages (G is single-buffered)
+constexpr int OFF_P = 0;                    // [PS] x {P0, P1}
+constexpr int OFF_G0 = OFF_P + PS * P_BYTES;
 constexpr int OFF_G1 = OFF_G0 + G0_BYTES;
 constexpr int OFF_GP = OFF_G1 + G1_BYTES;
 constexpr int OFF_X = OFF_GP + GP_BYTES;
-constexpr int OFF_BAR = OFF_X + XS * X_BYTES;
+constexpr int OFF_OUT = OFF_X + XS * X_BYTES;
+constexpr int OFF_BAR = OFF_OUT + EPI_WARPS * OUT_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr int THREADS = 576;
-constexpr int EPI_WARPS = 16;
+static_assert(SMEM <= 232448, "shared memory");
+static_assert(P_BYTES % 1024 == 0 && OFF_X % 1024 == 0 && OFF_OUT % 1024 == 0, "alignment");
 // TMEM columns: D2[n] (grad_phi, 64 each) at n*64, D1[b] (gxs, 128 each) at 256 + b*128
 constexpr int TMEM_COLS = 512;
 }  // namespace bwdtc
 
 struct BwdTcMaps {
-  CUtensorMap x, g0, g1, gp, p0, p1;
+  CUtensorMap x, g0, g1, gp, p0, p1, gx;
 };
 
 // A cell is `subt` consecutive token tiles of one column group; subt never exceeds the
@@ -116,7 +123,7 @@ __global__ void __launch_bounds__(bwdtc::THREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, __nv_bfloat16* __restrict__ gx,
-                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo, bool gx32,
+                  float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
                   long long* __restrict__ wdbg) {
   long long wcyc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const long long tstart = clock64();
@@ -128,16 +135,16 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   uint64_t* xempty = bar + XS;       // [XS] epilogue warps and grad_phi MMAs read the tile
   uint64_t* gfull = bar + 2 * XS;    // G0/G1 (gxs operand) of an item landed
   uint64_t* gempty = gfull + 1;      // the item's gxs MMAs are done with G0/G1
-  uint64_t* pfull = gfull + 2;
-  uint64_t* pempty = gfull + 3;
-  uint64_t* d1full = gfull + 4;      // [2]
-  uint64_t* d1empty = gfull + 6;     // [2]
-  uint64_t* d2full = gfull + 8;
-  uint64_t* d2empty = gfull + 9;
-  uint64_t* tdone = gfull + 10;
-  uint64_t* gpfull = gfull + 11;     // GP (grad_phi operand) of an item landed
-  uint64_t* gpempty = gfull + 12;    // the item's grad_phi MMAs are done with GP
-  uint32_t* tmem_slot = (uint32_t*)(gfull + 13);
+  uint64_t* pfull = gfull + 2;       // [PS] phi operand of a step landed
+  uint64_t* pempty = gfull + 4;      // [PS] the step's gxs MMAs are done with it
+  uint64_t* d1full = gfull + 6;      // [2]
+  uint64_t* d1empty = gfull + 8;     // [2]
+  uint64_t* d2full = gfull + 10;
+  uint64_t* d2empty = gfull + 11;
+  uint64_t* tdone = gfull + 12;
+  uint64_t* gpfull = gfull + 13;     // GP (grad_phi operand) of an item landed
+  uint64_t* gpempty = gfull + 14;    // the item's grad_phi MMAs are done with GP
+  uint32_t* tmem_slot = (uint32_t*)(gfull + 15);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -158,8 +165,10 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     tc::mbar_init(gempty, 1);
     tc::mbar_init(gpfull, 1);
     tc::mbar_init(gpempty, 1);
-    tc::mbar_init(pfull, 1);
-    tc::mbar_init(pempty, 1);
+    for (int b = 0; b < PS; ++b) {
+      tc::mbar_init(&pfull[b], 1);
+      tc::mbar_init(&pempty[b], 1);
+    }
     tc::mbar_init(d2full, 1);
     tc::mbar_init(d2empty, EPI_WARPS);
     tc::mbar_init(tdone, 1);
@@ -171,6 +180,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     tc::prefetch_tmap(&maps.g0);
     tc::prefetch_tmap(&maps.gp);
     tc::prefetch_tmap(&maps.p0);
+    tc::prefetch_tmap(&maps.gx);
   }
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -187,22 +197,22 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      uint32_t xi = 0, gi = 0, seg = 0;
+      uint32_t xi = 0, gi = 0;
       bool ok = true;
       ItemCursor cur;
       cur.init(it0, it1, ntiles, subt);
       for (; cur.item < it1 && ok; cur.next()) {
         const int i = cur.i;
         const int d0 = (int)(cur.g * GC);
-        if (cur.seg_start) {
-          if (!TW(0, tc::mbar_wait(pempty, (seg & 1) ^ 1, abort_flag))) break;
-          tc::mbar_arrive_expect_tx(pfull, N * (P0_BYTES + P1_BYTES));
-          for (int n = 0; n < N; ++n) {
-            tc::tma_load_2d(sm + OFF_P0 + n * P0_BYTES, &maps.p0, pfull, 0, (int)(n * D + d0));
-            tc::tma_load_2d(sm + OFF_P1 + n * P1_BYTES, &maps.p1, pfull, 0, (int)(n * D + d0));
-          }
-        }
         for (int n = 0; n < N; ++n, ++xi) {
+          // the step's phi operand (4.6 MB in all, L2-resident): ahead of its x tile,
+          // since the gxs MMAs need it one step before the x tile is used
+          const int pb = xi & 1;
+          if (!TW(0, tc::mbar_wait(&pempty[pb], ((xi >> 1) & 1) ^ 1, abort_flag))) { ok = false; break; }
+          tc::mbar_arrive_expect_tx(&pfull[pb], P_BYTES);
+          uint8_t* pdst = sm + OFF_P + pb * P_BYTES;
+          tc::tma_load_2d(pdst, &maps.p0, &pfull[pb], 0, (int)(n * D + d0));
+          tc::tma_load_2d(pdst + P0_BYTES, &maps.p1, &pfull[pb], 0, (int)(n * D + d0));
           const int s = xi % XS;
           if (!TW(2, tc::mbar_wait(&xempty[s], ((xi / XS) & 1) ^ 1, abort_flag))) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&xfull[s], X_BYTES);
@@ -223,7 +233,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             ++gi;
           }
         }
-        if (cur.seg_end) ++seg;
       }
     }
   } else if (warp == 1) {
@@ -249,34 +258,30 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       A.n = 0; A.s = 0; A.gi = 0; A.xph = 0;
       B = A;
       const int64_t nsteps = (it1 - it0) * N;
-      uint32_t seg_a = 0, seg_b = 0;
+      uint32_t seg_b = 0;
       const uint32_t sg0 = tc::smem_u32(sm + OFF_G0), sg1 = tc::smem_u32(sm + OFF_G1);
-      const uint32_t sp0 = tc::smem_u32(sm + OFF_P0), sp1 = tc::smem_u32(sm + OFF_P1);
+      const uint32_t sp = tc::smem_u32(sm + OFF_P);
       const uint32_t sx0 = tc::smem_u32(sm + OFF_X), sgp = tc::smem_u32(sm + OFF_GP);
       bool ok = true;
       auto issue_gxs = [&](int64_t st) -> bool {
         // ---- gxs of step st (position A)
         const int n = A.n;
         const int e = (int)(st & 1);
-        if (n == 0) {
-          if (A.c.seg_start && !TW(0, tc::mbar_wait(pfull, seg_a & 1, abort_flag))) return false;
-          if (!TW(0, tc::mbar_wait(gfull, A.gi & 1, abort_flag))) return false;
-        }
+        if (n == 0 && !TW(0, tc::mbar_wait(gfull, A.gi & 1, abort_flag))) return false;
+        if (!TW(0, tc::mbar_wait(&pfull[e], (uint32_t)(st >> 1) & 1, abort_flag))) return false;
         if (!TW(1, tc::mbar_wait(&d1empty[e], ((uint32_t)(st >> 1) & 1) ^ 1, abort_flag))) return false;
         tc::tc_fence_after();
         const uint32_t d1 = tmem + 256 + e * 128;
         const uint64_t a0 = tc::smem_desc(sg0, 16, 1024, tc::kSwizzle128);
-        const uint64_t b0 = tc::smem_desc(sp0 + n * P0_BYTES, 16, 1024, tc::kSwizzle128);
+        const uint32_t spb = sp + e * P_BYTES;
+        const uint64_t b0 = tc::smem_desc(spb, 16, 1024, tc::kSwizzle128);
 #pragma unroll
         for (int k = 0; k < 4; ++k) tc::mma_bf16(d1, a0 + 2 * k, b0 + 2 * k, id_gxs, k != 0);
         tc::mma_bf16(d1, tc::smem_desc(sg1, 16, 256, tc::kSwizzle32),
-                     tc::smem_desc(sp1 + n * P1_BYTES, 16, 256, tc::kSwizzle32), id_gxs, 1);
+                     tc::smem_desc(spb + P0_BYTES, 16, 256, tc::kSwizzle32), id_gxs, 1);
         tc::mma_commit(&d1full[e]);
+        tc::mma_commit(&pempty[e]);
         if (n == N - 1) tc::mma_commit(gempty);  // last gxs use of this item's G0/G1
-        if (n == N - 1 && A.c.seg_end) {
-          tc::mma_commit(pempty);  // last use of this segment's P
-          ++seg_a;
-        }
         A.next();
         return true;
       };
@@ -329,6 +334,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     const int q = warp & 3;
     const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;            // token row (D1) / column row (D2)
+    uint8_t* ob = sm + OFF_OUT + (warp - 2) * OUT_BYTES;
     uint32_t di = 0, seg = 0;
     bool first_seg = true;
     ItemCursor cur;
@@ -339,6 +345,10 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       const int64_t d0 = cur.g * GC;
       const int64_t t = i * 128 + r;
       const bool live = t < T;
+      const int64_t row0 = i * 128 + q * 32;  // first token row of this warp's store box
+#ifdef MHC_PROFILE_WAITS
+      const long long _p4 = clock64();
+#endif
       float inv = 0.f, cf = 0.f, pr[N];
       uint4 gyv[4];
       if (live) {
@@ -355,6 +365,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 #pragma unroll
         for (int j = 0; j < 4; ++j) gyv[j] = make_uint4(0, 0, 0, 0);
       }
+#ifdef MHC_PROFILE_WAITS
+      wcyc[4] += clock64() - _p4;
+#endif
       bool ok = true;
       for (int n = 0; n < N; ++n, ++di) {
         const int e = di & 1, s = di % XS;
@@ -368,6 +381,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
           ok = false;
           break;
         }
+#ifdef MHC_PROFILE_WAITS
+        const long long _p3 = clock64();
+#endif
         // x row r, columns [32h, 32h+32): box h/2, 16-byte chunks 4(h%2)..+3 (swizzled)
         const uint8_t* xrow = sm + OFF_X + s * X_BYTES + (h >> 1) * (X_BYTES / 2) + r * 128;
         uint4 xv[4];
@@ -381,12 +397,18 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         if (lane == 0) tc::mbar_arrive(&xempty[s]);
 #ifdef MHC_PROFILE_WAITS
         long long _p2 = clock64();
+        wcyc[3] += _p2 - _p3;
 #endif
         // gxs in two halves of 16 columns (keeps the live registers under the 96 that
-        // 18 warps per CTA allow); grad_x goes straight from registers to global memory,
-        // 64 contiguous bytes per thread
+        // 18 warps per CTA allow).  grad_x goes through this warp's own 2 KB buffer
+        // ([32 tok][32 col], 64-byte swizzle: chunk c of row r at (c ^ (r/2 % 4))) and
+        // one TMA store per warp and step; the buffer is reused once that store has
+        // read it.
         const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + 256 + e * 128 + h * 32;
-        __nv_bfloat16* dst = gx + t * (N * D) + n * D + d0 + h * 32;
+        uint8_t* orow = ob + lane * 64;
+        const int osw = (lane >> 1) & 3;
+        if (lane == 0) tc::bulk_wait_read<0>();
+        __syncwarp();
         const float prn = pr[n];
         const float2 pr2 = make_float2(prn, prn), inv2 = make_float2(inv, inv),
                      ncf2 = make_float2(-cf, -cf);
@@ -418,14 +440,15 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             }
             ov[jj] = narrow<__nv_bfloat16>(o);
           }
-          if (live) {
-            if (gx32) {
-              st_global_32B(dst + 16 * jp, ov[0], ov[1]);
-            } else {
-              st_stream(dst + 16 * jp, ov[0]);
-              st_stream(dst + 16 * jp + 8, ov[1]);
-            }
-          }
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj)
+            *reinterpret_cast<uint4*>(orow + (((2 * jp + jj) ^ osw) << 4)) = ov[jj];
+        }
+        tc::fence_proxy_async();          // generic smem writes -> TMA store reads
+        __syncwarp();
+        if (lane == 0 && row0 < T) {
+          tc::tma_store_2d(&maps.gx, ob, (int)(n * D + d0 + h * 32), (int)row0);
+          tc::bulk_commit_group();
         }
 #ifdef MHC_PROFILE_WAITS
         wcyc[5] += clock64() - _p2;
@@ -461,6 +484,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       }
     }
   }
+  if (warp >= 2 && lane == 0) tc::bulk_wait_all<0>();  // grad_x stores have landed
   if (*abort_flag && threadIdx.x == 0) flag_timeout();
 #ifdef MHC_PROFILE_WAITS
   // row per CTA: [total, producer x4, mma x4, epilogue warp 2 x4]
@@ -630,6 +654,10 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
     return st;
   if ((st = make_tmap_2d(&m.p1, w.p1, bf, 2, 16, HC, 32, 16, 128, CU_TENSOR_MAP_SWIZZLE_32B)))
     return st;
+  // grad_x store boxes: 32 columns (64 B) x 32 token rows, one per epilogue warp and step
+  if ((st = make_tmap_2d(&m.gx, a.grad_x, bf, 2, HC, T, HC * 2, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_64B)))
+    return st;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -641,7 +669,6 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
   pre_bwd_tc_kernel<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
                                                     (__nv_bfloat16*)a.grad_x, w.part, T, D, geo,
-                                                    (reinterpret_cast<uintptr_t>(a.grad_x) & 31) == 0,
 #ifdef MHC_PROFILE_WAITS
                                                     getenv("MHC_WAIT_DBG")
                                                         ? (long long*)strtoull(getenv("MHC_WAIT_DBG"), nullptr, 10)
