@@ -18,6 +18,7 @@ int post_bwd_dispatch(int32_t N, int32_t dtype, const void* gy, const void* x,
 
 int pre_fwd_tc_device_error();
 int pre_bwd_tc_device_error();
+int pre_bwd_tc8_device_error();
 
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
@@ -108,7 +109,8 @@ int mhc_device_status(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return MHC_ERR_CUDA;
   const int a = pre_fwd_tc_device_error();
   const int b = pre_bwd_tc_device_error();
-  return a != MHC_OK ? a : b;
+  const int c = pre_bwd_tc8_device_error();
+  return a != MHC_OK ? a : (b != MHC_OK ? b : c);
 }
 
 int mhc_post_fwd(const void* x, const float* h_res, const void* h_out, const float* h_post,

@@ -357,6 +357,11 @@ size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D);
 void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
                              __nv_bfloat16** g1, __nv_bfloat16** gp);
 int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream_t s);
+bool pre_bwd_tc8_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
+                          const void* gy, const void* gx);
+size_t pre_bwd_tc8_ws_bytes(int64_t T, int64_t D);
+int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                     cudaStream_t s);
 
 struct BwdWs {
   float *gpre, *gm, *coef, *partials, *hist, *gphi_part;
@@ -385,10 +390,15 @@ static bool tc_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
   return dtype == MHC_BF16 && N == 4 && D % 128 == 0 && T > 0;
 }
 
-// generic region, then (bf16, N=4, D%128==0 only) the tensor-core region
+static bool tc8_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
+  return dtype == MHC_BF16 && N == 8 && D % 64 == 0 && T > 0;
+}
+
+// generic region, then (bf16, N=4, D%128==0 or N=8, D%64==0) the tensor-core region
 size_t pre_bwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype, int32_t iters) {
   size_t n = bwd_layout(nullptr, T, N, D, iters).total;
   if (tc_shape(T, N, D, dtype)) n += align_up(pre_bwd_tc_ws_bytes(T, D));
+  if (tc8_shape(T, N, D, dtype)) n += align_up(pre_bwd_tc8_ws_bytes(T, D));
   return n;
 }
 
@@ -400,6 +410,8 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const int nblk = (int)cdiv(T, 128);
   const bool use_tc = std::is_same<E, __nv_bfloat16>::value &&
                       pre_bwd_tc_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
+  const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value &&
+                       pre_bwd_tc8_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
   char* tc_ws = (char*)a.workspace + w.total;
   __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr;
   if (use_tc) pre_bwd_tc_operand_ptrs(tc_ws, T, D, &g0, &g1, &gp);
@@ -428,6 +440,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
                                                                        a.grad_alpha, a.grad_base);
   MHC_LAUNCH_CHECK();
   if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.coef, s);
+  if (use_tc8) return pre_bwd_tc8_main(a, tc_ws, w.gm, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   pre_bwd_gx_kernel<E, N><<<ggrid, kGxCC, 0, s>>>((const E*)a.x, (const E*)a.grad_y, a.phi,
                                                   w.gm, a.inv_rms, w.coef, a.pre,

@@ -315,3 +315,31 @@ def test_pre_skip_x_scaled_opt_in():
     y, post, comb = M.mhc_pre_clamp_sinkhorn_fn(xd, d[1], d[2], d[3], materialize_x_scaled=False)
     (y.float().sum() + comb.sum()).backward()
     assert xd.grad is not None and torch.isfinite(xd.grad.float()).all()
+
+
+@pytest.mark.parametrize("T,D", [(148 * 128 + 77, 256), (1000, 4096)])
+def test_pre_bwd_n8_tensor_core(T, D):
+    """N=8 (hcMix=80) tensor-core backward: grad_x tiles over many 64-column steps with
+    CTA ranges that start mid-tile, and grad_phi column tiles shared by several CTAs
+    (partials summed in a fixed order), against the fp64 oracle on the same saved
+    tensors; repeated calls are bitwise equal."""
+    N = 8
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=T + D,
+                                                       phi_std=1.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    out = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True, **kw)
+    args = (d[0], d[1], d[2], d[3], out["inv_rms"], out["x_scaled"], out["mixes"],
+            out["h_res_logits"], out["pre"], d[4], d[5], d[6])
+    got = M.mhc_pre_clamp_sinkhorn_backward(*args, **kw)
+    again = M.mhc_pre_clamp_sinkhorn_backward(*args, **kw)
+    for u, v in zip(got, again):
+        assert torch.equal(u, v)
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=-10.0, clamp_max=10.0, iter_times=20, dtype=F64)
+    assert rel_err(got[0], want[0]) <= TOL_BF16
+    for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
+        assert rel_err(a, b) <= TOL_FP32, name
+    from FlagOS_mhc import _C
+    assert _C.lib().mhc_device_status() == 0
