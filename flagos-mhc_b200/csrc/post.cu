@@ -205,6 +205,176 @@ post_fwd_x16_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
 static inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31) == 0; }
 
 // ---------------------------------------------------------------------------
+// N = 8, 16-bit storage, D % 32 == 0: one warp per token, lane (g, c) = (lane/4, lane%4)
+// owns row g at the 8 consecutive d of chunk c of every 32-wide step, so every load and
+// store is a 16-byte pack.  The per-token 8x8 products run on mma.sync m16n8k16 (fp32
+// accumulate); the fp32 h_res / h_post enter as bf16 (or fp16) hi + lo halves, which
+// reproduces the fp32 products to ~2^-17.  A generic N=8 lane would need 64 h_res and 64
+// accumulators in registers.
+//   grad_h_res[j,i] = <x[j], gy[i]>, grad_h_post[i] = <h_out, gy[i]>:  A = [x rows; h_out]
+//     (16 x 16 d), B = gy rows (16 d x 8), both straight from the lane's registers (the
+//     k slots of a lane map to its own d, identically for A and B).
+//   grad_x[j,d] = sum_i h_res[j,i] gy[i,d], grad_h_out[d] = sum_i h_post[i] gy[i,d]:
+//     A = [h_res_hi | h_res_lo ; h_post_hi | h_post_lo] (rows j, then row 8), B = gy
+//     transposed by movmatrix (one per register r), which makes the result land back in
+//     the lane's own row / d layout.
+//   out[i,d] = sum_j h_res[j,i] x[j,d] + h_post[i] h_out[d]: the same with A = h_res^T
+//     and B = x transposed, plus the h_post term in fp32.
+template <typename E>
+__device__ __forceinline__ uint32_t pack_e2(float a, float b) {
+  if constexpr (std::is_same<E, __half>::value) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+template <typename E>
+__device__ __forceinline__ float round_e(float v) {
+  if constexpr (std::is_same<E, __half>::value) return __half2float(__float2half_rn(v));
+  else return __bfloat162float(__float2bfloat16_rn(v));
+}
+// hi / lo halves of two fp32 values, packed as (lo index in the low 16 bits)
+template <typename E>
+__device__ __forceinline__ void split_e2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const float ah = round_e<E>(a), bh = round_e<E>(b);
+  hi = pack_e2<E>(ah, bh);
+  lo = pack_e2<E>(a - ah, b - bh);
+}
+template <typename E>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1, float c0, float c1, float c2, float c3) {
+  if constexpr (std::is_same<E, __half>::value)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1),
+          "f"(c2), "f"(c3));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1),
+          "f"(c2), "f"(c3));
+}
+// transpose of the warp's 8x8 16-bit matrix held one 32-bit register per lane
+__device__ __forceinline__ uint32_t movtrans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+__device__ __forceinline__ uint32_t u4_at(const uint4& v, int r) {
+  return r == 0 ? v.x : r == 1 ? v.y : r == 2 ? v.z : v.w;
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256)
+post_fwd_n8_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
+                   const E* __restrict__ h_out, const float* __restrict__ h_post,
+                   E* __restrict__ out, int64_t T, int64_t D) {
+  constexpr int N = 8;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
+       t += nwarps) {
+    // A = [h_res^T hi | h_res^T lo] rows i = g: (h_res[2c][g], h_res[2c+1][g])
+    const float* hr = h_res + t * N * N;
+    uint32_t a[4];
+    split_e2<E>(__ldg(hr + (2 * c) * N + g), __ldg(hr + (2 * c + 1) * N + g), a[0], a[2]);
+    a[1] = a[3] = 0u;
+    const float hp = __ldg(h_post + t * N + g);
+    const E* xr = x + (t * N + g) * D;
+    const E* ht = h_out + t * D;
+    E* orow = out + (t * N + g) * D;
+#pragma unroll 2
+    for (int64_t d0 = 8 * c; d0 < D; d0 += 32) {
+      const uint4 xv = ld_stream(reinterpret_cast<const uint4*>(xr + d0));
+      const uint4 hv = ld_stream(reinterpret_cast<const uint4*>(ht + d0));
+      float hf[8], o[8];
+      widen<E>(hv, hf);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const uint32_t b = movtrans(u4_at(xv, r));
+        float cc[4];
+        mma16816<E>(cc, a, b, b, 0.f, 0.f, 0.f, 0.f);
+        o[2 * r] = fmaf(hp, hf[2 * r], cc[0]);
+        o[2 * r + 1] = fmaf(hp, hf[2 * r + 1], cc[1]);
+      }
+      st_stream(reinterpret_cast<uint4*>(orow + d0), narrow<E>(o));
+    }
+  }
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256)
+post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
+                   const float* __restrict__ h_res, const E* __restrict__ h_out,
+                   const float* __restrict__ h_post, E* __restrict__ gx,
+                   float* __restrict__ ghres, E* __restrict__ ghout,
+                   float* __restrict__ ghpost, int64_t T, int64_t D) {
+  constexpr int N = 8;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
+       t += nwarps) {
+    // A of grad_x: rows j = g: (h_res[g][2c], h_res[g][2c+1]) hi | lo; row 8: h_post
+    const float* hr = h_res + t * N * N;
+    uint32_t a[4];
+    split_e2<E>(__ldg(hr + g * N + 2 * c), __ldg(hr + g * N + 2 * c + 1), a[0], a[2]);
+    if (g == 0) {
+      split_e2<E>(__ldg(h_post + t * N + 2 * c), __ldg(h_post + t * N + 2 * c + 1), a[1], a[3]);
+    } else {
+      a[1] = a[3] = 0u;
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const E* xr = x + (t * N + g) * D;
+    const E* gyr = gy + (t * N + g) * D;
+    const E* ht = h_out + t * D;
+    E* gxr = gx + (t * N + g) * D;
+    E* ght = ghout + t * D;
+#pragma unroll 2
+    for (int64_t d0 = 8 * c; d0 < D; d0 += 32) {
+      const uint4 xv = ld_stream(reinterpret_cast<const uint4*>(xr + d0));
+      const uint4 gv = ld_stream(reinterpret_cast<const uint4*>(gyr + d0));
+      uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+      if (g == 0) hv = ld_stream(reinterpret_cast<const uint4*>(ht + d0));
+      // <x[j], gy[i]> and <h_out, gy[i]>: two k-16 slices of this step
+      float dd[4];
+      {
+        const uint32_t a0[4] = {xv.x, hv.x, xv.y, hv.y};
+        mma16816<E>(dd, a0, gv.x, gv.y, 0.f, 0.f, 0.f, 0.f);
+        const uint32_t a1[4] = {xv.z, hv.z, xv.w, hv.w};
+        mma16816<E>(dd, a1, gv.z, gv.w, dd[0], dd[1], dd[2], dd[3]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += dd[u];
+      float o[8], oh[8];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const uint32_t b = movtrans(u4_at(gv, r));
+        float cc[4];
+        mma16816<E>(cc, a, b, b, 0.f, 0.f, 0.f, 0.f);
+        o[2 * r] = cc[0];
+        o[2 * r + 1] = cc[1];
+        oh[2 * r] = cc[2];
+        oh[2 * r + 1] = cc[3];
+      }
+      st_stream(reinterpret_cast<uint4*>(gxr + d0), narrow<E>(o));
+      if (g == 0) st_stream(reinterpret_cast<uint4*>(ght + d0), narrow<E>(oh));
+    }
+    ghres[t * N * N + g * N + 2 * c] = acc[0];
+    ghres[t * N * N + g * N + 2 * c + 1] = acc[1];
+    if (g == 0) {
+      ghpost[t * N + 2 * c] = acc[2];
+      ghpost[t * N + 2 * c + 1] = acc[3];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
 static int post_grid(int64_t T) {
@@ -219,6 +389,14 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
                            cudaStream_t s) {
   const bool vec = (D % Pack<E>::n == 0) && aligned16(x) && aligned16(h_out) && aligned16(out);
   dim3 grid(post_grid(T)), block(256);
+  if constexpr (sizeof(E) == 2 && N == 8) {
+    if (D % 32 == 0 && vec) {
+      post_fwd_n8_kernel<E><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out, h_post,
+                                                   (E*)out, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
+  }
   if constexpr (sizeof(E) == 2 && N <= 4) {
     if (D % 16 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
       post_fwd_x16_kernel<E, N><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
@@ -244,6 +422,15 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
   const bool vec = (D % Pack<E>::n == 0) && aligned16(gy) && aligned16(x) &&
                    aligned16(h_out) && aligned16(gx) && aligned16(ghout);
   dim3 grid(post_grid(T)), block(256);
+  if constexpr (sizeof(E) == 2 && N == 8) {
+    if (D % 32 == 0 && vec) {
+      post_bwd_n8_kernel<E><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+                                                   (const E*)h_out, h_post, (E*)gx, ghres,
+                                                   (E*)ghout, ghpost, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
+  }
   if (vec)
     post_bwd_kernel<E, N, true><<<grid, block, 0, s>>>(
         (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,
