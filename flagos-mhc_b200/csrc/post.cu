@@ -266,16 +266,42 @@ __device__ __forceinline__ uint32_t movtrans(uint32_t a) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
   return d;
 }
-__device__ __forceinline__ uint32_t u4_at(const uint4& v, int r) {
-  return r == 0 ? v.x : r == 1 ? v.y : r == 2 ? v.z : v.w;
+template <typename E>
+__device__ __forceinline__ void widen2(uint32_t w, float* f) {
+  if constexpr (std::is_same<E, __half>::value) {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    f[0] = __low2float(h);
+    f[1] = __high2float(h);
+  } else {
+    f[0] = bf16_lo(w);
+    f[1] = bf16_hi(w);
+  }
 }
 
-template <typename E>
+// V 16-byte packs per lane and row per step (V = 2: 32-byte accesses, 64-wide steps)
+template <int V>
+__device__ __forceinline__ void ld_row_packs(const void* p, uint32_t (&r)[4 * V]) {
+  if constexpr (V == 2) {
+    const U8 v = ld_global_32B(p);
+    r[0] = v.a.x; r[1] = v.a.y; r[2] = v.a.z; r[3] = v.a.w;
+    r[4] = v.b.x; r[5] = v.b.y; r[6] = v.b.z; r[7] = v.b.w;
+  } else {
+    const uint4 v = ld_stream(p);
+    r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+  }
+}
+template <typename E, int V>
+__device__ __forceinline__ void st_row_packs(void* p, const float* o) {
+  if constexpr (V == 2) st_global_32B(p, narrow<E>(o), narrow<E>(o + 8));
+  else st_stream(p, narrow<E>(o));
+}
+
+template <typename E, int V>
 __global__ void __launch_bounds__(256)
 post_fwd_n8_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                    const E* __restrict__ h_out, const float* __restrict__ h_post,
                    E* __restrict__ out, int64_t T, int64_t D) {
-  constexpr int N = 8;
+  constexpr int N = 8, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
@@ -290,32 +316,34 @@ post_fwd_n8_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
     const E* ht = h_out + t * D;
     E* orow = out + (t * N + g) * D;
 #pragma unroll 2
-    for (int64_t d0 = 8 * c; d0 < D; d0 += 32) {
-      const uint4 xv = ld_stream(reinterpret_cast<const uint4*>(xr + d0));
-      const uint4 hv = ld_stream(reinterpret_cast<const uint4*>(ht + d0));
-      float hf[8], o[8];
-      widen<E>(hv, hf);
+    for (int64_t d0 = 8 * V * c; d0 < D; d0 += 32 * V) {
+      uint32_t xv[R], hv[R];
+      ld_row_packs<V>(xr + d0, xv);
+      ld_row_packs<V>(ht + d0, hv);
+      float o[2 * R];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const uint32_t b = movtrans(u4_at(xv, r));
+      for (int r = 0; r < R; ++r) {
+        const uint32_t b = movtrans(xv[r]);
         float cc[4];
         mma16816<E>(cc, a, b, b, 0.f, 0.f, 0.f, 0.f);
-        o[2 * r] = fmaf(hp, hf[2 * r], cc[0]);
-        o[2 * r + 1] = fmaf(hp, hf[2 * r + 1], cc[1]);
+        float h2[2];
+        widen2<E>(hv[r], h2);
+        o[2 * r] = fmaf(hp, h2[0], cc[0]);
+        o[2 * r + 1] = fmaf(hp, h2[1], cc[1]);
       }
-      st_stream(reinterpret_cast<uint4*>(orow + d0), narrow<E>(o));
+      st_row_packs<E, V>(orow + d0, o);
     }
   }
 }
 
-template <typename E>
+template <typename E, int V>
 __global__ void __launch_bounds__(256)
 post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                    const float* __restrict__ h_res, const E* __restrict__ h_out,
                    const float* __restrict__ h_post, E* __restrict__ gx,
                    float* __restrict__ ghres, E* __restrict__ ghout,
                    float* __restrict__ ghpost, int64_t T, int64_t D) {
-  constexpr int N = 8;
+  constexpr int N = 8, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
@@ -336,25 +364,26 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
     E* gxr = gx + (t * N + g) * D;
     E* ght = ghout + t * D;
 #pragma unroll 2
-    for (int64_t d0 = 8 * c; d0 < D; d0 += 32) {
-      const uint4 xv = ld_stream(reinterpret_cast<const uint4*>(xr + d0));
-      const uint4 gv = ld_stream(reinterpret_cast<const uint4*>(gyr + d0));
-      uint4 hv = make_uint4(0u, 0u, 0u, 0u);
-      if (g == 0) hv = ld_stream(reinterpret_cast<const uint4*>(ht + d0));
-      // <x[j], gy[i]> and <h_out, gy[i]>: two k-16 slices of this step
-      float dd[4];
-      {
-        const uint32_t a0[4] = {xv.x, hv.x, xv.y, hv.y};
-        mma16816<E>(dd, a0, gv.x, gv.y, 0.f, 0.f, 0.f, 0.f);
-        const uint32_t a1[4] = {xv.z, hv.z, xv.w, hv.w};
-        mma16816<E>(dd, a1, gv.z, gv.w, dd[0], dd[1], dd[2], dd[3]);
+    for (int64_t d0 = 8 * V * c; d0 < D; d0 += 32 * V) {
+      uint32_t xv[R], gv[R], hv[R];
+      ld_row_packs<V>(xr + d0, xv);
+      ld_row_packs<V>(gyr + d0, gv);
+#pragma unroll
+      for (int r = 0; r < R; ++r) hv[r] = 0u;
+      if (g == 0) ld_row_packs<V>(ht + d0, hv);
+      // <x[j], gy[i]> and <h_out, gy[i]>: k-16 slices of this step (4 d per lane each)
+      float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int sl = 0; sl < R / 2; ++sl) {
+        const uint32_t as[4] = {xv[2 * sl], hv[2 * sl], xv[2 * sl + 1], hv[2 * sl + 1]};
+        mma16816<E>(dd, as, gv[2 * sl], gv[2 * sl + 1], dd[0], dd[1], dd[2], dd[3]);
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) acc[u] += dd[u];
-      float o[8], oh[8];
+      float o[2 * R], oh[2 * R];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const uint32_t b = movtrans(u4_at(gv, r));
+      for (int r = 0; r < R; ++r) {
+        const uint32_t b = movtrans(gv[r]);
         float cc[4];
         mma16816<E>(cc, a, b, b, 0.f, 0.f, 0.f, 0.f);
         o[2 * r] = cc[0];
@@ -362,8 +391,8 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
         oh[2 * r] = cc[2];
         oh[2 * r + 1] = cc[3];
       }
-      st_stream(reinterpret_cast<uint4*>(gxr + d0), narrow<E>(o));
-      if (g == 0) st_stream(reinterpret_cast<uint4*>(ght + d0), narrow<E>(oh));
+      st_row_packs<E, V>(gxr + d0, o);
+      if (g == 0) st_row_packs<E, V>(ght + d0, oh);
     }
     ghres[t * N * N + g * N + 2 * c] = acc[0];
     ghres[t * N * N + g * N + 2 * c + 1] = acc[1];
@@ -390,9 +419,15 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
   const bool vec = (D % Pack<E>::n == 0) && aligned16(x) && aligned16(h_out) && aligned16(out);
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 8) {
+    if (D % 64 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
+      post_fwd_n8_kernel<E, 2><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
+                                                      h_post, (E*)out, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
     if (D % 32 == 0 && vec) {
-      post_fwd_n8_kernel<E><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out, h_post,
-                                                   (E*)out, T, D);
+      post_fwd_n8_kernel<E, 1><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
+                                                      h_post, (E*)out, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
@@ -423,10 +458,18 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
                    aligned16(h_out) && aligned16(gx) && aligned16(ghout);
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 8) {
+    if (D % 64 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
+        aligned32(ghout)) {
+      post_bwd_n8_kernel<E, 2><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+                                                      (const E*)h_out, h_post, (E*)gx, ghres,
+                                                      (E*)ghout, ghpost, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
     if (D % 32 == 0 && vec) {
-      post_bwd_n8_kernel<E><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
-                                                   (const E*)h_out, h_post, (E*)gx, ghres,
-                                                   (E*)ghout, ghpost, T, D);
+      post_bwd_n8_kernel<E, 1><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+                                                      (const E*)h_out, h_post, (E*)gx, ghres,
+                                                      (E*)ghout, ghpost, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
