@@ -264,6 +264,96 @@ def reference_arm(args, rank, world):
     return 0
 
 
+# ----------------------------------------------------------------------------- other configs
+def _timed(fn, steps, warmup, nev):
+    """Mean ms between consecutive events that fn(ev) records, over `steps` runs."""
+    for _ in range(warmup):
+        fn(None)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(steps)]
+    for k in range(steps):
+        fn(evs[k])
+    torch.cuda.synchronize()
+    return [statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(steps))
+            for i in range(nev - 1)]
+
+
+def other_configs(M, dev, peak, steps=3, warmup=2):
+    """Config C1 (pre forward, need_backward) and config C4 (the N=8 layer step:
+    pre -> h_out = y.W (cuBLAS) -> post, then the backward of the same chain), synthetic
+    inputs with the configs' distributions.  Reported beside the headline number."""
+    res = {}
+    bf = torch.bfloat16
+    # ---- C1: T=16384, N=4, D=4096, pre forward with need_backward=True
+    T, N, D = 16384, 4, 4096
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+    phi = torch.randn(24, N * D, generator=g, device=dev) / 128.0
+    alpha = torch.rand(3, generator=g, device=dev) + 0.5
+    base = torch.randn(24, generator=g, device=dev) * 0.1
+
+    def c1(ev):
+        if ev is not None:
+            ev[0].record()
+        M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
+        if ev is not None:
+            ev[1].record()
+    ms = _timed(c1, max(steps, 5), warmup, 2)[0]
+    nbytes = T * 106756
+    res["C1_pre_fwd"] = {"shape": [T, N, D], "ms": ms, "tokens_per_s": T / (ms / 1e3),
+                         "GB/s": nbytes / (ms / 1e3) / 1e9,
+                         "frac_of_peak": nbytes / (ms / 1e3) / 1e9 / peak}
+    del x, phi
+    torch.cuda.empty_cache()
+    # ---- C4: T=65536, N=8, D=4096 layer step
+    T, N, D = 65536, 8, 4096
+    HM = N * (N + 2)
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+    phi = torch.randn(HM, N * D, generator=g, device=dev) / 181.0
+    alpha = torch.rand(3, generator=g, device=dev) + 0.5
+    base = torch.randn(HM, generator=g, device=dev) * 0.1
+    W = (torch.randn(D, D, generator=g, device=dev) / 64.0).to(bf)
+    gz = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+
+    def c4(ev):
+        rec = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
+        rec(0)
+        out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
+        rec(1)
+        h_out = out["y"] @ W
+        rec(2)
+        M.mhc_post(x, out["comb_frag"], h_out, out["post_out"])
+        rec(3)
+        gxp, ghres, ghout, ghpost = M.mhc_post_backward(gz, x, out["comb_frag"], h_out,
+                                                        out["post_out"])
+        rec(4)
+        gy = ghout @ W.t()
+        gW = out["y"].t() @ ghout
+        rec(5)
+        gxq, gphi, ga, gb = M.mhc_pre_clamp_sinkhorn_backward(
+            x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+            out["h_res_logits"], out["pre"], gy, ghpost, ghres, **KW)
+        rec(6)
+        gxp.add_(gxq)
+        rec(7)
+        return gW
+    t = _timed(c4, steps, warmup, 8)
+    mhc_ms = t[0] + t[2] + t[3] + t[5]
+    nbytes = T * 698728
+    res["C4_layer_step"] = {
+        "shape": [T, N, D],
+        "ms": {"pre_fwd": t[0], "gemm_fwd": t[1], "post_fwd": t[2], "post_bwd": t[3],
+               "gemm_bwd": t[4], "pre_bwd": t[5], "grad_x_sum": t[6]},
+        "mhc_ms": mhc_ms, "mhc_tokens_per_s": T / (mhc_ms / 1e3),
+        "mhc_GB/s": nbytes / (mhc_ms / 1e3) / 1e9,
+        "mhc_frac_of_peak": nbytes / (mhc_ms / 1e3) / 1e9 / peak,
+        "note": "mhc_* = the four mHC ops (698,728 algorithmic B/token); the y.W GEMMs "
+                "(cuBLAS) and the grad_x sum are timed separately",
+    }
+    return res
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -274,6 +364,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_TOK, help="tokens per GPU")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="skip the C1 / C4 measurements reported beside the headline")
     ap.add_argument("--skip-x-scaled", action="store_true",
                     help="opt-in variant: the forward does not write the fp32 x_scaled "
                          "(not the reference contract; the default keeps it)")
@@ -390,6 +482,12 @@ def main():
                        "and the per-token small outputs (activations stay on the device)"}
         del host
 
+    others = None
+    if rank == 0 and world == 1 and not args.no_other_configs:
+        del inp
+        torch.cuda.empty_cache()
+        others = other_configs(M, dev, peak)
+
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, times = cpu_oracle_rate(256, 10.0, 30.0)
@@ -418,6 +516,7 @@ def main():
             "ops": ops, "allreduce_ms": op_ms["allreduce"],
             "gpu_launches": int(launches),
             "clocks": ck, "e2e": e2e, "cpu_baseline": cpu_base,
+            "other_configs": others,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
