@@ -245,6 +245,7 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
       Gx8Cursor c;
       c.init(s0, S);
       uint32_t gi = 0, yi = 0;
+      const uint64_t pol_stream = tc::l2_evict_first(), pol_keep = tc::l2_evict_last();
       for (int64_t gs = s0; gs < s1; ++gs, c.next()) {
         const uint32_t k = (uint32_t)(gs - s0);
         const int row = (int)(c.tile * 128);
@@ -253,24 +254,25 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
           if (!tc::mbar_wait(gempty, (gi & 1) ^ 1, abort_flag)) break;
           tc::mbar_arrive_expect_tx(gfull, G_BYTES);
           for (int a = 0; a < 4; ++a)
-            tc::tma_load_2d(sm + OFF_G + a * G_ATOM, &maps.g, gfull, 64 * a, row);
+            tc::tma_load_2d_hint(sm + OFF_G + a * G_ATOM, &maps.g, gfull, 64 * a, row, pol_keep);
           ++gi;
         }
         if (c.blk_start) {
           if (!tc::mbar_wait(yempty, (yi & 1) ^ 1, abort_flag)) break;
           tc::mbar_arrive_expect_tx(yfull, GY_BYTES);
-          tc::tma_load_2d(sm + OFF_GY, &maps.gy, yfull, c.blk * CB, row);
+          tc::tma_load_2d_hint(sm + OFF_GY, &maps.gy, yfull, c.blk * CB, row, pol_stream);
           ++yi;
         }
         const int pb = k % PS;
         if (!tc::mbar_wait(&pempty[pb], ((k / PS) & 1) ^ 1, abort_flag)) break;
         tc::mbar_arrive_expect_tx(&pfull[pb], P_BYTES);
         for (int a = 0; a < 4; ++a)
-          tc::tma_load_2d(sm + OFF_P + pb * P_BYTES + a * P_ATOM, &maps.p, &pfull[pb], 64 * a, col);
+          tc::tma_load_2d_hint(sm + OFF_P + pb * P_BYTES + a * P_ATOM, &maps.p, &pfull[pb], 64 * a,
+                               col, pol_keep);
         const int s = k % XS;
         if (!tc::mbar_wait(&xempty[s], ((k / XS) & 1) ^ 1, abort_flag)) break;
         tc::mbar_arrive_expect_tx(&xfull[s], X_BYTES);
-        tc::tma_load_2d(sm + OFF_X + s * X_BYTES, &maps.x, &xfull[s], col, row);
+        tc::tma_load_2d_hint(sm + OFF_X + s * X_BYTES, &maps.x, &xfull[s], col, row, pol_stream);
       }
     }
   } else if (warp == 1) {
@@ -473,6 +475,7 @@ bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ pa
   if (warp == 0) {
     if (lane == 0) {
       int64_t ct = s0 / ntiles, tile = s0 - ct * ntiles;
+      const uint64_t pol_stream = tc::l2_evict_first(), pol_keep = tc::l2_evict_last();
       for (int64_t gs = s0; gs < s1; ++gs) {
         const uint32_t k = (uint32_t)(gs - s0);
         const int s = k % S;
@@ -480,9 +483,11 @@ bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ pa
         tc::mbar_arrive_expect_tx(&full[s], STAGE);
         uint8_t* st = sm + s * STAGE;
         for (int b = 0; b < 4; ++b)
-          tc::tma_load_2d(st + b * XBOX, &maps.x, &full[s], (int)(ct * CT + 64 * b), (int)(tile * 128));
+          tc::tma_load_2d_hint(st + b * XBOX, &maps.x, &full[s], (int)(ct * CT + 64 * b),
+                               (int)(tile * 128), pol_stream);
         for (int b = 0; b < 3; ++b)
-          tc::tma_load_2d(st + X_BYTES + b * GBOX, &maps.gp, &full[s], 64 * b, (int)(tile * 128));
+          tc::tma_load_2d_hint(st + X_BYTES + b * GBOX, &maps.gp, &full[s], 64 * b,
+                               (int)(tile * 128), pol_keep);
         if (++tile == ntiles) { tile = 0; ++ct; }
       }
     }

@@ -124,6 +124,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      const uint64_t pol_stream = tc::l2_evict_first(), pol_keep = tc::l2_evict_last();
       for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % S;
@@ -133,10 +134,10 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
             const int col = kc * C::KC + b * C::BOX;
-            tc::tma_load_2d(sA + s * C::A_BYTES + b * C::A_BOX, &tm_x, &full[s], col,
-                            (int)(tile * 128));
-            tc::tma_load_2d(sB + s * C::B_STRIDE + b * C::B_BOX_STRIDE, &tm_phi, &full[s], col,
-                            0);
+            tc::tma_load_2d_hint(sA + s * C::A_BYTES + b * C::A_BOX, &tm_x, &full[s], col,
+                                 (int)(tile * 128), pol_stream);
+            tc::tma_load_2d_hint(sB + s * C::B_STRIDE + b * C::B_BOX_STRIDE, &tm_phi, &full[s],
+                                 col, 0, pol_keep);
           }
         }
       }
