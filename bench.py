@@ -316,7 +316,7 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
     W = (torch.randn(D, D, generator=g, device=dev) / 64.0).to(bf)
     gz = torch.randn(T, N, D, generator=g, device=dev).to(bf)
 
-    def c4(ev):
+    def c4(ev, fused=False):
         rec = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
         rec(0)
         out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
@@ -331,25 +331,38 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
         gy = ghout @ W.t()
         gW = out["y"].t() @ ghout
         rec(5)
-        gxq, gphi, ga, gb = M.mhc_pre_clamp_sinkhorn_backward(
-            x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
-            out["h_res_logits"], out["pre"], gy, ghpost, ghres, **KW)
-        rec(6)
-        gxp.add_(gxq)
+        if fused:
+            # x feeds both ops: the post backward's grad_x is added inside the pre backward
+            M.mhc_pre_clamp_sinkhorn_backward(
+                x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+                out["h_res_logits"], out["pre"], gy, ghpost, ghres, grad_x_accumulate=gxp,
+                **KW)
+            rec(6)
+        else:
+            gxq = M.mhc_pre_clamp_sinkhorn_backward(
+                x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+                out["h_res_logits"], out["pre"], gy, ghpost, ghres, **KW)[0]
+            rec(6)
+            gxp.add_(gxq)
         rec(7)
         return gW
     t = _timed(c4, steps, warmup, 8)
+    tf = _timed(lambda ev: c4(ev, fused=True), steps, warmup, 8)
     mhc_ms = t[0] + t[2] + t[3] + t[5]
     nbytes = T * 698728
     res["C4_layer_step"] = {
         "shape": [T, N, D],
         "ms": {"pre_fwd": t[0], "gemm_fwd": t[1], "post_fwd": t[2], "post_bwd": t[3],
                "gemm_bwd": t[4], "pre_bwd": t[5], "grad_x_sum": t[6]},
+        "fused_grad_x_sum": {"pre_bwd_with_grad_x_accumulate": tf[5],
+                             "saves_ms": t[5] + t[6] - tf[5]},
         "mhc_ms": mhc_ms, "mhc_tokens_per_s": T / (mhc_ms / 1e3),
         "mhc_GB/s": nbytes / (mhc_ms / 1e3) / 1e9,
         "mhc_frac_of_peak": nbytes / (mhc_ms / 1e3) / 1e9 / peak,
         "note": "mhc_* = the four mHC ops (698,728 algorithmic B/token); the y.W GEMMs "
-                "(cuBLAS) and the grad_x sum are timed separately",
+                "(cuBLAS) and the torch grad_x sum are timed separately; fused_grad_x_sum "
+                "runs the same step with the post backward's grad_x added inside the pre "
+                "backward (grad_x_accumulate) instead of the torch sum",
     }
     return res
 

@@ -50,6 +50,9 @@ _SIGS = {
     "mhc_pre_bwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp, _i64, _i32,
                                    _i64, _i32, _f32, _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp,
                                    _vp, _sz, _vp]),
+    "mhc_pre_bwd_accumulate": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp,
+                                              _i64, _i32, _i64, _i32, _f32, _f32, _f32, _f32,
+                                              _i32, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
 }
 
 

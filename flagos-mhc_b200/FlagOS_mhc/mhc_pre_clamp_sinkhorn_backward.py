@@ -17,7 +17,8 @@ from .mhc_pre_clamp_sinkhorn import _check_params
 
 def mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, inv_rms, x_scaled, mixes, h_res_logits,
                                     pre, grad_y, grad_post_out, grad_comb_frag, norm_eps=1e-6,
-                                    hc_eps=1e-6, clamp_min=0.0, clamp_max=0.0, iter_times=20):
+                                    hc_eps=1e-6, clamp_min=0.0, clamp_max=0.0, iter_times=20,
+                                    grad_x_accumulate=None):
     """Returns (grad_x, grad_phi, grad_alpha, grad_base).
 
     Reference: ``mhc_pre_clamp_sinkhorn_backward``
@@ -25,6 +26,11 @@ def mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, inv_rms, x_scaled, mixe
     ``h_res_logits`` are accepted for signature compatibility and not read
     (the reference does not read ``h_res_logits`` either, :1301): the kernels
     use ``grad_phi = (inv_rms*grad_mixes)^T x``, which needs no fp32 copy of x.
+
+    ``grad_x_accumulate`` (an addition to the reference API, optional): a tensor of x's
+    shape whose values are added to grad_x inside the kernel (fp32 sum, rounded once).
+    A layer whose x also feeds ``mhc_post`` passes the post backward's grad_x here
+    instead of letting autograd add the two gradients in a separate pass.
     """
     if x.dim() == 4:
         B, S, N, D = x.shape
@@ -52,6 +58,11 @@ def mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, inv_rms, x_scaled, mixe
     inv_f, mixes_f, pre_f = f(inv_rms.reshape(T)), f(mixes.reshape(T, hc_mix)), f(pre.reshape(T, N))
     gpost_f, gcomb_f = f(grad_post_out.reshape(T, N)), f(grad_comb_frag.reshape(T, N, N))
     grad_x = torch.empty(T, N, D, dtype=xf.dtype, device=dev)
+    acc = None
+    if grad_x_accumulate is not None:
+        assert grad_x_accumulate.numel() == T * N * D, "grad_x_accumulate must have x's shape"
+        acc = grad_x_accumulate.reshape(T, N, D).to(xf.dtype).contiguous()
+        _C.require_cuda(acc)
     n_phi = hc_mix * hc_d
     packed = torch.empty(n_phi + 3 + hc_mix, dtype=torch.float32, device=dev)
     grad_phi = packed[:n_phi].view(hc_mix, hc_d)
@@ -62,12 +73,16 @@ def mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, inv_rms, x_scaled, mixe
     with torch.cuda.device(dev):
         ws_bytes = L.mhc_pre_bwd_workspace_bytes(T, N, D, code, int(iter_times))
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-        st = L.mhc_pre_bwd(_C.ptr(xf), _C.ptr(phi_f), _C.ptr(alpha_f), _C.ptr(base_f),
-                           _C.ptr(inv_f), _C.ptr(mixes_f), _C.ptr(pre_f), _C.ptr(gy),
-                           _C.ptr(gpost_f), _C.ptr(gcomb_f), T, N, D, code, float(norm_eps),
-                           float(hc_eps), float(clamp_min), float(clamp_max), int(iter_times),
-                           _C.ptr(grad_x), _C.ptr(grad_phi), _C.ptr(grad_alpha),
-                           _C.ptr(grad_base), _C.ptr(ws), ws_bytes, _C.stream_of(xf))
+        head = (_C.ptr(xf), _C.ptr(phi_f), _C.ptr(alpha_f), _C.ptr(base_f), _C.ptr(inv_f),
+                _C.ptr(mixes_f), _C.ptr(pre_f), _C.ptr(gy), _C.ptr(gpost_f), _C.ptr(gcomb_f),
+                T, N, D, code, float(norm_eps), float(hc_eps), float(clamp_min),
+                float(clamp_max), int(iter_times))
+        tail = (_C.ptr(grad_x), _C.ptr(grad_phi), _C.ptr(grad_alpha), _C.ptr(grad_base),
+                _C.ptr(ws), ws_bytes, _C.stream_of(xf))
+        if acc is None:
+            st = L.mhc_pre_bwd(*head, *tail)
+        else:
+            st = L.mhc_pre_bwd_accumulate(*head, _C.ptr(acc), *tail)
     _C.check(st, "mhc_pre_clamp_sinkhorn_backward")
     return (grad_x.to(gx_dtype).view(x.shape), grad_phi.view(phi.shape), grad_alpha, grad_base)
 

@@ -173,14 +173,16 @@ size_t mhc_pre_bwd_workspace_bytes(int64_t T, int32_t N, int64_t D, int32_t dtyp
   return pre_bwd_ws_bytes(T, N, D, dtype, iter_times);
 }
 
-int mhc_pre_bwd(const void* x, const float* phi, const float* alpha, const float* base,
-                const float* inv_rms, const float* mixes, const float* pre, const void* grad_y,
-                const float* grad_post_out, const float* grad_comb_frag, int64_t T, int32_t N,
-                int64_t D, int32_t dtype, float norm_eps, float hc_eps, float clamp_min,
-                float clamp_max, int32_t iter_times, void* grad_x, float* grad_phi,
-                float* grad_alpha, float* grad_base, void* workspace, size_t workspace_bytes,
-                void* stream) {
-  (void)norm_eps;  // inv_rms arrives precomputed
+}  // extern "C"
+
+static int pre_bwd_entry(const void* x, const float* phi, const float* alpha, const float* base,
+                         const float* inv_rms, const float* mixes, const float* pre,
+                         const void* grad_y, const float* grad_post_out,
+                         const float* grad_comb_frag, int64_t T, int32_t N, int64_t D,
+                         int32_t dtype, float hc_eps, float clamp_min, float clamp_max,
+                         int32_t iter_times, const void* grad_x_acc, void* grad_x,
+                         float* grad_phi, float* grad_alpha, float* grad_base, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   RETURN_IF(check_common(T, N, D, dtype));
   PreBwdArgs a{};
   RETURN_IF(small_params(hc_eps, clamp_min, clamp_max, iter_times, &a.sp));
@@ -198,8 +200,41 @@ int mhc_pre_bwd(const void* x, const float* phi, const float* alpha, const float
   a.pre = pre; a.grad_y = grad_y; a.grad_post = grad_post_out; a.grad_comb = grad_comb_frag;
   a.T = T; a.D = D; a.N = N; a.dtype = dtype;
   a.grad_x = grad_x; a.grad_phi = grad_phi; a.grad_alpha = grad_alpha; a.grad_base = grad_base;
+  a.grad_x_acc = grad_x_acc;
   a.workspace = workspace; a.workspace_bytes = workspace_bytes;
   return pre_bwd_dispatch(a, (cudaStream_t)stream);
+}
+
+extern "C" {
+
+int mhc_pre_bwd(const void* x, const float* phi, const float* alpha, const float* base,
+                const float* inv_rms, const float* mixes, const float* pre, const void* grad_y,
+                const float* grad_post_out, const float* grad_comb_frag, int64_t T, int32_t N,
+                int64_t D, int32_t dtype, float norm_eps, float hc_eps, float clamp_min,
+                float clamp_max, int32_t iter_times, void* grad_x, float* grad_phi,
+                float* grad_alpha, float* grad_base, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  (void)norm_eps;  // inv_rms arrives precomputed
+  return pre_bwd_entry(x, phi, alpha, base, inv_rms, mixes, pre, grad_y, grad_post_out,
+                       grad_comb_frag, T, N, D, dtype, hc_eps, clamp_min, clamp_max, iter_times,
+                       nullptr, grad_x, grad_phi, grad_alpha, grad_base, workspace,
+                       workspace_bytes, stream);
+}
+
+int mhc_pre_bwd_accumulate(const void* x, const float* phi, const float* alpha,
+                           const float* base, const float* inv_rms, const float* mixes,
+                           const float* pre, const void* grad_y, const float* grad_post_out,
+                           const float* grad_comb_frag, int64_t T, int32_t N, int64_t D,
+                           int32_t dtype, float norm_eps, float hc_eps, float clamp_min,
+                           float clamp_max, int32_t iter_times, const void* grad_x_accumulate,
+                           void* grad_x, float* grad_phi, float* grad_alpha, float* grad_base,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  (void)norm_eps;
+  if (T > 0 && !grad_x_accumulate) return MHC_ERR_INVALID_ARGUMENT;
+  return pre_bwd_entry(x, phi, alpha, base, inv_rms, mixes, pre, grad_y, grad_post_out,
+                       grad_comb_frag, T, N, D, dtype, hc_eps, clamp_min, clamp_max, iter_times,
+                       grad_x_accumulate, grad_x, grad_phi, grad_alpha, grad_base, workspace,
+                       workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(kGxCC)
 pre_bwd_gx_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                   const float* __restrict__ phi, const float* __restrict__ gm,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
-                  const float* __restrict__ pre, E* __restrict__ gx, int64_t T, int64_t D) {
+                  const float* __restrict__ pre, const E* acc, E* gx,  // may alias
+                  int64_t T, int64_t D) {
   constexpr int HM = hc_mix(N);
   const int64_t HC = (int64_t)N * D;
   __shared__ float sgm[kGxTT][HM];
@@ -292,7 +293,9 @@ pre_bwd_gx_kernel(const E* __restrict__ x, const E* __restrict__ gy,
     const float xv = ld1<E>(x + t * HC + c);
     const float g = ld1<E>(gy + t * D + d);
     const float r = fmaf(sinv[tt], gxs, -scoef[tt] * xv);
-    st1<E>(gx + t * HC + c, fmaf(g, spre[tt][n], r));
+    float v = fmaf(g, spre[tt][n], r);
+    if (acc) v += ld1<E>(acc + t * HC + c);
+    st1<E>(gx + t * HC + c, v);
   }
 }
 
@@ -408,9 +411,10 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const int64_t T = a.T, D = a.D, HC = (int64_t)N * D;
   BwdWs w = bwd_layout((char*)a.workspace, T, N, D, a.sp.iters);
   const int nblk = (int)cdiv(T, 128);
-  const bool use_tc = std::is_same<E, __nv_bfloat16>::value &&
+  const bool acc_ok = a.grad_x_acc == nullptr || aligned16(a.grad_x_acc);
+  const bool use_tc = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
                       pre_bwd_tc_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
-  const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value &&
+  const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
                        pre_bwd_tc8_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
   char* tc_ws = (char*)a.workspace + w.total;
   __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr;
@@ -444,7 +448,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   pre_bwd_gx_kernel<E, N><<<ggrid, kGxCC, 0, s>>>((const E*)a.x, (const E*)a.grad_y, a.phi,
                                                   w.gm, a.inv_rms, w.coef, a.pre,
-                                                  (E*)a.grad_x, T, D);
+                                                  (const E*)a.grad_x_acc, (E*)a.grad_x, T, D);
   MHC_LAUNCH_CHECK();
   const int ns = gphi_splits(T);
   const int64_t tps = cdiv(T, ns);

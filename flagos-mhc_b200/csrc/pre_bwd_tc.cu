@@ -71,7 +71,7 @@ constexpr int OFF_GP = OFF_G1 + G1_BYTES;
 constexpr int OFF_X = OFF_GP + GP_BYTES;
 constexpr int OFF_OUT = OFF_X + XS * X_BYTES;
 constexpr int OFF_BAR = OFF_OUT + EPI_WARPS * OUT_BYTES;
-constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr int SMEM = 1024 + OFF_BAR + 512;
 static_assert(SMEM <= 232448, "shared memory");
 static_assert(P_BYTES % 1024 == 0 && OFF_X % 1024 == 0 && OFF_OUT % 1024 == 0, "alignment");
 // TMEM columns: D2[n] (grad_phi, 64 each) at n*64, D1[b] (gxs, 128 each) at 256 + b*128
@@ -79,7 +79,7 @@ constexpr int TMEM_COLS = 512;
 }  // namespace bwdtc
 
 struct BwdTcMaps {
-  CUtensorMap x, g0, g1, gp, p0, p1, gx;
+  CUtensorMap x, g0, g1, gp, p0, p1, gx, gxa;
 };
 
 // A cell is `subt` consecutive token tiles of one column group; subt never exceeds the
@@ -119,6 +119,7 @@ struct ItemCursor {
   }
 };
 
+template <bool ACC>
 __global__ void __launch_bounds__(bwdtc::THREADS, 1)
 pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
@@ -144,7 +145,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
   uint64_t* tdone = gfull + 12;
   uint64_t* gpfull = gfull + 13;     // GP (grad_phi operand) of an item landed
   uint64_t* gpempty = gfull + 14;    // the item's grad_phi MMAs are done with GP
-  uint32_t* tmem_slot = (uint32_t*)(gfull + 15);
+  uint64_t* accbar = gfull + 15;     // [EPI_WARPS] the warp's grad_x_acc box landed
+  uint32_t* tmem_slot = (uint32_t*)(gfull + 15 + EPI_WARPS);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -172,6 +174,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     tc::mbar_init(d2full, 1);
     tc::mbar_init(d2empty, EPI_WARPS);
     tc::mbar_init(tdone, 1);
+    for (int w = 0; w < EPI_WARPS; ++w) tc::mbar_init(&accbar[w], 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -335,6 +338,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;            // token row (D1) / column row (D2)
     uint8_t* ob = sm + OFF_OUT + (warp - 2) * OUT_BYTES;
+    uint64_t* mybar = &accbar[warp - 2];
+    uint32_t ai = 0;  // grad_x_acc boxes this warp loaded
     uint32_t di = 0, seg = 0;
     bool first_seg = true;
     ItemCursor cur;
@@ -372,6 +377,14 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
       for (int n = 0; n < N; ++n, ++di) {
         const int e = di & 1, s = di % XS;
         const uint32_t xph = (di / XS) & 1;
+        // accumulate mode: this warp's grad_x_acc box goes into its output buffer (once
+        // the previous grad_x store has read it), overlapping the waits below
+        const bool ld_acc = ACC && row0 < T;
+        if (ld_acc && lane == 0) {
+          tc::bulk_wait_read<0>();
+          tc::mbar_arrive_expect_tx(mybar, OUT_BYTES);
+          tc::tma_load_2d(ob, &maps.gxa, mybar, (int)(n * D + d0 + h * 32), (int)row0);
+        }
         if (!__all_sync(0xffffffffu, TW(0, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag)))) {
           ok = false;
           break;
@@ -409,6 +422,13 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         const int osw = (lane >> 1) & 3;
         if (lane == 0) tc::bulk_wait_read<0>();
         __syncwarp();
+        if (ld_acc) {
+          if (!__all_sync(0xffffffffu, tc::mbar_wait(mybar, ai & 1, abort_flag))) {
+            ok = false;
+            break;
+          }
+          ++ai;
+        }
         const float prn = pr[n];
         const float2 pr2 = make_float2(prn, prn), inv2 = make_float2(inv, inv),
                      ncf2 = make_float2(-cf, -cf);
@@ -437,6 +457,13 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
               const float2 oo = __ffma2_rn(make_float2(gf[u], gf[u + 1]), pr2, rr);
               o[u] = oo.x;
               o[u + 1] = oo.y;
+            }
+            if (ld_acc) {
+              float a8[8];
+              widen<__nv_bfloat16>(
+                  *reinterpret_cast<const uint4*>(orow + (((2 * jp + jj) ^ osw) << 4)), a8);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) o[u] += a8[u];
             }
             ov[jj] = narrow<__nv_bfloat16>(o);
           }
@@ -658,15 +685,23 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
   if ((st = make_tmap_2d(&m.gx, a.grad_x, bf, 2, HC, T, HC * 2, 32, 32,
                          CU_TENSOR_MAP_SWIZZLE_64B)))
     return st;
+  m.gxa = m.gx;
+  if (a.grad_x_acc &&
+      (st = make_tmap_2d(&m.gxa, a.grad_x_acc, bf, 2, HC, T, HC * 2, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_64B)))
+    return st;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel<false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel<true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr_set[dev] = true;
   }
-  pre_bwd_tc_kernel<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
+  auto kern = a.grad_x_acc ? pre_bwd_tc_kernel<true> : pre_bwd_tc_kernel<false>;
+  kern<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
                                                     (__nv_bfloat16*)a.grad_x, w.part, T, D, geo,
 #ifdef MHC_PROFILE_WAITS

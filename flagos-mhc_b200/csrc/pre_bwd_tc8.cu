@@ -56,7 +56,7 @@ constexpr int OFF_X = OFF_P + PS * P_BYTES;
 constexpr int OFF_GY = OFF_X + XS * X_BYTES;
 constexpr int OFF_OUT = OFF_GY + GY_BYTES;
 constexpr int OFF_BAR = OFF_OUT + EPI_WARPS * OUT_BYTES;
-constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr int SMEM = 1024 + OFF_BAR + 512;
 constexpr int TMEM_COLS = 128;             // D1[2] x 64 columns
 static_assert(SMEM <= 232448, "shared memory");
 }  // namespace gx
@@ -149,7 +149,7 @@ __global__ void bwd8_g_prep_kernel(const float* __restrict__ gm, const float* __
 }
 
 struct Bwd8GxMaps {
-  CUtensorMap x, gy, g, p, gx;
+  CUtensorMap x, gy, g, p, gx, gxa;
 };
 
 // Step cursor of the gx kernel: step = (token tile, column block b, sub-chunk n) with n
@@ -174,6 +174,7 @@ struct Gx8Cursor {
   }
 };
 
+template <bool ACC>
 __global__ void __launch_bounds__(bwd8::gx::THREADS, 1)
 bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict__ inv_rms,
                const float* __restrict__ coef, const float* __restrict__ pre, int64_t T,
@@ -194,7 +195,8 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
   uint64_t* yfull = gfull + 2;
   uint64_t* yempty = gfull + 3;       // epilogue warps read the grad_y block
   uint64_t* tdone = gfull + 4;
-  uint32_t* tmem_slot = (uint32_t*)(gfull + 5);
+  uint64_t* accbar = gfull + 5;       // [EPI_WARPS] the warp's grad_x_acc box landed
+  uint32_t* tmem_slot = (uint32_t*)(gfull + 5 + EPI_WARPS);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -220,6 +222,7 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
     tc::mbar_init(yfull, 1);
     tc::mbar_init(yempty, EPI_WARPS);
     tc::mbar_init(tdone, 1);
+    for (int w = 0; w < EPI_WARPS; ++w) tc::mbar_init(&accbar[w], 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -320,6 +323,8 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
     uint8_t* ob = sm + OFF_OUT + (warp - 2) * OUT_BYTES;
     uint8_t* orow = ob + lane * 64;
     const int osw = (lane >> 1) & 3;
+    uint64_t* mybar = &accbar[warp - 2];
+    uint32_t ai = 0;  // grad_x_acc boxes this warp loaded
     Gx8Cursor c;
     c.init(s0, S);
     uint32_t yi = 0;
@@ -335,6 +340,15 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
       }
       const float prn = live ? pre[t * N + c.n] : 0.f;
       const int e = k & 1, s = k % XS;
+      // accumulate mode: this warp's grad_x_acc box goes into its output buffer (once the
+      // previous grad_x store has read it), overlapping the waits below
+      const int64_t row0 = c.tile * 128 + q * 32;
+      const bool ld_acc = ACC && row0 < T;
+      if (ld_acc && lane == 0) {
+        tc::bulk_wait_read<0>();
+        tc::mbar_arrive_expect_tx(mybar, OUT_BYTES);
+        tc::tma_load_2d(ob, &maps.gxa, mybar, (int)(c.n * D + c.blk * CB + hh * 32), (int)row0);
+      }
       if (!__all_sync(0xffffffffu, tc::mbar_wait(&d1full[e], (k >> 1) & 1, abort_flag))) break;
       tc::tc_fence_after();
       // row r, columns [32hh, 32hh+32) of a [128][64] 128B-swizzled tile
@@ -361,6 +375,10 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
       }
       if (c.blk_start) ++yi;
       __syncwarp();
+      if (ld_acc) {
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(mybar, ai & 1, abort_flag))) break;
+        ++ai;
+      }
       const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + e * CB + hh * 32;
       const float2 pr2 = make_float2(prn, prn), inv2 = make_float2(inv, inv),
                    ncf2 = make_float2(-cf, -cf);
@@ -389,12 +407,17 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
             o[u] = oo.x;
             o[u + 1] = oo.y;
           }
+          if (ld_acc) {
+            float a8[8];
+            widen<__nv_bfloat16>(*reinterpret_cast<const uint4*>(orow + ((jv ^ osw) << 4)), a8);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) o[u] += a8[u];
+          }
           *reinterpret_cast<uint4*>(orow + ((jv ^ osw) << 4)) = narrow<__nv_bfloat16>(o);
         }
       }
       tc::fence_proxy_async();  // generic smem writes -> TMA store reads
       __syncwarp();
-      const int64_t row0 = c.tile * 128 + q * 32;
       if (lane == 0 && row0 < T) {
         tc::tma_store_2d(&maps.gx, ob, (int)(c.n * D + c.blk * CB + hh * 32), (int)row0);
         tc::bulk_commit_group();
@@ -681,6 +704,11 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   if ((st = make_tmap_2d(&mx.gx, a.grad_x, bf, 2, HC, T, HC * 2, 32, 32,
                          CU_TENSOR_MAP_SWIZZLE_64B)))
     return st;
+  mx.gxa = mx.gx;
+  if (a.grad_x_acc &&
+      (st = make_tmap_2d(&mx.gxa, a.grad_x_acc, bf, 2, HC, T, HC * 2, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_64B)))
+    return st;
   Bwd8GpMaps mp;
   if ((st = make_tmap_2d(&mp.x, a.x, bf, 2, HC, T, HC * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
@@ -692,7 +720,9 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel<false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, gx::SMEM));
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel<true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, gx::SMEM));
     MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gphi_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, gp::SMEM));
@@ -701,7 +731,8 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   const int64_t total_gx = geo.ntiles * (HC / CB);
   int ngx = sm_count();
   if (total_gx < ngx) ngx = (int)total_gx;
-  bwd8_gx_kernel<<<ngx, gx::THREADS, gx::SMEM, s>>>(mx, a.inv_rms, coef, a.pre, T, D, total_gx);
+  auto kgx = a.grad_x_acc ? bwd8_gx_kernel<true> : bwd8_gx_kernel<false>;
+  kgx<<<ngx, gx::THREADS, gx::SMEM, s>>>(mx, a.inv_rms, coef, a.pre, T, D, total_gx);
   MHC_LAUNCH_CHECK();
   bwd8_gphi_kernel<<<geo.grid_gp, gp::THREADS, gp::SMEM, s>>>(mp, w.part, geo.ntiles,
                                                               geo.total_gp, geo.maxslot);

@@ -40,6 +40,7 @@ struct PreBwdArgs {
   int32_t N, dtype;
   SmallParams sp;
   void* grad_x;
+  const void* grad_x_acc;  // optional: grad_x = this op's contribution + grad_x_acc
   float* grad_phi;
   float* grad_alpha;
   float* grad_base;

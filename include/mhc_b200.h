@@ -140,6 +140,27 @@ int mhc_pre_bwd(const void* x, const float* phi, const float* alpha,
                 float* grad_alpha, float* grad_base, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/*
+ * mhc_pre_bwd_accumulate -- mhc_pre_bwd that adds an existing gradient into
+ * grad_x: grad_x = (this operator's grad_x, fp32) + grad_x_accumulate, rounded
+ * once to dtype.  No counterpart in the reference, whose callers let autograd
+ * add the post and pre contributions to x's gradient in a separate pass (three
+ * more x-sized transfers); src/autograd.py:14-87 is where that sum arises.
+ * grad_x_accumulate has grad_x's shape and dtype and may be the same buffer
+ * as grad_x (in-place accumulation).  Everything else is as mhc_pre_bwd.
+ */
+int mhc_pre_bwd_accumulate(const void* x, const float* phi, const float* alpha,
+                           const float* base, const float* inv_rms,
+                           const float* mixes, const float* pre,
+                           const void* grad_y, const float* grad_post_out,
+                           const float* grad_comb_frag, int64_t T, int32_t N,
+                           int64_t D, int32_t dtype, float norm_eps,
+                           float hc_eps, float clamp_min, float clamp_max,
+                           int32_t iter_times, const void* grad_x_accumulate,
+                           void* grad_x, float* grad_phi, float* grad_alpha,
+                           float* grad_base, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Size of the static device scratch array used by mhc_pre_fwd_noalloc. */
 #define MHC_PRE_FWD_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -343,3 +343,48 @@ def test_pre_bwd_n8_tensor_core(T, D):
         assert rel_err(a, b) <= TOL_FP32, name
     from FlagOS_mhc import _C
     assert _C.lib().mhc_device_status() == 0
+
+
+@pytest.mark.parametrize("T,N,D,dt", [(300, 4, 256, torch.bfloat16), (300, 8, 128, torch.bfloat16),
+                                      (37, 4, 100, torch.bfloat16), (130, 4, 64, torch.float32)])
+def test_pre_bwd_grad_x_accumulate(T, N, D, dt):
+    """grad_x_accumulate (layer fusion: the post backward's grad_x added inside the pre
+    backward): grad_x = own contribution + accumulator, rounded once; the parameter
+    gradients are bitwise those of the plain call; the C entry point may run in place."""
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, dt, seed=T + N + D,
+                                                       phi_std=1.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    out = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True, **kw)
+    args = (d[0], d[1], d[2], d[3], out["inv_rms"], out["x_scaled"], out["mixes"],
+            out["h_res_logits"], out["pre"], d[4], d[5], d[6])
+    g = torch.Generator().manual_seed(7)
+    acc = torch.randn(T, N, D, generator=g).to(dt).to(DEV)
+    plain = M.mhc_pre_clamp_sinkhorn_backward(*args, **kw)
+    fused = M.mhc_pre_clamp_sinkhorn_backward(*args, grad_x_accumulate=acc, **kw)
+    for u, v in zip(plain[1:], fused[1:]):
+        assert torch.equal(u, v)
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=-10.0, clamp_max=10.0, iter_times=20, dtype=F64)
+    ref = want[0].to(F64) + acc.cpu().to(F64)
+    assert rel_err(fused[0], ref) <= _tol(dt)
+    # in place through the C ABI: grad_x and the accumulator are one buffer
+    from FlagOS_mhc import _C
+    L = _C.lib()
+    code = _C.dtype_code(dt)
+    f32 = lambda t: t.float().contiguous()  # noqa: E731
+    buf = acc.clone()
+    ws_bytes = L.mhc_pre_bwd_workspace_bytes(T, N, D, code, 20)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=DEV)
+    gphi = torch.empty_like(plain[1]); ga = torch.empty(3, device=DEV); gb = torch.empty_like(plain[3])
+    st = L.mhc_pre_bwd_accumulate(
+        _C.ptr(d[0]), _C.ptr(f32(d[1])), _C.ptr(f32(d[2])), _C.ptr(f32(d[3])),
+        _C.ptr(out["inv_rms"]), _C.ptr(out["mixes"]), _C.ptr(out["pre"]), _C.ptr(d[4]),
+        _C.ptr(d[5]), _C.ptr(d[6]), T, N, D, code, 1e-6, 1e-6, -10.0, 10.0, 20,
+        _C.ptr(buf), _C.ptr(buf), _C.ptr(gphi), _C.ptr(ga), _C.ptr(gb), _C.ptr(ws), ws_bytes,
+        _C.stream_of(d[0]))
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(buf, fused[0])
+    assert L.mhc_device_status() == 0
