@@ -281,10 +281,13 @@ __device__ __forceinline__ void widen2(uint32_t w, float* f) {
 // V 16-byte packs per lane and row per step (V = 2: 32-byte accesses, 64-wide steps)
 template <int V>
 __device__ __forceinline__ void ld_row_packs(const void* p, uint32_t (&r)[4 * V]) {
-  if constexpr (V == 2) {
-    const U8 v = ld_global_32B(p);
-    r[0] = v.a.x; r[1] = v.a.y; r[2] = v.a.z; r[3] = v.a.w;
-    r[4] = v.b.x; r[5] = v.b.y; r[6] = v.b.z; r[7] = v.b.w;
+  if constexpr (V >= 2) {
+#pragma unroll
+    for (int h = 0; h < V / 2; ++h) {
+      const U8 v = ld_global_32B((const char*)p + 32 * h);
+      r[8 * h + 0] = v.a.x; r[8 * h + 1] = v.a.y; r[8 * h + 2] = v.a.z; r[8 * h + 3] = v.a.w;
+      r[8 * h + 4] = v.b.x; r[8 * h + 5] = v.b.y; r[8 * h + 6] = v.b.z; r[8 * h + 7] = v.b.w;
+    }
   } else {
     const uint4 v = ld_stream(p);
     r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
@@ -292,8 +295,13 @@ __device__ __forceinline__ void ld_row_packs(const void* p, uint32_t (&r)[4 * V]
 }
 template <typename E, int V>
 __device__ __forceinline__ void st_row_packs(void* p, const float* o) {
-  if constexpr (V == 2) st_global_32B(p, narrow<E>(o), narrow<E>(o + 8));
-  else st_stream(p, narrow<E>(o));
+  if constexpr (V >= 2) {
+#pragma unroll
+    for (int h = 0; h < V / 2; ++h)
+      st_global_32B((char*)p + 32 * h, narrow<E>(o + 16 * h), narrow<E>(o + 16 * h + 8));
+  } else {
+    st_stream(p, narrow<E>(o));
+  }
 }
 
 template <typename E, int V>
@@ -419,6 +427,12 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
   const bool vec = (D % Pack<E>::n == 0) && aligned16(x) && aligned16(h_out) && aligned16(out);
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 8) {
+    if (D % 128 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
+      post_fwd_n8_kernel<E, 4><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
+                                                      h_post, (E*)out, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
     if (D % 64 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
       post_fwd_n8_kernel<E, 2><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
                                                       h_post, (E*)out, T, D);
@@ -458,6 +472,14 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
                    aligned16(h_out) && aligned16(gx) && aligned16(ghout);
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 8) {
+    if (D % 128 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
+        aligned32(ghout)) {
+      post_bwd_n8_kernel<E, 4><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+                                                      (const E*)h_out, h_post, (E*)gx, ghres,
+                                                      (E*)ghout, ghpost, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
     if (D % 64 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
         aligned32(ghout)) {
       post_bwd_n8_kernel<E, 2><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,

@@ -58,7 +58,7 @@ def test_pre_golden(path):
 
 
 # ---------------------------------------------------------------- oracle sweeps
-POST_SHAPES = [(1, 4, 64), (3, 4, 7168), (63, 4, 200), (65, 4, 1000), (37, 8, 256), (300, 8, 4096), (29, 8, 96),
+POST_SHAPES = [(1, 4, 64), (3, 4, 7168), (63, 4, 200), (65, 4, 1000), (37, 8, 256), (300, 8, 4096), (29, 8, 96), (21, 8, 192),
                (17, 1, 48), (9, 2, 24), (11, 3, 40), (7, 5, 72), (6, 6, 96), (5, 7, 80),
                (40, 4, 1), (13, 4, 7)]
 
