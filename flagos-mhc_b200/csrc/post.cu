@@ -411,6 +411,88 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
   }
 }
 
+// N = 4, 16-bit storage: the N=8 scheme with two tokens per warp.  Lane (g, c) owns row
+// g & 3 of token 2p + g/4; the mma rows 0-3 / 4-7 are the two tokens' rows, rows 8 and 12
+// their h_out (grad_h_post) or h_post (grad_h_out).  grad_x takes a block-diagonal A
+// (each token's h_res hi | lo against its own grad_y rows); the dot products of rows of
+// different tokens come out of the same MMAs and are dropped.
+template <typename E, int V>
+__global__ void __launch_bounds__(256)
+post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
+                     const float* __restrict__ h_res, const E* __restrict__ h_out,
+                     const float* __restrict__ h_post, E* __restrict__ gx,
+                     float* __restrict__ ghres, E* __restrict__ ghout,
+                     float* __restrict__ ghpost, int64_t T, int64_t D) {
+  constexpr int N = 4, R = 4 * V;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int tb = g >> 2, j = g & 3;            // token of the pair, row of the token
+  const bool mine = (c >> 1) == tb;            // mma columns 2c, 2c+1 belong to this token
+  const bool hrow = j == 0;                    // lanes holding row 8 / 12 (h_out, h_post)
+  const int i0 = (2 * c) & 3;                  // those columns' index within the token
+  const int64_t npairs = (T + 1) / 2;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t p = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < npairs;
+       p += nwarps) {
+    const int64_t t = 2 * p + tb;
+    const bool live = t < T;
+    uint32_t a[4] = {0u, 0u, 0u, 0u};
+    if (live && mine) {
+      const float* hr = h_res + t * N * N + j * N + i0;
+      split_e2<E>(__ldg(hr), __ldg(hr + 1), a[0], a[2]);
+      if (hrow) split_e2<E>(__ldg(h_post + t * N + i0), __ldg(h_post + t * N + i0 + 1), a[1], a[3]);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int64_t row = live ? (t * N + j) * D : 0;
+    const E* xr = x + row;
+    const E* gyr = gy + row;
+    const E* ht = h_out + (live ? t * D : 0);
+    E* gxr = gx + row;
+    E* ght = ghout + (live ? t * D : 0);
+#pragma unroll 2
+    for (int64_t d0 = 8 * V * c; d0 < D; d0 += 32 * V) {
+      uint32_t xv[R], gv[R], hv[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) xv[r] = gv[r] = hv[r] = 0u;
+      if (live) {
+        ld_row_packs<V>(xr + d0, xv);
+        ld_row_packs<V>(gyr + d0, gv);
+        if (hrow) ld_row_packs<V>(ht + d0, hv);
+      }
+      float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int sl = 0; sl < R / 2; ++sl) {
+        const uint32_t as[4] = {xv[2 * sl], hv[2 * sl], xv[2 * sl + 1], hv[2 * sl + 1]};
+        mma16816<E>(dd, as, gv[2 * sl], gv[2 * sl + 1], dd[0], dd[1], dd[2], dd[3]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += dd[u];
+      float o[2 * R], oh[2 * R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t b = movtrans(gv[r]);
+        float cc[4];
+        mma16816<E>(cc, a, b, b, 0.f, 0.f, 0.f, 0.f);
+        o[2 * r] = cc[0];
+        o[2 * r + 1] = cc[1];
+        oh[2 * r] = cc[2];
+        oh[2 * r + 1] = cc[3];
+      }
+      if (live) {
+        st_row_packs<E, V>(gxr + d0, o);
+        if (hrow) st_row_packs<E, V>(ght + d0, oh);
+      }
+    }
+    if (live && mine) {
+      ghres[t * N * N + j * N + i0] = acc[0];
+      ghres[t * N * N + j * N + i0 + 1] = acc[1];
+      if (hrow) {
+        ghpost[t * N + i0] = acc[2];
+        ghpost[t * N + i0 + 1] = acc[3];
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
@@ -471,6 +553,25 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
   const bool vec = (D % Pack<E>::n == 0) && aligned16(gy) && aligned16(x) &&
                    aligned16(h_out) && aligned16(gx) && aligned16(ghout);
   dim3 grid(post_grid(T)), block(256);
+  if constexpr (sizeof(E) == 2 && N == 4) {
+    const bool a32 = aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
+                     aligned32(ghout);
+    dim3 pgrid(post_grid((T + 1) / 2));
+    if (D % 128 == 0 && a32) {
+      post_bwd_n4x2_kernel<E, 4><<<pgrid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+                                                         (const E*)h_out, h_post, (E*)gx, ghres,
+                                                         (E*)ghout, ghpost, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
+    if (D % 64 == 0 && a32) {
+      post_bwd_n4x2_kernel<E, 2><<<pgrid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+                                                         (const E*)h_out, h_post, (E*)gx, ghres,
+                                                         (E*)ghout, ghpost, T, D);
+      MHC_LAUNCH_CHECK();
+      return MHC_OK;
+    }
+  }
   if constexpr (sizeof(E) == 2 && N == 8) {
     if (D % 128 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
         aligned32(ghout)) {
