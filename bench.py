@@ -532,7 +532,7 @@ def main():
                        + (", packed grad_phi NCCL all-reduce" if world > 1 else ""),
                        "l2": "no flush: every step streams ~21 GB, x alone is 1.88 GB > 126 MB L2"},
             "hbm_frac_step": step_bytes / (ms_step / 1e3) / 1e9 / peak,
-            "roofline": {"bound": "hbm", "kernel": "post_bwd_kernel", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "post_bwd_n4x2_kernel", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "algorithmic_bytes": ab[dom], "traffic": traffic},
             "ops": ops, "allreduce_ms": op_ms["allreduce"],
