@@ -388,3 +388,24 @@ def test_pre_bwd_grad_x_accumulate(T, N, D, dt):
     torch.cuda.synchronize()
     assert torch.equal(buf, fused[0])
     assert L.mhc_device_status() == 0
+
+
+@pytest.mark.parametrize("iters", [0, 1, 2, 5, 20, 33, 70])
+def test_pre_bwd_n8_iteration_counts(iters):
+    """N=8 backward (hcMix=80 small-stage VJP, tensor-core main pass) at iteration counts
+    from 0 to 70 against the fp64 oracle on the same saved tensors."""
+    T, N, D = 300, 8, 256
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=iters + 3,
+                                                       phi_std=2.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-3.0, clamp_max=3.0, iter_times=iters)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    out = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True, **kw)
+    got = M.mhc_pre_clamp_sinkhorn_backward(
+        d[0], d[1], d[2], d[3], out["inv_rms"], out["x_scaled"], out["mixes"],
+        out["h_res_logits"], out["pre"], d[4], d[5], d[6], **kw)
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=-3.0, clamp_max=3.0, iter_times=iters, dtype=F64)
+    assert rel_err(got[0], want[0]) <= TOL_BF16
+    for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
+        assert rel_err(a, b) <= TOL_FP32, name
