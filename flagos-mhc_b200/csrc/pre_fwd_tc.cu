@@ -72,7 +72,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                   const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
                   SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
                   float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
-                  float* __restrict__ logits_out) {
+                  float* __restrict__ logits_out, int ksplit, float* __restrict__ part) {
   using C = MixCfg<N, NB>;
   constexpr int HM = C::HM, S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -125,8 +125,11 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
       uint32_t it = 0;
       bool ok = true;
       const uint64_t pol_stream = tc::l2_evict_first(), pol_keep = tc::l2_evict_last();
-      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        for (int kc = 0; kc < nk; ++kc, ++it) {
+      for (int64_t u = blockIdx.x; u < ntiles * ksplit && ok; u += gridDim.x) {
+        const int64_t tile = u / ksplit;
+        const int spl = (int)(u - tile * ksplit);
+        const int kcb = (int)((int64_t)nk * spl / ksplit), kce = (int)((int64_t)nk * (spl + 1) / ksplit);
+        for (int kc = kcb; kc < kce; ++kc, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
@@ -148,13 +151,17 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
       constexpr uint32_t idesc = tc::idesc_bf16(128, C::NP, false, false);
       uint32_t it = 0, j = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        for (int kc0 = 0; kc0 < nk && ok; kc0 += C::KSEG, ++j) {
+      for (int64_t u = blockIdx.x; u < ntiles * ksplit && ok; u += gridDim.x) {
+        const int64_t tile = u / ksplit;
+        const int spl = (int)(u - tile * ksplit);
+        const int kcb = (int)((int64_t)nk * spl / ksplit), kce = (int)((int64_t)nk * (spl + 1) / ksplit);
+        (void)tile;
+        for (int kc0 = kcb; kc0 < kce && ok; kc0 += C::KSEG, ++j) {
           const int buf = j & 1;
           if (!tc::mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t d = tmem + buf * C::BUFCOL;
-          const int kc1 = kc0 + C::KSEG < nk ? kc0 + C::KSEG : nk;
+          const int kc1 = kc0 + C::KSEG < kce ? kc0 + C::KSEG : kce;
           for (int kc = kc0; kc < kc1; ++kc, ++it) {
             const int s = it % S;
             if (!tc::mbar_wait(&full[s], (it / S) & 1, abort_flag)) { ok = false; break; }
@@ -189,13 +196,16 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
     sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t it = 0, j = 0;
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    for (int64_t u = blockIdx.x; u < ntiles * ksplit; u += gridDim.x) {
+      const int64_t tile = u / ksplit;
+      const int spl = (int)(u - tile * ksplit);
+      const int kcb = (int)((int64_t)nk * spl / ksplit), kce = (int)((int64_t)nk * (spl + 1) / ksplit);
       float sq = 0.f;
       float mix[HM];
 #pragma unroll
       for (int k = 0; k < HM; ++k) mix[k] = 0.f;
       bool ok = true;
-      for (int kc = 0; kc < nk; ++kc, ++it) {
+      for (int kc = kcb; kc < kce; ++kc, ++it) {
         const int s = it % S;
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (it / S) & 1, abort_flag))) {
           ok = false;
@@ -220,7 +230,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
         tc::fence_proxy_async();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[s]);
-        if ((kc + 1) % C::KSEG == 0 || kc + 1 == nk) {
+        if ((kc - kcb + 1) % C::KSEG == 0 || kc + 1 == kce) {
           // end of a K segment: fold its TMEM partial (hi + lo rows) into registers
           const int buf = j & 1;
           if (!__all_sync(0xffffffffu, tc::mbar_wait(&tfull[buf], (j >> 1) & 1, abort_flag))) {
@@ -247,7 +257,16 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
       }
       if (!ok) break;
       const int64_t t = tile * 128 + r;
-      if (t < T) {
+      if (part != nullptr) {
+        // split K (few tiles): this K range's partial sums; pre_mix_finish_kernel adds
+        // the ranges in order and runs the small stage
+        if (t < T) {
+          float* dst = part + ((int64_t)spl * T + t) * (HM + 1);
+#pragma unroll
+          for (int k = 0; k < HM; ++k) dst[k] = mix[k];
+          dst[HM] = sq;
+        }
+      } else if (t < T) {
         const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
 #pragma unroll
         for (int k = 0; k < HM; ++k) mix[k] *= inv;
@@ -264,6 +283,37 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 }
 
+// Split-K finish: thread per token sums the K-range partials in order, then the small
+// stage (as the mix kernel's epilogue does for a whole row).
+template <int N>
+__global__ void __launch_bounds__(128)
+pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* __restrict__ alpha,
+                      const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
+                      SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
+                      float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
+                      float* __restrict__ logits_out) {
+  constexpr int HM = hc_mix(N);
+  __shared__ float sbase[HM];
+  for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
+  __syncthreads();
+  sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float mix[HM], sq = 0.f;
+#pragma unroll
+  for (int k = 0; k < HM; ++k) mix[k] = 0.f;
+  for (int p = 0; p < ksplit; ++p) {
+    const float* src = part + ((int64_t)p * T + t) * (HM + 1);
+#pragma unroll
+    for (int k = 0; k < HM; ++k) mix[k] += src[k];
+    sq += src[HM];
+  }
+  const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
+#pragma unroll
+  for (int k = 0; k < HM; ++k) mix[k] *= inv;
+  small_outputs<N>(mix, sbase, sp, t, inv, inv_rms, mixes, pre, post, comb, logits_out);
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -273,11 +323,23 @@ bool pre_fwd_tc_eligible(const PreFwdArgs& a) {
          a.T > 0 && a.T <= (int64_t)INT32_MAX - 256;
 }
 
+// Split K across CTAs when the tiles cannot fill the GPU (small T): K ranges per tile.
+static int mix_ksplit(int64_t T, int32_t N, int64_t D) {
+  const int64_t ntiles = cdiv(T, 128), sms = sm_count();
+  if (ntiles <= 0 || 2 * ntiles > sms) return 1;
+  const int64_t nk = cdiv((int64_t)N * D, (N <= 4 ? 2 : 1) * 64);
+  int64_t k = sms / ntiles;
+  if (k > nk / 4) k = nk / 4;  // at least 4 K chunks per range
+  return (int)(k < 1 ? 1 : k);
+}
+
+// workspace: phi as bf16 hi/lo rows, then (split K only) the partials [ksplit][T][HM+1]
 size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D) {
-  (void)T;
   const int HM = hc_mix(N);
   const int NP = (2 * HM + 15) / 16 * 16;
-  return align_up((size_t)NP * N * D * 2);
+  const int ks = mix_ksplit(T, N, D);
+  return align_up((size_t)NP * N * D * 2) +
+         (ks > 1 ? align_up((size_t)ks * T * (HM + 1) * 4) : 0);
 }
 
 template <int N, int NB>
@@ -307,11 +369,19 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
     attr_set[dev] = true;
   }
   const int64_t ntiles = cdiv(T, 128);
-  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  const int ks = mix_ksplit(T, N, a.D);
+  float* part = ks > 1 ? (float*)((char*)a.workspace + align_up((size_t)C::NP * HC * 2)) : nullptr;
+  const int grid = (int)std::min<int64_t>(ntiles * ks, sm_count());
   pre_mix_tc_kernel<N, NB><<<grid, C::THREADS, C::SMEM, s>>>(
       tx, tp, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
-      a.comb_frag, a.h_res_logits);
+      a.comb_frag, a.h_res_logits, ks, part);
   MHC_LAUNCH_CHECK();
+  if (part) {
+    pre_mix_finish_kernel<N><<<(unsigned)cdiv(T, 128), 128, 0, s>>>(
+        part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
+        a.post_out, a.comb_frag, a.h_res_logits);
+    MHC_LAUNCH_CHECK();
+  }
   return MHC_OK;
 }
 
