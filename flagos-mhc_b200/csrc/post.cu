@@ -163,16 +163,21 @@ __device__ __forceinline__ void store16(E* p, const float* o) {
   st_global_32B(p, narrow<E>(o), narrow<E>(o + 8));
 }
 
-template <typename E, int N>
+// SPLIT (small T): a block takes one token, warp w a contiguous range of its D steps.
+template <typename E, int N, bool SPLIT>
 __global__ void __launch_bounds__(256, 2)
 post_fwd_x16_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                     const E* __restrict__ h_out, const float* __restrict__ h_post,
                     E* __restrict__ out, int64_t T, int64_t D) {
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
   const int64_t nchunk = D / 16;
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
-       t += nwarps) {
+  const int64_t nst = (nchunk + 31) / 32;
+  const int64_t clo = SPLIT ? nst * w / nw * 32 : 0;
+  const int64_t chi_ = SPLIT ? nst * (w + 1) / nw * 32 : nchunk;
+  const int64_t chi = chi_ < nchunk ? chi_ : nchunk;
+  const int64_t tstride = SPLIT ? gridDim.x : (int64_t)gridDim.x * nw;
+  for (int64_t t = SPLIT ? blockIdx.x : (int64_t)blockIdx.x * nw + w; t < T; t += tstride) {
     float hr[N * N], hp[N];
 #pragma unroll
     for (int e = 0; e < N * N; ++e) hr[e] = __ldg(h_res + t * N * N + e);
@@ -181,7 +186,7 @@ post_fwd_x16_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
     const E* xt = x + t * N * D;
     const E* ht = h_out + t * D;
     E* ot = out + t * N * D;
-    for (int64_t c = lane; c < nchunk; c += 32) {
+    for (int64_t c = clo + lane; c < chi; c += 32) {
       U8 xv[N];
 #pragma unroll
       for (int j = 0; j < N; ++j) xv[j] = ld_global_32B(xt + j * D + c * 16);
@@ -416,7 +421,9 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
 // their h_out (grad_h_post) or h_post (grad_h_out).  grad_x takes a block-diagonal A
 // (each token's h_res hi | lo against its own grad_y rows); the dot products of rows of
 // different tokens come out of the same MMAs and are dropped.
-template <typename E, int V>
+// SPLIT (small T): a block of warps takes one token pair, warp w a contiguous range of
+// the D steps; the dot-product partials are added across the warps in a fixed order.
+template <typename E, int V, bool SPLIT>
 __global__ void __launch_bounds__(256)
 post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                      const float* __restrict__ h_res, const E* __restrict__ h_out,
@@ -430,9 +437,14 @@ post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
   const bool hrow = j == 0;                    // lanes holding row 8 / 12 (h_out, h_post)
   const int i0 = (2 * c) & 3;                  // those columns' index within the token
   const int64_t npairs = (T + 1) / 2;
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t p = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < npairs;
-       p += nwarps) {
+  const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
+  const int64_t nsteps = D / (32 * V);
+  const int64_t dlo = SPLIT ? nsteps * w / nw * (32 * V) : 0;
+  const int64_t dhi = SPLIT ? nsteps * (w + 1) / nw * (32 * V) : D;
+  __shared__ float red[SPLIT ? 8 : 1][32][4];
+  const int64_t pstride = SPLIT ? gridDim.x : (int64_t)gridDim.x * nw;
+  for (int64_t p = SPLIT ? blockIdx.x : (int64_t)blockIdx.x * nw + w; p < npairs;
+       p += pstride) {
     const int64_t t = 2 * p + tb;
     const bool live = t < T;
     uint32_t a[4] = {0u, 0u, 0u, 0u};
@@ -449,7 +461,7 @@ post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
     E* gxr = gx + row;
     E* ght = ghout + (live ? t * D : 0);
 #pragma unroll 2
-    for (int64_t d0 = 8 * V * c; d0 < D; d0 += 32 * V) {
+    for (int64_t d0 = dlo + 8 * V * c; d0 < dhi; d0 += 32 * V) {
       uint32_t xv[R], gv[R], hv[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) xv[r] = gv[r] = hv[r] = 0u;
@@ -481,6 +493,18 @@ post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
         st_row_packs<E, V>(gxr + d0, o);
         if (hrow) st_row_packs<E, V>(ght + d0, oh);
       }
+    }
+    if constexpr (SPLIT) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) red[w][lane][u] = acc[u];
+      __syncthreads();
+      if (w == 0) {
+        for (int ww = 1; ww < nw; ++ww)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) acc[u] += red[ww][lane][u];
+      }
+      __syncthreads();
+      if (w != 0) continue;
     }
     if (live && mine) {
       ghres[t * N * N + j * N + i0] = acc[0];
@@ -530,8 +554,12 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
   }
   if constexpr (sizeof(E) == 2 && N <= 4) {
     if (D % 16 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
-      post_fwd_x16_kernel<E, N><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
-                                                      h_post, (E*)out, T, D);
+      if (T < (int64_t)sm_count() * 8)  // small T (fewer than 8 tokens per SM): a block per token
+        post_fwd_x16_kernel<E, N, true><<<(unsigned)T, block, 0, s>>>(
+            (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
+      else
+        post_fwd_x16_kernel<E, N, false><<<grid, block, 0, s>>>(
+            (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
@@ -556,21 +584,27 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
   if constexpr (sizeof(E) == 2 && N == 4) {
     const bool a32 = aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
                      aligned32(ghout);
-    dim3 pgrid(post_grid((T + 1) / 2));
-    if (D % 128 == 0 && a32) {
-      post_bwd_n4x2_kernel<E, 4><<<pgrid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
-                                                         (const E*)h_out, h_post, (E*)gx, ghres,
-                                                         (E*)ghout, ghpost, T, D);
-      MHC_LAUNCH_CHECK();
-      return MHC_OK;
-    }
-    if (D % 64 == 0 && a32) {
-      post_bwd_n4x2_kernel<E, 2><<<pgrid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
-                                                         (const E*)h_out, h_post, (E*)gx, ghres,
-                                                         (E*)ghout, ghpost, T, D);
-      MHC_LAUNCH_CHECK();
-      return MHC_OK;
-    }
+    const int64_t npairs = (T + 1) / 2;
+    dim3 pgrid(post_grid(npairs));
+    // small T (fewer pairs than 8 per SM): a block per pair, its warps split D
+    const bool split = npairs < (int64_t)sm_count() * 8;
+    dim3 sgrid((unsigned)npairs);
+#define MHC_N4X2(VV)                                                                        \
+  do {                                                                                      \
+    if (split)                                                                              \
+      post_bwd_n4x2_kernel<E, VV, true><<<sgrid, block, 0, s>>>(                            \
+          (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,         \
+          (E*)ghout, ghpost, T, D);                                                         \
+    else                                                                                    \
+      post_bwd_n4x2_kernel<E, VV, false><<<pgrid, block, 0, s>>>(                           \
+          (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,         \
+          (E*)ghout, ghpost, T, D);                                                         \
+    MHC_LAUNCH_CHECK();                                                                     \
+    return MHC_OK;                                                                          \
+  } while (0)
+    if (D % 128 == 0 && a32) MHC_N4X2(4);
+    if (D % 64 == 0 && a32) MHC_N4X2(2);
+#undef MHC_N4X2
   }
   if constexpr (sizeof(E) == 2 && N == 8) {
     if (D % 128 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
