@@ -22,22 +22,29 @@
 
 namespace mhc {
 
-template <typename E, int N, bool VEC>
+// SPLIT (small T): a block takes one token, warp w a contiguous range of its chunks; the
+// warps' sums are added in a fixed order.
+template <typename E, int N, bool VEC, bool SPLIT>
 __global__ void __launch_bounds__(256)
 pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                     float* __restrict__ gpre, int64_t T, int64_t D) {
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
   const int64_t nchunk = D / P;
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T;
-       t += nwarps) {
+  const int64_t nst = (nchunk + 31) / 32;
+  const int64_t clo = SPLIT ? nst * w / nw * 32 : 0;
+  const int64_t chi_ = SPLIT ? nst * (w + 1) / nw * 32 : nchunk;
+  const int64_t chi = chi_ < nchunk ? chi_ : nchunk;
+  __shared__ float red[SPLIT ? 8 : 1][N];
+  const int64_t tstride = SPLIT ? gridDim.x : (int64_t)gridDim.x * nw;
+  for (int64_t t = SPLIT ? blockIdx.x : (int64_t)blockIdx.x * nw + w; t < T; t += tstride) {
     float acc[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) acc[n] = 0.f;
     const E* xt = x + t * N * D;
     const E* gt = gy + t * D;
-    for (int64_t c = lane; c < nchunk; c += 32) {
+    for (int64_t c = clo + lane; c < chi; c += 32) {
       float g[P], xv[N][P];
       load_pack<E, VEC>(gt + c * P, g);
 #pragma unroll
@@ -49,6 +56,20 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
     }
 #pragma unroll
     for (int n = 0; n < N; ++n) acc[n] = warp_sum(acc[n]);
+    if constexpr (SPLIT) {
+      if (lane == 0)
+#pragma unroll
+        for (int n = 0; n < N; ++n) red[w][n] = acc[n];
+      __syncthreads();
+      if (w == 0)
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+          acc[n] = 0.f;
+          for (int ww = 0; ww < nw; ++ww) acc[n] += red[ww][n];
+        }
+      __syncthreads();
+      if (w != 0) continue;
+    }
 #pragma unroll
     for (int n = 0; n < N; ++n)
       if (lane == n) gpre[t * N + n] = acc[n];
@@ -136,10 +157,26 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
     float g[NN];
 #pragma unroll
     for (int e = 0; e < NN; ++e) g[e] = gcomb[t * NN + e];
+    // the iterate of the next (older) iteration is loaded while this one is processed
+    // (N <= 4: one iteration's loads would otherwise wait a full round trip each)
+    float Qn[NN];
+    if (sp.iters > 1) {
+#pragma unroll
+      for (int e = 0; e < NN; ++e) Qn[e] = hist[((int64_t)(sp.iters - 2) * NN + e) * T + t];
+    }
     for (int it = sp.iters - 1; it >= 1; --it) {
       float Q[NN], rs[N], cs[N];  // reciprocals of the row / column divisors
+      if constexpr (N <= 4) {
 #pragma unroll
-      for (int e = 0; e < NN; ++e) Q[e] = hist[((int64_t)(it - 1) * NN + e) * T + t];
+        for (int e = 0; e < NN; ++e) Q[e] = Qn[e];
+        if (it > 1) {
+#pragma unroll
+          for (int e = 0; e < NN; ++e) Qn[e] = hist[((int64_t)(it - 2) * NN + e) * T + t];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < NN; ++e) Q[e] = hist[((int64_t)(it - 1) * NN + e) * T + t];
+      }
       row_norm<N>(Q, sp.hc_eps, rs);       // Q = M_in / (rowsum + eps)
       float U[NN];
 #pragma unroll
@@ -428,12 +465,17 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const bool vec = (D % Pack<E>::n == 0) && aligned16(a.x) && aligned16(a.grad_y);
   const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;
   dim3 sgrid((unsigned)(want < cap ? want : cap));
-  if (vec)
-    pre_bwd_dots_kernel<E, N, true><<<sgrid, 256, 0, s>>>((const E*)a.x, (const E*)a.grad_y,
-                                                          w.gpre, T, D);
+  // small T (fewer than 8 tokens per SM): a block per token, its warps split the row
+  const bool dsplit = T < cap;
+  if (vec && dsplit)
+    pre_bwd_dots_kernel<E, N, true, true><<<(unsigned)T, 256, 0, s>>>(
+        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
+  else if (vec)
+    pre_bwd_dots_kernel<E, N, true, false><<<sgrid, 256, 0, s>>>(
+        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
   else
-    pre_bwd_dots_kernel<E, N, false><<<sgrid, 256, 0, s>>>((const E*)a.x, (const E*)a.grad_y,
-                                                           w.gpre, T, D);
+    pre_bwd_dots_kernel<E, N, false, false><<<sgrid, 256, 0, s>>>(
+        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
   MHC_LAUNCH_CHECK();
   pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(a.mixes, a.alpha, a.base, w.gpre, a.grad_post,
                                                a.grad_comb, a.inv_rms, T, HC, a.sp, w.hist,

@@ -283,8 +283,9 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 }
 
-// Split-K finish: thread per token sums the K-range partials in order, then the small
-// stage (as the mix kernel's epilogue does for a whole row).
+// Split-K finish: a warp per token; lane l adds the K-range partials l, l+32, ... and a
+// fixed-shape warp tree combines the lanes (deterministic), then lane 0 runs the small
+// stage as the mix kernel's epilogue does for a whole row.
 template <int N>
 __global__ void __launch_bounds__(128)
 pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* __restrict__ alpha,
@@ -297,17 +298,22 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
   for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
   __syncthreads();
   sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   float mix[HM], sq = 0.f;
 #pragma unroll
   for (int k = 0; k < HM; ++k) mix[k] = 0.f;
-  for (int p = 0; p < ksplit; ++p) {
+  for (int p = lane; p < ksplit; p += 32) {
     const float* src = part + ((int64_t)p * T + t) * (HM + 1);
 #pragma unroll
     for (int k = 0; k < HM; ++k) mix[k] += src[k];
     sq += src[HM];
   }
+#pragma unroll
+  for (int k = 0; k < HM; ++k) mix[k] = warp_sum(mix[k]);
+  sq = warp_sum(sq);
+  if (lane != 0) return;
   const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
 #pragma unroll
   for (int k = 0; k < HM; ++k) mix[k] *= inv;
@@ -377,7 +383,7 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
       a.comb_frag, a.h_res_logits, ks, part);
   MHC_LAUNCH_CHECK();
   if (part) {
-    pre_mix_finish_kernel<N><<<(unsigned)cdiv(T, 128), 128, 0, s>>>(
+    pre_mix_finish_kernel<N><<<(unsigned)cdiv(T, 4), 128, 0, s>>>(
         part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
         a.post_out, a.comb_frag, a.h_res_logits);
     MHC_LAUNCH_CHECK();
