@@ -139,13 +139,13 @@ pre_apply_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
   }
 }
 
-// bf16 x, D % 16 == 0: a lane handles 16 consecutive d per row with 32-byte accesses
-// (one load per row of x, one store of y, two stores of x_scaled per row).
-template <int N>
+// 16-bit x (bf16 or fp16), D % 16 == 0: a lane handles 16 consecutive d per row with
+// 32-byte accesses (one load per row of x, one store of y, two stores of x_scaled per row).
+template <typename E, int N>
 __global__ void __launch_bounds__(256)
-pre_apply_bf16x16_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ inv_rms,
-                         const float* __restrict__ pre, __nv_bfloat16* __restrict__ y,
-                         float* __restrict__ x_scaled, int64_t T, int64_t D) {
+pre_apply_x16_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
+                     const float* __restrict__ pre, E* __restrict__ y,
+                     float* __restrict__ x_scaled, int64_t T, int64_t D) {
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t nchunk = D / 16;
@@ -155,7 +155,7 @@ pre_apply_bf16x16_kernel(const __nv_bfloat16* __restrict__ x, const float* __res
     float pr[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
-    const __nv_bfloat16* xt = x + t * N * D;
+    const E* xt = x + t * N * D;
     float* xst = x_scaled ? x_scaled + t * N * D : nullptr;
     for (int64_t c = lane; c < nchunk; c += 32) {
       U8 xv[N];
@@ -167,8 +167,8 @@ pre_apply_bf16x16_kernel(const __nv_bfloat16* __restrict__ x, const float* __res
 #pragma unroll
       for (int n = 0; n < N; ++n) {
         float f[16];
-        widen<__nv_bfloat16>(xv[n].a, f);
-        widen<__nv_bfloat16>(xv[n].b, f + 8);
+        widen<E>(xv[n].a, f);
+        widen<E>(xv[n].b, f + 8);
 #pragma unroll
         for (int e = 0; e < 16; ++e) o[e] = fmaf(f[e], pr[n], o[e]);
         if (xst) {
@@ -183,7 +183,7 @@ pre_apply_bf16x16_kernel(const __nv_bfloat16* __restrict__ x, const float* __res
           }
         }
       }
-      st_global_32B(y + t * D + c * 16, narrow<__nv_bfloat16>(o), narrow<__nv_bfloat16>(o + 8));
+      st_global_32B(y + t * D + c * 16, narrow<E>(o), narrow<E>(o + 8));
     }
   }
 }
@@ -199,7 +199,8 @@ int pre_fwd_tc_mix(const PreFwdArgs& a, cudaStream_t s);
 size_t pre_fwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype) {
   const int HM = hc_mix(N);
   const size_t generic = align_up((size_t)T * HM * 4) + align_up((size_t)T * 4);
-  const size_t tc = (dtype == MHC_BF16 && (N == 4 || N == 8)) ? pre_fwd_tc_ws_bytes(T, N, D) : 0;
+  const size_t tc = ((dtype == MHC_BF16 || dtype == MHC_F16) && (N == 4 || N == 8))
+                        ? pre_fwd_tc_ws_bytes(T, N, D) : 0;
   return generic > tc ? generic : tc;
 }
 
@@ -210,7 +211,7 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
   char* ws = (char*)a.workspace;
   float* raw = (float*)ws;
   float* sumsq = (float*)(ws + align_up((size_t)T * HM * 4));
-  if (T > 0 && std::is_same<E, __nv_bfloat16>::value && pre_fwd_tc_eligible(a)) {
+  if (T > 0 && sizeof(E) == 2 && pre_fwd_tc_eligible(a)) {
     const int st = pre_fwd_tc_mix(a, s);
     if (st != MHC_OK) return st;
   } else if (T > 0) {
@@ -230,14 +231,19 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
                      (a.x_scaled == nullptr || aligned16(a.x_scaled));
     const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;
     dim3 grid((unsigned)(want < cap ? want : cap));
-    const bool v16 = std::is_same<E, __nv_bfloat16>::value && D % 16 == 0 &&
+    const bool v16 = sizeof(E) == 2 && D % 16 == 0 &&
                      (reinterpret_cast<uintptr_t>(a.x) & 31) == 0 &&
                      (reinterpret_cast<uintptr_t>(a.y) & 31) == 0 &&
                      (a.x_scaled == nullptr || (reinterpret_cast<uintptr_t>(a.x_scaled) & 31) == 0);
-    if (v16)
-      pre_apply_bf16x16_kernel<N><<<grid, 256, 0, s>>>((const __nv_bfloat16*)a.x, a.inv_rms, a.pre,
-                                                       (__nv_bfloat16*)a.y, a.x_scaled, T, D);
-    else if (vec)
+    if constexpr (sizeof(E) == 2) {
+      if (v16) {
+        pre_apply_x16_kernel<E, N><<<grid, 256, 0, s>>>((const E*)a.x, a.inv_rms, a.pre, (E*)a.y,
+                                                        a.x_scaled, T, D);
+        MHC_LAUNCH_CHECK();
+        return MHC_OK;
+      }
+    }
+    if (vec)
       pre_apply_kernel<E, N, true><<<grid, 256, 0, s>>>((const E*)a.x, a.inv_rms, a.pre,
                                                         (E*)a.y, a.x_scaled, T, D);
     else

@@ -48,31 +48,69 @@ struct MixCfg {
   static constexpr int THREADS = 192;
 };
 
-__global__ void pre_phi_split_kernel(const float* __restrict__ phi, __nv_bfloat16* __restrict__ hl,
-                                     int HM, int NP, int64_t HC) {
+template <typename E> __device__ __forceinline__ E to_e(float v);
+template <> __device__ __forceinline__ __nv_bfloat16 to_e<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half to_e<__half>(float v) { return __float2half_rn(v); }
+__device__ __forceinline__ float from_e(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float from_e(__half v) { return __half2float(v); }
+
+// fp16 operands (x fp16): phi is split after scaling by 2^s so that max|phi| * 2^s < 2^14,
+// keeping the lo halves out of fp16's subnormal range and the hi halves finite; the mix
+// is multiplied by 2^-s afterwards (exact).  This kernel finds max|phi| (the bit patterns
+// of non-negative floats order like the floats).
+__global__ void pre_phi_maxabs_kernel(const float* __restrict__ phi, int64_t n,
+                                      unsigned* __restrict__ slot) {
+  float m = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(phi[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(slot, __float_as_uint(m));
+}
+
+// phi (fp32) -> phi_hl [NP x HC] in E: rows [0,HM) = hi, [HM,2HM) = lo = phi - hi, rest 0.
+// maxslot == nullptr: no scaling (bf16's exponent range is fp32's).
+template <typename E>
+__global__ void pre_phi_split_kernel(const float* __restrict__ phi, E* __restrict__ hl, int HM,
+                                     int NP, int64_t HC, const unsigned* __restrict__ maxslot,
+                                     float* __restrict__ descale) {
+  float scale = 1.f;
+  if (maxslot != nullptr) {
+    const float m = __uint_as_float(*maxslot);
+    if (m > 0.f && isfinite(m)) {
+      int e;
+      frexpf(m, &e);  // m < 2^e
+      scale = ldexpf(1.f, 14 - e);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) *descale = 1.f / scale;
+  }
   const int64_t n = (int64_t)NP * HC;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / HC, c = i - r * HC;
     float v = 0.f;
     if (r < HM) {
-      v = phi[r * HC + c];
+      v = phi[r * HC + c] * scale;
     } else if (r < 2 * HM) {
-      const float p = phi[(r - HM) * HC + c];
-      v = p - __bfloat162float(__float2bfloat16_rn(p));
+      const float p = phi[(r - HM) * HC + c] * scale;
+      v = p - from_e(to_e<E>(p));
     }
-    hl[i] = __float2bfloat16_rn(v);
+    hl[i] = to_e<E>(v);
   }
 }
 
-template <int N, int NB>
+template <int N, int NB, typename E>
 __global__ void __launch_bounds__(MixCfg<N, NB>::THREADS, 1)
 pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                   const __grid_constant__ CUtensorMap tm_phi, const float* __restrict__ alpha,
                   const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
                   SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
                   float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
-                  float* __restrict__ logits_out, int ksplit, float* __restrict__ part) {
+                  float* __restrict__ logits_out, int ksplit, float* __restrict__ part,
+                  const float* __restrict__ descale) {
   using C = MixCfg<N, NB>;
   constexpr int HM = C::HM, S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -148,7 +186,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_bf16(128, C::NP, false, false);
+      constexpr uint32_t idesc = tc::idesc_16<E>(128, C::NP, false, false);
       uint32_t it = 0, j = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < ntiles * ksplit && ok; u += gridDim.x) {
@@ -220,7 +258,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
           // visit the row's 16-byte chunks in swizzled order: the 8 rows of an atom then
           // hit 8 different bank groups (a plain c order is a 32-way bank conflict)
           float f[8];
-          widen<__nv_bfloat16>(row[c ^ (r & 7)], f);
+          widen<E>(row[c ^ (r & 7)], f);
 #pragma unroll
           for (int e = 0; e < 8; ++e) csq = fmaf(f[e], f[e], csq);
         }
@@ -268,8 +306,9 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
         }
       } else if (t < T) {
         const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
+        const float sc = descale ? inv * *descale : inv;  // descale: an exact power of two
 #pragma unroll
-        for (int k = 0; k < HM; ++k) mix[k] *= inv;
+        for (int k = 0; k < HM; ++k) mix[k] *= sc;
         small_outputs<N>(mix, sbase, sp, t, inv, inv_rms, mixes, pre, post, comb, logits_out);
       }
     }
@@ -292,7 +331,7 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
                       const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
                       SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
                       float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
-                      float* __restrict__ logits_out) {
+                      float* __restrict__ logits_out, const float* __restrict__ descale) {
   constexpr int HM = hc_mix(N);
   __shared__ float sbase[HM];
   for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
@@ -315,8 +354,9 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
   sq = warp_sum(sq);
   if (lane != 0) return;
   const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
+  const float sc = descale ? inv * *descale : inv;
 #pragma unroll
-  for (int k = 0; k < HM; ++k) mix[k] *= inv;
+  for (int k = 0; k < HM; ++k) mix[k] *= sc;
   small_outputs<N>(mix, sbase, sp, t, inv, inv_rms, mixes, pre, post, comb, logits_out);
 }
 
@@ -325,7 +365,8 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
 // ---------------------------------------------------------------------------
 bool pre_fwd_tc_eligible(const PreFwdArgs& a) {
   const int64_t HC = (int64_t)a.N * a.D;
-  return a.dtype == MHC_BF16 && (a.N == 4 || a.N == 8) && HC % 8 == 0 && aligned16(a.x) &&
+  return (a.dtype == MHC_BF16 || a.dtype == MHC_F16) && (a.N == 4 || a.N == 8) && HC % 8 == 0 &&
+         aligned16(a.x) &&
          a.T > 0 && a.T <= (int64_t)INT32_MAX - 256;
 }
 
@@ -339,53 +380,68 @@ static int mix_ksplit(int64_t T, int32_t N, int64_t D) {
   return (int)(k < 1 ? 1 : k);
 }
 
-// workspace: phi as bf16 hi/lo rows, then (split K only) the partials [ksplit][T][HM+1]
+// workspace: phi as 16-bit hi/lo rows, (split K only) the partials [ksplit][T][HM+1], then
+// the fp16 scale slots (max|phi| bits, 2^-s)
 size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D) {
   const int HM = hc_mix(N);
   const int NP = (2 * HM + 15) / 16 * 16;
   const int ks = mix_ksplit(T, N, D);
   return align_up((size_t)NP * N * D * 2) +
-         (ks > 1 ? align_up((size_t)ks * T * (HM + 1) * 4) : 0);
+         (ks > 1 ? align_up((size_t)ks * T * (HM + 1) * 4) : 0) + 256;
 }
 
-template <int N, int NB>
+template <int N, int NB, typename E>
 static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
   using C = MixCfg<N, NB>;
+  constexpr bool f16 = std::is_same<E, __half>::value;
   const int64_t T = a.T, HC = (int64_t)N * a.D;
-  __nv_bfloat16* phi_hl = (__nv_bfloat16*)a.workspace;
+  const int ks = mix_ksplit(T, N, a.D);
+  E* phi_hl = (E*)a.workspace;
+  float* part = ks > 1 ? (float*)((char*)a.workspace + align_up((size_t)C::NP * HC * 2)) : nullptr;
+  char* slots = (char*)a.workspace + align_up((size_t)C::NP * HC * 2) +
+                (ks > 1 ? align_up((size_t)ks * T * (C::HM + 1) * 4) : 0);
+  unsigned* maxslot = f16 ? (unsigned*)slots : nullptr;
+  float* descale = f16 ? (float*)(slots + 16) : nullptr;
   {
     const int64_t n = (int64_t)C::NP * HC;
     const int grid = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 8);
-    pre_phi_split_kernel<<<grid, 256, 0, s>>>(a.phi, phi_hl, C::HM, C::NP, HC);
+    if (f16) {
+      MHC_CUDA_CHECK(cudaMemsetAsync(maxslot, 0, sizeof(unsigned), s));
+      const int64_t m = (int64_t)C::HM * HC;
+      pre_phi_maxabs_kernel<<<(int)std::min<int64_t>(cdiv(m, 256), (int64_t)sm_count() * 4), 256,
+                              0, s>>>(a.phi, m, maxslot);
+      MHC_LAUNCH_CHECK();
+    }
+    pre_phi_split_kernel<E><<<grid, 256, 0, s>>>(a.phi, phi_hl, C::HM, C::NP, HC, maxslot,
+                                                 descale);
     MHC_LAUNCH_CHECK();
   }
+  const CUtensorMapDataType dt =
+      f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tx, tp;
-  int st = make_tmap_2d(&tx, a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, T, HC * 2, C::BOX, 128,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  int st = make_tmap_2d(&tx, a.x, dt, 2, HC, T, HC * 2, C::BOX, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
-  st = make_tmap_2d(&tp, phi_hl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HC, C::NP, HC * 2, C::BOX,
-                    C::NP, CU_TENSOR_MAP_SWIZZLE_128B);
+  st = make_tmap_2d(&tp, phi_hl, dt, 2, HC, C::NP, HC * 2, C::BOX, C::NP,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_tc_kernel<N, NB>,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_tc_kernel<N, NB, E>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev] = true;
   }
   const int64_t ntiles = cdiv(T, 128);
-  const int ks = mix_ksplit(T, N, a.D);
-  float* part = ks > 1 ? (float*)((char*)a.workspace + align_up((size_t)C::NP * HC * 2)) : nullptr;
   const int grid = (int)std::min<int64_t>(ntiles * ks, sm_count());
-  pre_mix_tc_kernel<N, NB><<<grid, C::THREADS, C::SMEM, s>>>(
+  pre_mix_tc_kernel<N, NB, E><<<grid, C::THREADS, C::SMEM, s>>>(
       tx, tp, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
-      a.comb_frag, a.h_res_logits, ks, part);
+      a.comb_frag, a.h_res_logits, ks, part, descale);
   MHC_LAUNCH_CHECK();
   if (part) {
     pre_mix_finish_kernel<N><<<(unsigned)cdiv(T, 4), 128, 0, s>>>(
         part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
-        a.post_out, a.comb_frag, a.h_res_logits);
+        a.post_out, a.comb_frag, a.h_res_logits, descale);
     MHC_LAUNCH_CHECK();
   }
   return MHC_OK;
@@ -397,7 +453,8 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
 // ring still holds several stages.
 template <int N>
 static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
-  return pre_fwd_tc_nb<N, (N <= 4 ? 2 : 1)>(a, s);
+  if (a.dtype == MHC_F16) return pre_fwd_tc_nb<N, (N <= 4 ? 2 : 1), __half>(a, s);
+  return pre_fwd_tc_nb<N, (N <= 4 ? 2 : 1), __nv_bfloat16>(a, s);
 }
 
 // Runs the tensor-core mix (+ fused small stage); the caller then runs pre_apply.

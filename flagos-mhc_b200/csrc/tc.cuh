@@ -6,6 +6,8 @@
 
 #include <cuda.h>  // CUtensorMap (type only; the encoder is fetched at run time)
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace mhc {
@@ -201,6 +203,18 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
          ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor: kind::f16, A = B = fp16, D = fp32.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major,
+                                                 bool b_mn_major) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+template <typename E>
+__host__ __device__ constexpr uint32_t idesc_16(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return std::is_same<E, __half>::value ? idesc_f16(M, N, a_mn_major, b_mn_major)
+                                        : idesc_bf16(M, N, a_mn_major, b_mn_major);
 }
 
 }  // namespace tc

@@ -98,7 +98,7 @@ PRE_SHAPES = [(1, 4, 64), (5, 4, 7168), (63, 4, 256), (130, 4, 64), (9, 8, 64), 
 
 
 @pytest.mark.parametrize("clamp", [(0.0, 0.0), (-1.0, 1.0)])
-@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("T,N,D", PRE_SHAPES)
 def test_pre_vs_oracle(T, N, D, dt, clamp):
     x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, dt, seed=T * 13 + N * 5 + D,
