@@ -140,6 +140,26 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// 16-bit element conversions (round to nearest even)
+template <typename E> __device__ __forceinline__ E to_e(float v);
+template <> __device__ __forceinline__ __nv_bfloat16 to_e<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half to_e<__half>(float v) { return __float2half_rn(v); }
+__device__ __forceinline__ float from_e(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float from_e(__half v) { return __half2float(v); }
+
+// fp16 tensor-core operands: values are multiplied by 2^s before their hi/lo split, with
+// 2^s chosen from their maximum magnitude (bits of a non-negative float) so that the
+// maximum stays below 2^14: the hi halves stay finite and the lo halves normal.
+__device__ __forceinline__ float f16_operand_scale(unsigned max_bits) {
+  const float m = __uint_as_float(max_bits);
+  if (!(m > 0.f) || !isfinite(m)) return 1.f;
+  int e;
+  frexpf(m, &e);  // m < 2^e
+  return ldexpf(1.f, 14 - e);
+}
+
 __device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
 
 // ---------------------------------------------------------------------------

@@ -396,7 +396,8 @@ bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const v
 size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D);
 void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
                              __nv_bfloat16** g1, __nv_bfloat16** gp);
-int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream_t s);
+int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                    cudaStream_t s);
 bool pre_bwd_tc8_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
                           const void* gy, const void* gx);
 size_t pre_bwd_tc8_ws_bytes(int64_t T, int64_t D);
@@ -427,7 +428,7 @@ static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t ite
 }
 
 static bool tc_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
-  return dtype == MHC_BF16 && N == 4 && D % 128 == 0 && T > 0;
+  return (dtype == MHC_BF16 || dtype == MHC_F16) && N == 4 && D % 128 == 0 && T > 0;
 }
 
 static bool tc8_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
@@ -449,13 +450,16 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   BwdWs w = bwd_layout((char*)a.workspace, T, N, D, a.sp.iters);
   const int nblk = (int)cdiv(T, 128);
   const bool acc_ok = a.grad_x_acc == nullptr || aligned16(a.grad_x_acc);
-  const bool use_tc = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
+  constexpr bool is_bf16 = std::is_same<E, __nv_bfloat16>::value;
+  const bool use_tc = sizeof(E) == 2 && acc_ok &&
                       pre_bwd_tc_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
   const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
                        pre_bwd_tc8_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
   char* tc_ws = (char*)a.workspace + w.total;
   __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr;
-  if (use_tc) pre_bwd_tc_operand_ptrs(tc_ws, T, D, &g0, &g1, &gp);
+  // bf16: pass 1 writes the operand rows; fp16: they need the maxima first (written from
+  // grad_mixes by pre_bwd_tc_main)
+  if (use_tc && is_bf16) pre_bwd_tc_operand_ptrs(tc_ws, T, D, &g0, &g1, &gp);
   if (T == 0) {
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_alpha, 0, 3 * sizeof(float), s));
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_base, 0, HM * sizeof(float), s));
@@ -479,13 +483,14 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   MHC_LAUNCH_CHECK();
   pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(a.mixes, a.alpha, a.base, w.gpre, a.grad_post,
                                                a.grad_comb, a.inv_rms, T, HC, a.sp, w.hist,
-                                               use_tc ? nullptr : w.gm, w.coef, w.partials,
+                                               (use_tc && is_bf16) ? nullptr : w.gm, w.coef,
+                                               w.partials,
                                                g0, g1, gp);
   MHC_LAUNCH_CHECK();
   pre_reduce_ab_kernel<<<(unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s>>>(w.partials, nblk, HM,
                                                                        a.grad_alpha, a.grad_base);
   MHC_LAUNCH_CHECK();
-  if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.coef, s);
+  if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.gm, w.coef, s);
   if (use_tc8) return pre_bwd_tc8_main(a, tc_ws, w.gm, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   pre_bwd_gx_kernel<E, N><<<ggrid, kGxCC, 0, s>>>((const E*)a.x, (const E*)a.grad_y, a.phi,

@@ -119,12 +119,15 @@ struct ItemCursor {
   }
 };
 
-template <bool ACC>
+// E: bf16 or fp16 (x, grad_y, grad_x and the operand rows).  scl: fp16 only, the maxima
+// (phi, grad_mixes, inv*grad_mixes) the operand rows were scaled by.
+template <bool ACC, typename E>
 __global__ void __launch_bounds__(bwdtc::THREADS, 1)
-pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* __restrict__ gy,
+pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ gy,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
-                  const float* __restrict__ pre, __nv_bfloat16* __restrict__ gx,
+                  const float* __restrict__ pre, E* __restrict__ gx,
                   float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
+                  const unsigned* __restrict__ scl,
                   long long* __restrict__ wdbg) {
   long long wcyc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const long long tstart = clock64();
@@ -244,8 +247,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     // need only the per-item G and the stationary P, never x) and the grad_phi MMAs of
     // step st-1 (which need the x tile), so D1 does not wait on the x load of its step.
     if (lane == 0) {
-      constexpr uint32_t id_gxs = tc::idesc_bf16(128, 128, false, false);
-      constexpr uint32_t id_gphi = tc::idesc_bf16(128, 64, true, true);
+      constexpr uint32_t id_gxs = tc::idesc_16<E>(128, 128, false, false);
+      constexpr uint32_t id_gphi = tc::idesc_16<E>(128, 64, true, true);
       // step = (item, n); A runs one step ahead of B (the grad_phi step)
       struct StepPos {
         ItemCursor c;
@@ -334,6 +337,10 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
     // ------------------------------------------------------------ epilogue warps
     // 16 warps: lane quarter q = warp % 4 (the TMEM lanes this warp may read), column
     // quarter h = (warp - 2) / 4 (32 of the group's 128 columns).
+    // fp16: gxs comes out scaled by 2^(sg + sphi); folding 2^-(sg + sphi) into inv is exact
+    const float gdsc = std::is_same<E, __half>::value
+                           ? 1.f / (f16_operand_scale(scl[1]) * f16_operand_scale(scl[0]))
+                           : 1.f;
     const int q = warp & 3;
     const int h = (warp - 2) >> 2;
     const int r = q * 32 + lane;            // token row (D1) / column row (D2)
@@ -361,7 +368,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
         cf = coef[t];
 #pragma unroll
         for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
-        const __nv_bfloat16* gyr = gy + t * D + d0 + h * 32;
+        const E* gyr = gy + t * D + d0 + h * 32;
         const U8 g01 = ld_global_32B(gyr), g23 = ld_global_32B(gyr + 16);
         gyv[0] = g01.a; gyv[1] = g01.b; gyv[2] = g23.a; gyv[3] = g23.b;
       } else {
@@ -430,7 +437,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
           ++ai;
         }
         const float prn = pr[n];
-        const float2 pr2 = make_float2(prn, prn), inv2 = make_float2(inv, inv),
+        const float2 pr2 = make_float2(prn, prn), inv2 = make_float2(inv * gdsc, inv * gdsc),
                      ncf2 = make_float2(-cf, -cf);
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
@@ -447,8 +454,8 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
           for (int jj = 0; jj < 2; ++jj) {
             const int j = 2 * jp + jj;
             float xf[8], gf[8], o[8];
-            widen<__nv_bfloat16>(xv[j], xf);
-            widen<__nv_bfloat16>(gyv[j], gf);
+            widen<E>(xv[j], xf);
+            widen<E>(gyv[j], gf);
             // packed fp32 pairs (each lane rounds exactly like fmaf / a plain multiply)
 #pragma unroll
             for (int u = 0; u < 8; u += 2) {
@@ -460,12 +467,12 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
             }
             if (ld_acc) {
               float a8[8];
-              widen<__nv_bfloat16>(
+              widen<E>(
                   *reinterpret_cast<const uint4*>(orow + (((2 * jp + jj) ^ osw) << 4)), a8);
 #pragma unroll
               for (int u = 0; u < 8; ++u) o[u] += a8[u];
             }
-            ov[jj] = narrow<__nv_bfloat16>(o);
+            ov[jj] = narrow<E>(o);
           }
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj)
@@ -533,23 +540,25 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const __nv_bfloat16* _
 
 // phi (fp32 [HM][HC]) -> per-column bf16 operand rows P' = [phi_hi | phi_hi | phi_lo | 0]
 // split into P0 [HC][64] and P1 [HC][16].
-__global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi,
-                                        __nv_bfloat16* __restrict__ p0,
-                                        __nv_bfloat16* __restrict__ p1, int64_t HC) {
+template <typename E>
+__global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi, E* __restrict__ p0,
+                                        E* __restrict__ p1, int64_t HC,
+                                        const unsigned* __restrict__ scl) {
   using namespace bwdtc;
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= HC) return;
-  __nv_bfloat16 row[KG];
+  const float sc = scl ? f16_operand_scale(scl[0]) : 1.f;
+  E row[KG];
 #pragma unroll
   for (int k = 0; k < HM; ++k) {
-    const float p = phi[(int64_t)k * HC + c];
-    const __nv_bfloat16 hi = __float2bfloat16_rn(p);
+    const float p = phi[(int64_t)k * HC + c] * sc;
+    const E hi = to_e<E>(p);
     row[k] = hi;
     row[HM + k] = hi;
-    row[2 * HM + k] = __float2bfloat16_rn(p - __bfloat162float(hi));
+    row[2 * HM + k] = to_e<E>(p - from_e(hi));
   }
 #pragma unroll
-  for (int k = 3 * HM; k < KG; ++k) row[k] = __float2bfloat16_rn(0.f);
+  for (int k = 3 * HM; k < KG; ++k) row[k] = to_e<E>(0.f);
   const uint4* rv = reinterpret_cast<const uint4*>(row);
   uint4* d0 = reinterpret_cast<uint4*>(p0 + c * 64);
   uint4* d1 = reinterpret_cast<uint4*>(p1 + c * 16);
@@ -566,7 +575,7 @@ __global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi,
 constexpr int kMaxCellsPerGroup = 4096;
 __global__ void __launch_bounds__(256)
 pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ grad_phi,
-                           int64_t D, BwdGeom geo) {
+                           int64_t D, BwdGeom geo, const unsigned* __restrict__ scl) {
   using namespace bwdtc;
   constexpr int64_t SLOT = (int64_t)N * HM * GC;
   static_assert(SLOT % 256 == 0, "a block must not straddle two groups");
@@ -596,7 +605,82 @@ pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ g
     s += part[(cell * 2) * SLOT + inner];
     if (table ? split[ci] != 0 : cell_split(ci)) s += part[(cell * 2 + 1) * SLOT + inner];
   }
+  if (scl) s *= 1.f / f16_operand_scale(scl[2]);  // exact: a power of two
   grad_phi[(int64_t)k * (N * D) + n * D + g * GC + c] = s;
+}
+
+// fp16 operands: maxima of |phi|, |grad_mixes| and |inv * grad_mixes| (atomicMax on the
+// bits of non-negative floats, which order like the floats).
+__global__ void pre_bwd_f16_max_kernel(const float* __restrict__ phi, int64_t nphi,
+                                       const float* __restrict__ gm,
+                                       const float* __restrict__ inv_rms, int64_t T,
+                                       unsigned* __restrict__ scl) {
+  using namespace bwdtc;
+  float mp = 0.f, mg = 0.f, mgp = 0.f;
+  const int64_t ng = T * HM, n = nphi > ng ? nphi : ng;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < nphi) mp = fmaxf(mp, fabsf(phi[i]));
+    if (i < ng) {
+      const float g = fabsf(gm[i]);
+      mg = fmaxf(mg, g);
+      mgp = fmaxf(mgp, g * inv_rms[i / HM]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, o));
+    mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));
+    mgp = fmaxf(mgp, __shfl_xor_sync(0xffffffffu, mgp, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&scl[0], __float_as_uint(mp));
+    atomicMax(&scl[1], __float_as_uint(mg));
+    atomicMax(&scl[2], __float_as_uint(mgp));
+  }
+}
+
+// fp16 operand rows of one token from grad_mixes (the bf16 path writes them in pass 1):
+//   G' = [g_hi | g_lo | g_hi | 0] * 2^sg (K=80: g0 holds 0..63, g1 64..79)
+//   Gp = [(inv g)_hi | (inv g)_lo | 0] * 2^sgp (64)
+__global__ void pre_bwd_g_prep_f16_kernel(const float* __restrict__ gm,
+                                          const float* __restrict__ inv_rms, __half* __restrict__ g0,
+                                          __half* __restrict__ g1, __half* __restrict__ gp,
+                                          int64_t T, const unsigned* __restrict__ scl) {
+  using namespace bwdtc;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float sg = f16_operand_scale(scl[1]), sgp = f16_operand_scale(scl[2]);
+  const float inv = inv_rms[t];
+  __half row[80], prow[64];
+#pragma unroll
+  for (int k = 0; k < HM; ++k) {
+    const float g = gm[t * HM + k] * sg;
+    const __half hi = __float2half_rn(g);
+    row[k] = hi;
+    row[HM + k] = __float2half_rn(g - __half2float(hi));
+    row[2 * HM + k] = hi;
+    const float p = gm[t * HM + k] * inv * sgp;
+    const __half ph = __float2half_rn(p);
+    prow[k] = ph;
+    prow[HM + k] = __float2half_rn(p - __half2float(ph));
+  }
+#pragma unroll
+  for (int k = 3 * HM; k < 80; ++k) row[k] = __float2half_rn(0.f);
+#pragma unroll
+  for (int k = 2 * HM; k < 64; ++k) prow[k] = __float2half_rn(0.f);
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  const uint4* pv = reinterpret_cast<const uint4*>(prow);
+  uint4* d0 = reinterpret_cast<uint4*>(g0 + t * 64);
+  uint4* d1 = reinterpret_cast<uint4*>(g1 + t * 16);
+  uint4* dp = reinterpret_cast<uint4*>(gp + t * 64);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    d0[j] = rv[j];
+    dp[j] = pv[j];
+  }
+  d1[0] = rv[8];
+  d1[1] = rv[9];
 }
 
 // ---------------------------------------------------------------------------
@@ -604,7 +688,7 @@ pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ g
 // ---------------------------------------------------------------------------
 bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
                          const void* gy, const void* gx) {
-  return dtype == MHC_BF16 && N == 4 && D % bwdtc::GC == 0 && T > 0 &&
+  return (dtype == MHC_BF16 || dtype == MHC_F16) && N == 4 && D % bwdtc::GC == 0 && T > 0 &&
 
          T <= (int64_t)INT32_MAX - 256 && (int64_t)N * D <= INT32_MAX && aligned16(x) &&
          aligned16(gy) && aligned16(gx);
@@ -627,6 +711,7 @@ static BwdGeom bwd_tc_geometry(int64_t T, int64_t D) {
 struct BwdTcWs {
   __nv_bfloat16 *g0, *g1, *gp, *p0, *p1;
   float* part;
+  unsigned* scl;  // fp16: max |phi|, |grad_mixes|, |inv * grad_mixes| (float bits)
   size_t total;
 };
 
@@ -643,6 +728,7 @@ static BwdTcWs bwd_tc_layout(char* base, int64_t T, int64_t D) {
   w.p0 = (__nv_bfloat16*)take((size_t)HC * 64 * 2);
   w.p1 = (__nv_bfloat16*)take((size_t)HC * 16 * 2);
   w.part = (float*)take((size_t)(D / GC) * geo.cpg * 2 * N * HM * GC * 4);
+  w.scl = (unsigned*)take(256);
   w.total = off;
   return w;
 }
@@ -658,15 +744,31 @@ void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
   *gp = w.gp;
 }
 
-int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream_t s) {
+template <typename E>
+static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                          cudaStream_t s) {
   using namespace bwdtc;
+  constexpr bool f16 = std::is_same<E, __half>::value;
   const int64_t T = a.T, D = a.D, HC = N * D;
   const BwdGeom geo = bwd_tc_geometry(T, D);
   BwdTcWs w = bwd_tc_layout((char*)ws, T, D);
-  pre_bwd_phi_prep_kernel<<<(unsigned)cdiv(HC, 256), 256, 0, s>>>(a.phi, w.p0, w.p1, HC);
+  const unsigned* scl = f16 ? w.scl : nullptr;
+  if (f16) {
+    MHC_CUDA_CHECK(cudaMemsetAsync(w.scl, 0, 3 * sizeof(unsigned), s));
+    const int64_t n = std::max<int64_t>((int64_t)HM * HC, T * HM);
+    pre_bwd_f16_max_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 4),
+                             256, 0, s>>>(a.phi, (int64_t)HM * HC, gm, a.inv_rms, T, w.scl);
+    MHC_LAUNCH_CHECK();
+    pre_bwd_g_prep_f16_kernel<<<(unsigned)cdiv(T, 128), 128, 0, s>>>(
+        gm, a.inv_rms, (__half*)w.g0, (__half*)w.g1, (__half*)w.gp, T, w.scl);
+    MHC_LAUNCH_CHECK();
+  }
+  pre_bwd_phi_prep_kernel<E><<<(unsigned)cdiv(HC, 256), 256, 0, s>>>(a.phi, (E*)w.p0, (E*)w.p1,
+                                                                     HC, scl);
   MHC_LAUNCH_CHECK();
   BwdTcMaps m;
-  const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType bf =
+      f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int st;
   // operand rows: row extent T, so rows of the last tile beyond T read as zeros
   if ((st = make_tmap_2d(&m.x, a.x, bf, 2, HC, T, HC * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -694,16 +796,16 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel<false>,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel<false, E>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel<true>,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_bwd_tc_kernel<true, E>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr_set[dev] = true;
   }
-  auto kern = a.grad_x_acc ? pre_bwd_tc_kernel<true> : pre_bwd_tc_kernel<false>;
-  kern<<<geo.ncta, THREADS, SMEM, s>>>(m, (const __nv_bfloat16*)a.grad_y,
+  auto kern = a.grad_x_acc ? pre_bwd_tc_kernel<true, E> : pre_bwd_tc_kernel<false, E>;
+  kern<<<geo.ncta, THREADS, SMEM, s>>>(m, (const E*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
-                                                    (__nv_bfloat16*)a.grad_x, w.part, T, D, geo,
+                                                    (E*)a.grad_x, w.part, T, D, geo, scl,
 #ifdef MHC_PROFILE_WAITS
                                                     getenv("MHC_WAIT_DBG")
                                                         ? (long long*)strtoull(getenv("MHC_WAIT_DBG"), nullptr, 10)
@@ -714,9 +816,16 @@ int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* coef, cudaStream
   );
   MHC_LAUNCH_CHECK();
   const int64_t n = (D / GC) * N * HM * GC;
-  pre_bwd_gphi_reduce_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.part, a.grad_phi, D, geo);
+  pre_bwd_gphi_reduce_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.part, a.grad_phi, D, geo,
+                                                                   scl);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
+}
+
+int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                    cudaStream_t s) {
+  if (a.dtype == MHC_F16) return pre_bwd_tc_run<__half>(a, ws, gm, coef, s);
+  return pre_bwd_tc_run<__nv_bfloat16>(a, ws, gm, coef, s);
 }
 
 int pre_bwd_tc_device_error() { return read_and_clear_tu_error(); }

@@ -48,14 +48,6 @@ struct MixCfg {
   static constexpr int THREADS = 192;
 };
 
-template <typename E> __device__ __forceinline__ E to_e(float v);
-template <> __device__ __forceinline__ __nv_bfloat16 to_e<__nv_bfloat16>(float v) {
-  return __float2bfloat16_rn(v);
-}
-template <> __device__ __forceinline__ __half to_e<__half>(float v) { return __float2half_rn(v); }
-__device__ __forceinline__ float from_e(__nv_bfloat16 v) { return __bfloat162float(v); }
-__device__ __forceinline__ float from_e(__half v) { return __half2float(v); }
-
 // fp16 operands (x fp16): phi is split after scaling by 2^s so that max|phi| * 2^s < 2^14,
 // keeping the lo halves out of fp16's subnormal range and the hi halves finite; the mix
 // is multiplied by 2^-s afterwards (exact).  This kernel finds max|phi| (the bit patterns
@@ -79,12 +71,7 @@ __global__ void pre_phi_split_kernel(const float* __restrict__ phi, E* __restric
                                      float* __restrict__ descale) {
   float scale = 1.f;
   if (maxslot != nullptr) {
-    const float m = __uint_as_float(*maxslot);
-    if (m > 0.f && isfinite(m)) {
-      int e;
-      frexpf(m, &e);  // m < 2^e
-      scale = ldexpf(1.f, 14 - e);
-    }
+    scale = f16_operand_scale(*maxslot);
     if (blockIdx.x == 0 && threadIdx.x == 0) *descale = 1.f / scale;
   }
   const int64_t n = (int64_t)NP * HC;

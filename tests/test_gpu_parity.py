@@ -345,7 +345,8 @@ def test_pre_bwd_n8_tensor_core(T, D):
     assert _C.lib().mhc_device_status() == 0
 
 
-@pytest.mark.parametrize("T,N,D,dt", [(300, 4, 256, torch.bfloat16), (300, 8, 128, torch.bfloat16),
+@pytest.mark.parametrize("T,N,D,dt", [(300, 4, 256, torch.bfloat16), (300, 4, 256, torch.float16),
+                                      (300, 8, 128, torch.bfloat16),
                                       (37, 4, 100, torch.bfloat16), (130, 4, 64, torch.float32)])
 def test_pre_bwd_grad_x_accumulate(T, N, D, dt):
     """grad_x_accumulate (layer fusion: the post backward's grad_x added inside the pre
@@ -409,3 +410,26 @@ def test_pre_bwd_n8_iteration_counts(iters):
     assert rel_err(got[0], want[0]) <= TOL_BF16
     for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
         assert rel_err(a, b) <= TOL_FP32, name
+
+
+def test_pre_bwd_fp16_tensor_core_many_tiles():
+    """fp16 x on the tensor-core backward (fp16 operand rows scaled by powers of two from
+    the maxima of phi, grad_mixes and inv*grad_mixes): many tiles, a ragged last tile,
+    against the fp64 oracle on the same saved tensors."""
+    T, N, D = 148 * 128 + 77, 4, 256
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.float16, seed=5,
+                                                       phi_std=2.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-4.0, clamp_max=4.0, iter_times=20)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    out = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True, **kw)
+    got = M.mhc_pre_clamp_sinkhorn_backward(
+        d[0], d[1], d[2], d[3], out["inv_rms"], out["x_scaled"], out["mixes"],
+        out["h_res_logits"], out["pre"], d[4], d[5], d[6], **kw)
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=-4.0, clamp_max=4.0, iter_times=20, dtype=F64)
+    assert rel_err(got[0], want[0]) <= TOL_BF16
+    for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
+        assert rel_err(a, b) <= TOL_FP32, name
+    from FlagOS_mhc import _C
+    assert _C.lib().mhc_device_status() == 0
