@@ -309,10 +309,12 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 }
 
-// Split-K finish: a warp per token; lane l adds the K-range partials l, l+32, ... and a
-// fixed-shape warp tree combines the lanes (deterministic), then lane 0 runs the small
-// stage as the mix kernel's epilogue does for a whole row.
-template <int N>
+// Split-K finish.  WARP: a warp per token; lane l adds the K-range partials l, l+32, ...
+// and a fixed-shape warp tree combines the lanes (deterministic), then lane 0 runs the
+// small stage (many ranges, few tokens).  Otherwise a thread per token adds its ranges in
+// order and runs the small stage itself, so a warp instruction serves 32 tokens (the small
+// stage is issue-bound: 8192 tokens took 46 us one lane per warp).
+template <int N, bool WARP>
 __global__ void __launch_bounds__(128)
 pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* __restrict__ alpha,
                       const float* __restrict__ base, int64_t T, int64_t HC, float norm_eps,
@@ -325,21 +327,24 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
   __syncthreads();
   sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
   const int lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t t = WARP ? (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)
+                         : (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   float mix[HM], sq = 0.f;
 #pragma unroll
   for (int k = 0; k < HM; ++k) mix[k] = 0.f;
-  for (int p = lane; p < ksplit; p += 32) {
+  for (int p = WARP ? lane : 0; p < ksplit; p += WARP ? 32 : 1) {
     const float* src = part + ((int64_t)p * T + t) * (HM + 1);
 #pragma unroll
     for (int k = 0; k < HM; ++k) mix[k] += src[k];
     sq += src[HM];
   }
+  if (WARP) {
 #pragma unroll
-  for (int k = 0; k < HM; ++k) mix[k] = warp_sum(mix[k]);
-  sq = warp_sum(sq);
-  if (lane != 0) return;
+    for (int k = 0; k < HM; ++k) mix[k] = warp_sum(mix[k]);
+    sq = warp_sum(sq);
+    if (lane != 0) return;
+  }
   const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
   const float sc = descale ? inv * *descale : inv;
 #pragma unroll
@@ -426,7 +431,10 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
       a.comb_frag, a.h_res_logits, ks, part, descale);
   MHC_LAUNCH_CHECK();
   if (part) {
-    pre_mix_finish_kernel<N><<<(unsigned)cdiv(T, 4), 128, 0, s>>>(
+    // a warp per token only for many K ranges (few tokens): lanes then share the loads
+    const bool warp_tok = ks > 16;
+    auto fin = warp_tok ? pre_mix_finish_kernel<N, true> : pre_mix_finish_kernel<N, false>;
+    fin<<<(unsigned)cdiv(T, warp_tok ? 4 : 128), 128, 0, s>>>(
         part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
         a.post_out, a.comb_frag, a.h_res_logits, descale);
     MHC_LAUNCH_CHECK();

@@ -273,6 +273,34 @@ def test_pre_many_tiles_ragged(N):
     assert _C.lib().mhc_device_status() == 0
 
 
+@pytest.mark.parametrize("T,D,dt,xs", [(148 * 64 + 5, 48, torch.bfloat16, True),
+                                        (148 * 64 * 3 + 41, 400, torch.bfloat16, True),
+                                        (148 * 64 * 2 + 7, 400, torch.float16, True),
+                                        (148 * 64 * 2 + 7, 400, torch.bfloat16, False)])
+def test_pre_forward_large_ragged(T, D, dt, xs):
+    """N=4 forward over more tiles than SMs: ragged last tile, a K row (N*D) that is not a
+    multiple of the 128-column mix stage, d not a multiple of 32-byte apply groups of a
+    warp, with and without x_scaled; repeated calls are bitwise equal."""
+    N = 4
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, dt, seed=T + D,
+                                                       phi_std=2.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-4.0, clamp_max=4.0, iter_times=20)
+    d = [t.to(DEV) for t in (x, phi, alpha, base)]
+    out = M.mhc_pre_clamp_sinkhorn(*d, need_backward=True, materialize_x_scaled=xs, **kw)
+    again = M.mhc_pre_clamp_sinkhorn(*d, need_backward=True, materialize_x_scaled=xs, **kw)
+    for k in ("y", "post_out", "comb_frag", "inv_rms", "mixes", "pre"):
+        assert torch.equal(out[k], again[k]), k
+    ref = O.pre_fwd(x, phi, alpha, base, dtype=F64, **kw)
+    for k in ("post_out", "inv_rms", "mixes", "h_res_logits", "pre"):
+        assert rel_err(out[k], ref[k]) <= TOL_FP32, k
+    assert abs_err(out["comb_frag"], ref["comb_frag"]) <= TOL_SINKHORN_ABS
+    assert rel_err(out["y"], ref["y"]) <= _tol(dt)
+    if xs:
+        assert rel_err(out["x_scaled"], ref["x_scaled"]) <= TOL_FP32
+    from FlagOS_mhc import _C
+    assert _C.lib().mhc_device_status() == 0
+
+
 def test_pre_bwd_full_grad_phi_vs_oracle():
     """Config-3 widths (N=4, D=7168) at T=8192: grad_phi / grad_alpha / grad_base
     (sums over every token) against the fp64 oracle run on the same saved tensors."""
