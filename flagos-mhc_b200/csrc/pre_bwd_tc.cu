@@ -352,31 +352,38 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
     ItemCursor cur;
     cur.init(it0, it1, ntiles, subt);
     const bool starts_inside = cur.isub != 0;  // this CTA's run began inside a cell
-    for (; cur.item < it1; cur.next()) {
-      const int64_t item = cur.item, i = cur.i;
-      const int64_t d0 = cur.g * GC;
-      const int64_t t = i * 128 + r;
-      const bool live = t < T;
-      const int64_t row0 = i * 128 + q * 32;  // first token row of this warp's store box
-#ifdef MHC_PROFILE_WAITS
-      const long long _p4 = clock64();
-#endif
-      float inv = 0.f, cf = 0.f, pr[N];
-      uint4 gyv[4];
-      if (live) {
-        inv = inv_rms[t];
-        cf = coef[t];
+    // per-item operands of this lane's row: loaded one item ahead (issued right after the
+    // last step of the previous item used them), so their latency hides behind the flush
+    // and the barrier waits instead of stalling the first step
+    float inv = 0.f, cf = 0.f, pr[N];
+    uint4 gyv[4];
+    auto load_item = [&](int64_t g_, int64_t i_) {
+      const int64_t tt = i_ * 128 + r;
+      if (tt < T) {
+        inv = inv_rms[tt];
+        cf = coef[tt];
 #pragma unroll
-        for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
-        const E* gyr = gy + t * D + d0 + h * 32;
+        for (int n = 0; n < N; ++n) pr[n] = pre[tt * N + n];
+        const E* gyr = gy + tt * D + g_ * GC + h * 32;
         const U8 g01 = ld_global_32B(gyr), g23 = ld_global_32B(gyr + 16);
         gyv[0] = g01.a; gyv[1] = g01.b; gyv[2] = g23.a; gyv[3] = g23.b;
       } else {
+        inv = 0.f;
+        cf = 0.f;
 #pragma unroll
         for (int n = 0; n < N; ++n) pr[n] = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) gyv[j] = make_uint4(0, 0, 0, 0);
       }
+    };
+    if (cur.item < it1) load_item(cur.g, cur.i);
+    for (; cur.item < it1; cur.next()) {
+      const int64_t item = cur.item, i = cur.i;
+      const int64_t d0 = cur.g * GC;
+      const int64_t row0 = i * 128 + q * 32;  // first token row of this warp's store box
+#ifdef MHC_PROFILE_WAITS
+      const long long _p4 = clock64();
+#endif
 #ifdef MHC_PROFILE_WAITS
       wcyc[4] += clock64() - _p4;
 #endif
@@ -487,11 +494,16 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
 #ifdef MHC_PROFILE_WAITS
         wcyc[5] += clock64() - _p2;
 #endif
-        if (n == 0 && item + 1 < it1) {
-          // pull the next item's grad_y row segment into L2 while this item runs
+        if (item + 1 < it1 && (n == 0 || n == N - 1)) {
           const bool wrap = cur.i + 1 == ntiles;
-          const int64_t gn = wrap ? cur.g + 1 : cur.g, tn = (wrap ? 0 : i + 1) * 128 + r;
-          if (tn < T) prefetch_l2(gy + tn * D + gn * GC + h * 32);
+          const int64_t gn = wrap ? cur.g + 1 : cur.g, in = wrap ? 0 : i + 1;
+          if (n == 0) {
+            // pull the next item's grad_y row segment into L2 while this item runs
+            const int64_t tn = in * 128 + r;
+            if (tn < T) prefetch_l2(gy + tn * D + gn * GC + h * 32);
+          } else {
+            load_item(gn, in);  // this item's operands are dead after its last step
+          }
         }
       }
       if (!ok) break;
