@@ -309,11 +309,85 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   }
 }
 
-// Split-K finish.  WARP: a warp per token; lane l adds the K-range partials l, l+32, ...
-// and a fixed-shape warp tree combines the lanes (deterministic), then lane 0 runs the
-// small stage (many ranges, few tokens).  Otherwise a thread per token adds its ranges in
-// order and runs the small stage itself, so a warp instruction serves 32 tokens (the small
-// stage is issue-bound: 8192 tokens took 46 us one lane per warp).
+// One token's forward small stage on a group of N lanes of a warp (N a power of two):
+// lane n of the group owns row n of the N x N matrices; mrow = (mix[n], mix[N+n],
+// mix[2N+nN .. 2N+nN+N-1]), already scaled by inv_rms.  Column sums are gathered by
+// shuffles and added in row order, so the operations are those of small_forward in the
+// same order, with a chain N times shorter.  All 32 lanes call it (valid == false:
+// nothing is stored).
+template <int N>
+__device__ __forceinline__ void small_rows_outputs(const float* mrow, float inv,
+                                                   const float* base, const SmallParams& sp,
+                                                   int n, int64_t t, bool valid, int g0,
+                                                   float* inv_rms, float* mixes, float* pre,
+                                                   float* post, float* comb, float* logits_out) {
+  constexpr int HM = hc_mix(N);
+  const float pr = sigmoidf_(mrow[0] * sp.a0 + base[n]) + sp.hc_eps;
+  const float po = 2.0f * sigmoidf_(mrow[1] * sp.a1 + base[N + n]);
+  float l[N], M[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    l[j] = mrow[2 + j] * sp.a2 + base[2 * N + n * N + j];
+    M[j] = sp.clamp_on ? fminf(fmaxf(l[j], sp.clamp_min), sp.clamp_max) : l[j];
+  }
+  float m = M[0];
+#pragma unroll
+  for (int j = 1; j < N; ++j) m = fmaxf(m, M[j]);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    M[j] = expf(M[j] - m);
+    s += M[j];
+  }
+  const float rs = 1.0f / s;
+#pragma unroll
+  for (int j = 0; j < N; ++j) M[j] *= rs;
+#pragma unroll
+  for (int j = 0; j < N; ++j) M[j] += sp.hc_eps;
+  auto col_norm_rows = [&]() {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float v[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = __shfl_sync(0xffffffffu, M[j], g0 + i);
+      float c = 0.f;
+#pragma unroll
+      for (int i = 0; i < N; ++i) c += v[i];
+      const float rc = 1.0f / (c + sp.hc_eps);
+      M[j] *= rc;
+    }
+  };
+  col_norm_rows();
+  for (int it = 1; it < sp.iters; ++it) {
+    float r = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) r += M[j];
+    const float rr = 1.0f / (r + sp.hc_eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) M[j] *= rr;
+    col_norm_rows();
+  }
+  if (!valid) return;
+  if (n == 0) inv_rms[t] = inv;
+  mixes[t * HM + n] = mrow[0];
+  mixes[t * HM + N + n] = mrow[1];
+  pre[t * N + n] = pr;
+  post[t * N + n] = po;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    mixes[t * HM + 2 * N + n * N + j] = mrow[2 + j];
+    comb[t * N * N + n * N + j] = M[j];
+    if (logits_out) logits_out[t * N * N + n * N + j] = l[j];
+  }
+}
+
+// Split-K finish (the tensor-core mix runs for N = 4, 8): adds the K-range partials of
+// each token in range order and runs the small stage row-parallel (small_rows_outputs).
+// WARP (many ranges, few tokens): a warp per token; lane l adds ranges l, l+32, ... and a
+// fixed-shape warp tree combines the lanes (deterministic); lanes n, n+N, ... then take
+// row n.  Otherwise N lanes per token, lane n adding only the components its row needs.
+// (A thread per token running the whole chain took 46 us at T=8192; one lane per warp
+// running it is issue-bound.)
 template <int N, bool WARP>
 __global__ void __launch_bounds__(128)
 pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* __restrict__ alpha,
@@ -322,34 +396,61 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
                       float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
                       float* __restrict__ logits_out, const float* __restrict__ descale) {
   constexpr int HM = hc_mix(N);
+  static_assert((N & (N - 1)) == 0 && N > 1 && N <= 8, "row groups of N lanes");
   __shared__ float sbase[HM];
   for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
   __syncthreads();
   sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
-  const int lane = threadIdx.x & 31;
-  const int64_t t = WARP ? (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)
-                         : (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= T) return;
-  float mix[HM], sq = 0.f;
+  const int lane = threadIdx.x & 31, n = lane % N;
+  float mrow[N + 3];  // mix[n], mix[N+n], mix[2N+nN .. 2N+nN+N-1], sum of squares
 #pragma unroll
-  for (int k = 0; k < HM; ++k) mix[k] = 0.f;
-  for (int p = WARP ? lane : 0; p < ksplit; p += WARP ? 32 : 1) {
-    const float* src = part + ((int64_t)p * T + t) * (HM + 1);
+  for (int c = 0; c < N + 3; ++c) mrow[c] = 0.f;
+  int64_t t;
+  bool valid;
+  if constexpr (WARP) {
+    t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;  // whole warps
+    valid = lane < N;
+    float mix[HM], sq = 0.f;
 #pragma unroll
-    for (int k = 0; k < HM; ++k) mix[k] += src[k];
-    sq += src[HM];
-  }
-  if (WARP) {
+    for (int k = 0; k < HM; ++k) mix[k] = 0.f;
+    for (int p = lane; p < ksplit; p += 32) {
+      const float* src = part + ((int64_t)p * T + t) * (HM + 1);
+#pragma unroll
+      for (int k = 0; k < HM; ++k) mix[k] += src[k];
+      sq += src[HM];
+    }
 #pragma unroll
     for (int k = 0; k < HM; ++k) mix[k] = warp_sum(mix[k]);
     sq = warp_sum(sq);
-    if (lane != 0) return;
+#pragma unroll
+    for (int nn = 0; nn < N; ++nn) {  // row n's entries without dynamic register indexing
+      if (nn != n) continue;
+      mrow[0] = mix[nn];
+      mrow[1] = mix[N + nn];
+#pragma unroll
+      for (int j = 0; j < N; ++j) mrow[2 + j] = mix[2 * N + nn * N + j];
+    }
+    mrow[N + 2] = sq;
+  } else {
+    t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / N;
+    valid = t < T;
+    const int64_t tc = valid ? t : T - 1;  // invalid lanes still take part in the shuffles
+    for (int p = 0; p < ksplit; ++p) {
+      const float* src = part + ((int64_t)p * T + tc) * (HM + 1);
+      mrow[0] += src[n];
+      mrow[1] += src[N + n];
+#pragma unroll
+      for (int j = 0; j < N; ++j) mrow[2 + j] += src[2 * N + n * N + j];
+      mrow[N + 2] += src[HM];
+    }
   }
-  const float inv = inv_rms_from_sumsq(sq, HC, norm_eps);
+  const float inv = inv_rms_from_sumsq(mrow[N + 2], HC, norm_eps);
   const float sc = descale ? inv * *descale : inv;
 #pragma unroll
-  for (int k = 0; k < HM; ++k) mix[k] *= sc;
-  small_outputs<N>(mix, sbase, sp, t, inv, inv_rms, mixes, pre, post, comb, logits_out);
+  for (int c = 0; c < N + 2; ++c) mrow[c] *= sc;
+  small_rows_outputs<N>(mrow, inv, sbase, sp, n, t, valid, (lane / N) * N, inv_rms, mixes, pre,
+                        post, comb, logits_out);
 }
 
 // ---------------------------------------------------------------------------
@@ -434,7 +535,7 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
     // a warp per token only for many K ranges (few tokens): lanes then share the loads
     const bool warp_tok = ks > 16;
     auto fin = warp_tok ? pre_mix_finish_kernel<N, true> : pre_mix_finish_kernel<N, false>;
-    fin<<<(unsigned)cdiv(T, warp_tok ? 4 : 128), 128, 0, s>>>(
+    fin<<<(unsigned)cdiv(T, warp_tok ? 4 : 128 / N), 128, 0, s>>>(
         part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
         a.post_out, a.comb_frag, a.h_res_logits, descale);
     MHC_LAUNCH_CHECK();
