@@ -268,6 +268,223 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
   }
 }
 
+// Row-parallel small-stage VJP (N = 4, 8): N lanes per token, lane n owning row n of the
+// Sinkhorn matrices.  Column sums (normalisation and the column-norm VJP) are gathered by
+// shuffles and added in row order; row sums stay in the lane.  The chain of one token is
+// N times shorter than in pre_small_bwd_kernel and a warp serves 32/N tokens.  hist
+// layout [iter][T][N*N] (a token's iterate contiguous: its N lanes store one segment).
+// Contributions to grad_alpha / grad_base are summed by fixed shuffle trees per warp and in
+// warp order per block (deterministic), then by pre_reduce_ab_kernel; the token's
+// grad_mixes are gathered in shared memory for its lane 0, which forms the RMS
+// coefficient (same order as the one-thread kernel) and the tensor-core operand rows.
+template <int N>
+__global__ void __launch_bounds__(128)
+pre_small_bwd_rows_kernel(const float* __restrict__ mixes, const float* __restrict__ alpha,
+                          const float* __restrict__ base, const float* __restrict__ gpre,
+                          const float* __restrict__ gpost, const float* __restrict__ gcomb,
+                          const float* __restrict__ inv_rms, int64_t T, int64_t HC,
+                          SmallParams sp, float* __restrict__ hist, float* __restrict__ gm_out,
+                          float* __restrict__ coef_out, float* __restrict__ partials,
+                          __nv_bfloat16* __restrict__ g0, __nv_bfloat16* __restrict__ g1,
+                          __nv_bfloat16* __restrict__ gp) {
+  constexpr int HM = hc_mix(N);
+  constexpr int NN = N * N;
+  constexpr int NP = 3 + HM;
+  constexpr int TPB = 128 / N;  // tokens per block
+  static_assert(N == 4 || N == 8, "row groups of 4 or 8 lanes");
+  __shared__ float sbase[HM];
+  __shared__ float wred[4][NP];  // per-warp sums of the contributions
+  __shared__ float sg[TPB][HM];
+  for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
+  __syncthreads();
+  sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
+  const int lane = threadIdx.x & 31, n = lane % N, gl0 = (lane / N) * N;
+  const int tl = threadIdx.x / N;
+  const int64_t t = (int64_t)blockIdx.x * TPB + tl;
+  const bool valid = t < T;
+  const int64_t tc = valid ? t : T - 1;  // invalid lanes still take part in the shuffles
+  auto colsum = [&](float v) {  // sum over the group's rows of one column, row order
+    float c = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) c += __shfl_sync(0xffffffffu, v, gl0 + i);
+    return c;
+  };
+  const float* mx = mixes + tc * HM;
+  const float m_pre = mx[n], m_post = mx[N + n];
+  float ml[N], logit[N], P[N], M[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) ml[j] = mx[2 * N + n * N + j];
+  // forward recompute: logits row, clamp, softmax row, +eps, Sinkhorn
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    logit[j] = ml[j] * sp.a2 + sbase[2 * N + n * N + j];
+    P[j] = sp.clamp_on ? fminf(fmaxf(logit[j], sp.clamp_min), sp.clamp_max) : logit[j];
+  }
+  {
+    float m = P[0];
+#pragma unroll
+    for (int j = 1; j < N; ++j) m = fmaxf(m, P[j]);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      P[j] = expf(P[j] - m);
+      s += P[j];
+    }
+    const float rs = 1.0f / s;
+#pragma unroll
+    for (int j = 0; j < N; ++j) P[j] *= rs;
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) M[j] = P[j] + sp.hc_eps;
+  auto col_norm_row = [&](float* R, float* cs) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      const float c = 1.0f / (colsum(R[j]) + sp.hc_eps);
+      if (cs) cs[j] = c;
+      R[j] *= c;
+    }
+  };
+  auto row_norm_row = [&](float* R) {
+    float r = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) r += R[j];
+    const float rr = 1.0f / (r + sp.hc_eps);
+#pragma unroll
+    for (int j = 0; j < N; ++j) R[j] *= rr;
+    return rr;
+  };
+  col_norm_row(M, nullptr);
+  for (int it = 1; it < sp.iters; ++it) {
+    if (valid) {
+      float4* h4 = reinterpret_cast<float4*>(hist + ((int64_t)(it - 1) * T + t) * NN + n * N);
+#pragma unroll
+      for (int q = 0; q < N / 4; ++q)
+        h4[q] = make_float4(M[4 * q], M[4 * q + 1], M[4 * q + 2], M[4 * q + 3]);
+    }
+    row_norm_row(M);
+    col_norm_row(M, nullptr);
+  }
+  // backward through the Sinkhorn iterations (the next older iterate is loaded ahead)
+  float g[N], Qn[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) g[j] = gcomb[tc * NN + n * N + j];
+  auto load_row = [&](int it, float* R) {
+    const float4* h4 =
+        reinterpret_cast<const float4*>(hist + ((int64_t)(it - 1) * T + tc) * NN + n * N);
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q) {
+      const float4 v = valid ? h4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      R[4 * q] = v.x; R[4 * q + 1] = v.y; R[4 * q + 2] = v.z; R[4 * q + 3] = v.w;
+    }
+  };
+  if (sp.iters > 1) load_row(sp.iters - 1, Qn);
+  auto col_vjp = [&](const float* U, const float* cs) {  // dQ = (g - sum_i g*U) / colsum
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float s = 0.f;  // fma chain in row order, as the one-thread kernel's loop compiles
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        s = fmaf(__shfl_sync(0xffffffffu, g[j], gl0 + i), __shfl_sync(0xffffffffu, U[j], gl0 + i),
+                 s);
+      g[j] = (g[j] - s) * cs[j];
+    }
+  };
+  for (int it = sp.iters - 1; it >= 1; --it) {
+    float Q[N], U[N], cs[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) Q[j] = Qn[j];
+    if (it > 1) load_row(it - 1, Qn);
+    const float rs = row_norm_row(Q);      // Q = M_in / (rowsum + eps)
+#pragma unroll
+    for (int j = 0; j < N; ++j) U[j] = Q[j];
+    col_norm_row(U, cs);                   // U = Q / (colsum + eps)
+    col_vjp(U, cs);
+    float s = 0.f;                         // row-norm VJP: dM = (dQ - sum_j dQ*Q) / rowsum
+#pragma unroll
+    for (int j = 0; j < N; ++j) s += g[j] * Q[j];
+#pragma unroll
+    for (int j = 0; j < N; ++j) g[j] = (g[j] - s) * rs;
+  }
+  {  // iteration 0: U0 = M0 / cs0, M0 = P + eps
+    float U[N], cs[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) U[j] = P[j] + sp.hc_eps;
+    col_norm_row(U, cs);
+    col_vjp(U, cs);
+  }
+  // softmax VJP of row n: dl = P * (dP - sum_j dP*P); clamp passes where min <= l <= max
+  float c2 = 0.f, gl[N], dl[N];
+  {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) s += g[j] * P[j];
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      float d = P[j] * (g[j] - s);
+      if (sp.clamp_on && !(logit[j] >= sp.clamp_min && logit[j] <= sp.clamp_max)) d = 0.f;
+      gl[j] = d * sp.a2;
+      c2 = fmaf(d, ml[j], c2);
+      dl[j] = valid ? d : 0.f;
+    }
+  }
+  const float s0 = sigmoidf_(m_pre * sp.a0 + sbase[n]);
+  const float s1 = sigmoidf_(m_post * sp.a1 + sbase[N + n]);
+  const float dz0 = gpre[tc * N + n] * s0 * (1.0f - s0);
+  const float dz1 = gpost[tc * N + n] * 2.0f * s1 * (1.0f - s1);
+  // contributions to grad_alpha (3) and grad_base (HM): sums over the warp's tokens by
+  // fixed xor trees (common entries over all lanes, row entries over lanes of equal n),
+  // then over the block's 4 warps in order
+  {
+    float cm[3] = {valid ? dz0 * m_pre : 0.f, valid ? dz1 * m_post : 0.f, valid ? c2 : 0.f};
+    float rw[2 + N];
+    rw[0] = valid ? dz0 : 0.f;
+    rw[1] = valid ? dz1 : 0.f;
+#pragma unroll
+    for (int j = 0; j < N; ++j) rw[2 + j] = dl[j];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) cm[c] = warp_sum(cm[c]);
+#pragma unroll
+    for (int o = N; o < 32; o <<= 1)
+#pragma unroll
+      for (int c = 0; c < 2 + N; ++c) rw[c] += __shfl_xor_sync(0xffffffffu, rw[c], o);
+    const int w = threadIdx.x >> 5;
+    if (lane < 3) wred[w][lane] = lane == 0 ? cm[0] : (lane == 1 ? cm[1] : cm[2]);
+    if (lane < N) {
+      wred[w][3 + n] = rw[0];
+      wred[w][3 + N + n] = rw[1];
+#pragma unroll
+      for (int j = 0; j < N; ++j) wred[w][3 + 2 * N + n * N + j] = rw[2 + j];
+    }
+  }
+  sg[tl][n] = dz0 * sp.a0;
+  sg[tl][N + n] = dz1 * sp.a1;
+#pragma unroll
+  for (int j = 0; j < N; ++j) sg[tl][2 * N + n * N + j] = gl[j];
+  if (valid && gm_out) {
+    gm_out[t * HM + n] = dz0 * sp.a0;
+    gm_out[t * HM + N + n] = dz1 * sp.a1;
+#pragma unroll
+    for (int j = 0; j < N; ++j) gm_out[t * HM + 2 * N + n * N + j] = gl[j];
+  }
+  __syncwarp();
+  if (n == 0 && valid) {
+    float gmx[HM], dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < HM; ++k) {
+      gmx[k] = sg[tl][k];
+      dot = fmaf(gmx[k], mx[k], dot);
+    }
+    const float inv = inv_rms[t];
+    coef_out[t] = inv * inv / (float)HC * dot;
+    if constexpr (N == 4) {
+      if (g0) write_tc_operand_rows(gmx, inv, t, g0, g1, gp);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NP; i += blockDim.x)
+    partials[(int64_t)blockIdx.x * NP + i] = ((wred[0][i] + wred[1][i]) + wred[2][i]) + wred[3][i];
+}
+
 // One warp per output value: lanes take strided partials, then a fixed-shape tree
 // (warp_sum) -- deterministic for a given number of blocks.
 __global__ void pre_reduce_ab_kernel(const float* __restrict__ partials, int nblk, int HM,
@@ -412,7 +629,7 @@ struct BwdWs {
 static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t iters) {
   const int HM = hc_mix(N);
   const int64_t HC = (int64_t)N * D;
-  const int64_t nblk = cdiv(T, 128);
+  const int64_t nblk = cdiv(T, 16);  // blocks of the small-stage VJP (>= 16 tokens each)
   const int64_t hist_n = (int64_t)(iters > 1 ? iters - 1 : 0) * N * N * T;
   BwdWs w;
   size_t off = 0;
@@ -448,7 +665,6 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   constexpr int HM = hc_mix(N);
   const int64_t T = a.T, D = a.D, HC = (int64_t)N * D;
   BwdWs w = bwd_layout((char*)a.workspace, T, N, D, a.sp.iters);
-  const int nblk = (int)cdiv(T, 128);
   const bool acc_ok = a.grad_x_acc == nullptr || aligned16(a.grad_x_acc);
   constexpr bool is_bf16 = std::is_same<E, __nv_bfloat16>::value;
   const bool use_tc = sizeof(E) == 2 && acc_ok &&
@@ -481,11 +697,21 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
     pre_bwd_dots_kernel<E, N, false, false><<<sgrid, 256, 0, s>>>(
         (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
   MHC_LAUNCH_CHECK();
-  pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(a.mixes, a.alpha, a.base, w.gpre, a.grad_post,
-                                               a.grad_comb, a.inv_rms, T, HC, a.sp, w.hist,
-                                               (use_tc && is_bf16) ? nullptr : w.gm, w.coef,
-                                               w.partials,
-                                               g0, g1, gp);
+  // small-stage VJP.  Row-parallel (N lanes per token, N = 4, 8) while a thread per token
+  // would not give every SM a block: its chain is N times shorter but it issues ~3N^2
+  // shuffles per lane and iteration, so once the GPU is full the one-thread kernel wins
+  // (T=32768, N=4: 1.169 vs 1.191 ms pre backward; T=1: 56 vs 49.5 us).
+  constexpr bool rows_ok = N == 4 || N == 8;
+  const bool rows = rows_ok && cdiv(T, 128) < sm_count();
+  const int nblk = (int)cdiv(T, rows ? 128 / N : 128);
+  if (rows)
+    pre_small_bwd_rows_kernel<rows_ok ? N : 4><<<nblk, 128, 0, s>>>(
+        a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
+        w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
+  else
+    pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(
+        a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
+        w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   MHC_LAUNCH_CHECK();
   pre_reduce_ab_kernel<<<(unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s>>>(w.partials, nblk, HM,
                                                                        a.grad_alpha, a.grad_base);
