@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -71,37 +70,71 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 20 ms by a reader thread;
-    stop() keeps the samples taken between mark_start() and mark_stop()."""
-    Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    """SM clocks and throttle reasons of this process's GPU, read through NVML by a
+    thread every `period_s` (in-process, so every sample carries the host time at
+    which it was taken).  `stop()` summarises the samples taken between
+    mark_start() and mark_stop(); `load_window` also reports the samples since
+    mark_load() (the untimed soak steps right before the timed region plus the
+    region itself).  Reads only; changes no GPU setting."""
+    # NVML clocks-event reason bits (nvml.h: nvmlClocksEventReason*)
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, uuid):
-        self.uuid = (uuid or "").lower()
-        self.proc = None
-        self.rows = []          # (time, fields)
-        self.t0 = self.t1 = None
-
-    def _reader(self):
-        for ln in self.proc.stdout:
-            if ln.strip():
-                self.rows.append((time.perf_counter(), [c.strip() for c in ln.split(",")]))
-
-    def start(self, wait_s=5.0):
-        import threading
+    def __init__(self, dev_index, period_s=0.002):
+        self.period = period_s
+        self.rows = []           # (host time, sm MHz, max sm MHz, reasons bitmask)
+        self.t_load = self.t0 = self.t1 = None
+        self._stop = False
+        self._th = None
+        self.err = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = None
+            try:
+                uuid = str(torch.cuda.get_device_properties(dev_index).uuid)
+            except Exception:
+                pass
+            h = None
+            if uuid:
+                for i in range(pynvml.nvmlDeviceGetCount()):
+                    hi = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    u = pynvml.nvmlDeviceGetUUID(hi)
+                    u = u.decode() if isinstance(u, bytes) else u
+                    if uuid.lower() in u.lower():
+                        h = hi
+                        break
+            self.h = h if h is not None else pynvml.nvmlDeviceGetHandleByIndex(dev_index)
+            self.nv = pynvml
+        except Exception as e:  # no NVML: the line says so
+            self.nv = None
+            self.err = repr(e)
+
+    def _loop(self):
+        nv, h = self.nv, self.h
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                try:
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.rows.append((time.perf_counter(), sm, mx, rs))
+            except Exception as e:
+                self.err = repr(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        import threading
+        if self.nv is None:
             return
-        threading.Thread(target=self._reader, daemon=True).start()
-        t = time.perf_counter()
-        while not self.rows and time.perf_counter() - t < wait_s:
-            time.sleep(0.01)
+        self._th = threading.Thread(target=self._loop, daemon=True)
+        self._th.start()
+
+    def mark_load(self):
+        self.t_load = time.perf_counter()
 
     def mark_start(self):
         self.t0 = time.perf_counter()
@@ -109,46 +142,43 @@ class ClockSampler:
     def mark_stop(self):
         self.t1 = time.perf_counter()
 
+    def _summ(self, rows):
+        if not rows:
+            return None
+        reasons = sorted({n for r in rows for n, b in self.BITS.items() if r[3] & b})
+        return {"sm_mhz": statistics.median(r[1] for r in rows),
+                "sm_max_mhz": max(r[2] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = [f for t, f in self.rows if self.t0 is not None and self.t0 <= t <= (self.t1 or t)]
-        window = "timed region"
-        if not rows:  # region shorter than one sample period: nearest samples after its start
-            rows = [f for t, f in self.rows if self.t0 is not None and t >= self.t0][:3]
-            window = "first samples after the timed region began"
-        mine = [r for r in rows if self.uuid and self.uuid in r[0].lower()] or rows
-        sm, mx, reasons = [], [], set()
-        for r in mine:
-            try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-            except (ValueError, IndexError):
-                continue
-            for n, v in zip(self.NAMES, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm), "window": window}
+        if self.nv is None:
+            return {"error": "NVML unavailable: " + str(self.err)}
+        self._stop = True
+        if self._th is not None:
+            self._th.join(timeout=2)
+        timed = [r for r in self.rows if self.t0 <= r[0] <= self.t1]
+        load = [r for r in self.rows if (self.t_load or self.t0) <= r[0] <= self.t1]
+        out = self._summ(timed) or self._summ(load) or {}
+        out["window"] = "timed region" if timed else "soak + timed region"
+        out["load_window"] = self._summ(load)
+        out["period_ms"] = self.period * 1e3
+        out["source"] = "NVML in-process sampler"
+        return out
 
 
-def make_inputs(T, N, D, seed, dev):
-    """Config-2 (post) and config-3 (pre) inputs, generated on the device from a seed."""
-    g = torch.Generator(device=dev).manual_seed(seed)
+def make_inputs(T, N, D, seed, dev, param_seed=3):
+    """Config-2 (post) and config-3 (pre) inputs, generated on the device from a seed.
+    The per-token tensors use `seed` (each rank draws its own token shard); phi,
+    alpha and base use `param_seed` on every rank (they are replicated parameters)."""
     bf = torch.bfloat16
     HM, HC = N * (N + 2), N * D
     inp = {}
+    gp = torch.Generator(device=dev).manual_seed(param_seed)
+    inp["phi"] = torch.randn(HM, HC, generator=gp, device=dev) / HC ** 0.5
+    inp["alpha"] = torch.rand(3, generator=gp, device=dev) + 0.5
+    inp["base"] = torch.randn(HM, generator=gp, device=dev) * 0.1
+    g = torch.Generator(device=dev).manual_seed(seed)
     inp["x_pre"] = torch.randn(T, N, D, generator=g, device=dev).to(bf)
-    inp["phi"] = torch.randn(HM, HC, generator=g, device=dev) / HC ** 0.5
-    inp["alpha"] = torch.rand(3, generator=g, device=dev) + 0.5
-    inp["base"] = torch.randn(HM, generator=g, device=dev) * 0.1
     inp["gy_pre"] = torch.randn(T, D, generator=g, device=dev).to(bf)
     inp["gpost"] = torch.randn(T, N, generator=g, device=dev)
     inp["gcomb"] = torch.randn(T, N, N, generator=g, device=dev)
@@ -165,10 +195,13 @@ def make_inputs(T, N, D, seed, dev):
 
 
 KW = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-10.0, clamp_max=10.0, iter_times=20)
+# per-step inputs that come from the host in the end-to-end measurement
+HOST_INPUTS = ["x_pre", "gy_pre", "gpost", "gcomb", "x_post", "h_out", "h_res", "h_post",
+               "gy_post"]
 
 
-def run_step(M, inp, world, ev=None, x_scaled=True):
-    """The four operators (+ the gradient all-reduce). Returns the small results."""
+def run_step(M, inp, world, ev=None, x_scaled=True, reducer=None):
+    """The four operators (+ the cross-GPU gradient sum). Returns their results."""
     if ev is not None:
         ev[0].record()
     out = M.mhc_pre_clamp_sinkhorn(inp["x_pre"], inp["phi"], inp["alpha"], inp["base"],
@@ -182,83 +215,134 @@ def run_step(M, inp, world, ev=None, x_scaled=True):
                              inp["h_post"])
     if ev is not None:
         ev[3].record()
-    gx, gphi, ga, gb = M.mhc_pre_clamp_sinkhorn_backward(
+    grads = M.mhc_pre_clamp_sinkhorn_backward(
         inp["x_pre"], inp["phi"], inp["alpha"], inp["base"], out["inv_rms"], out["x_scaled"],
         out["mixes"], out["h_res_logits"], out["pre"], inp["gy_pre"], inp["gpost"],
         inp["gcomb"], **KW)
     if ev is not None:
         ev[4].record()
     if world > 1:
-        from FlagOS_mhc.distributed import allreduce_pre_grads
-        allreduce_pre_grads(gphi, ga, gb)
+        if reducer is not None:
+            reducer(grads[1], grads[2], grads[3])
+        else:
+            from FlagOS_mhc.distributed import allreduce_pre_grads
+            allreduce_pre_grads(grads[1], grads[2], grads[3])
     if ev is not None:
         ev[5].record()
-    return out, y, pg, (gx, gphi, ga, gb)
+    return out, y, pg, grads
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_oracle_rate(T_sample, budget_s, max_s, steps=None):
-    """Tokens/s of the CPU oracle (fp32, all host threads) on T_sample-token
-    slices of the benchmark shapes; repeats until budget_s (or `steps` reps)."""
-    from oracle import mhc_oracle as O
-    torch.set_num_threads(os.cpu_count())
-    g = torch.Generator().manual_seed(0)
-    N, D = N_HC, D_HID
+def _ref_inputs(T, N, D, seed=0):
+    """CPU tensors of the benchmark workload's shapes and distributions (bf16 storage,
+    fp32 parameters), for the `*_ref` timing."""
+    g = torch.Generator().manual_seed(seed)
     HM, HC = N * (N + 2), N * D
-    x = torch.randn(T_sample, N, D, generator=g).to(torch.bfloat16)
-    phi = torch.randn(HM, HC, generator=g) / HC ** 0.5
-    alpha, base = torch.rand(3, generator=g) + 0.5, torch.randn(HM, generator=g) * 0.1
-    gy = torch.randn(T_sample, D, generator=g).to(torch.bfloat16)
-    gpost, gcomb = torch.randn(T_sample, N, generator=g), torch.randn(T_sample, N, N, generator=g)
-    h_res = torch.softmax(torch.randn(T_sample, N, N, generator=g), -1)
-    h_post = 2 * torch.sigmoid(torch.randn(T_sample, N, generator=g))
-    h_out = torch.randn(T_sample, D, generator=g).to(torch.bfloat16)
-    gyp = torch.randn(T_sample, N, D, generator=g).to(torch.bfloat16)
+    bf = torch.bfloat16
+    d = {"x_pre": torch.randn(T, N, D, generator=g).to(bf),
+         "phi": torch.randn(HM, HC, generator=g) / HC ** 0.5,
+         "alpha": torch.rand(3, generator=g) + 0.5,
+         "base": torch.randn(HM, generator=g) * 0.1,
+         "gy_pre": torch.randn(T, D, generator=g).to(bf),
+         "gpost": torch.randn(T, N, generator=g), "gcomb": torch.randn(T, N, N, generator=g),
+         "x_post": torch.randn(T, N, D, generator=g).to(bf),
+         "h_out": torch.randn(T, D, generator=g).to(bf),
+         "h_res": torch.softmax(torch.randn(T, N, N, generator=g), -1),
+         "h_post": 2 * torch.sigmoid(torch.randn(T, N, generator=g)),
+         "gy_post": torch.randn(T, N, D, generator=g).to(bf)}
+    return d
 
-    def one():
-        O.pre_fwd(x, phi, alpha, base, **KW)
-        O.post_fwd(x, h_res, h_out, h_post)
-        O.post_bwd(gyp, x, h_res, h_out, h_post)
-        O.pre_bwd(x, phi, alpha, base, gy, gpost, gcomb, **KW)
 
-    times = []
-    t_all = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        one()
-        times.append(time.perf_counter() - t0)
-        el = time.perf_counter() - t_all
-        if steps is not None:
-            if len(times) >= steps:
+def _ref_step(M, d):
+    """One step of the workload through the `*_ref` functions (the reference's
+    pure-PyTorch path: src/mhc_pre_clamp_sinkhorn.py:974-1022,
+    src/mhc_pre_clamp_sinkhorn_backward.py:1397-1453, src/mhc_post.py:344-352,
+    src/mhc_post_backward.py:624-643, restated op for op in FlagOS_mhc)."""
+    M.mhc_pre_clamp_sinkhorn_ref(d["x_pre"], d["phi"], d["alpha"], d["base"], **KW)
+    M.mhc_post_ref(d["x_post"], d["h_res"], d["h_out"], d["h_post"])
+    M.mhc_post_backward_ref(d["gy_post"], d["x_post"], d["h_res"], d["h_out"], d["h_post"])
+    M.mhc_pre_clamp_sinkhorn_backward_ref(d["x_pre"], d["phi"], d["alpha"], d["base"],
+                                          d["gy_pre"], d["gpost"], d["gcomb"], **KW)
+
+
+def cpu_ref_rate(T_sample, steps=None, budget_s=None, warmup=0):
+    """Tokens/s of the `*_ref` path on T_sample-token slices of the benchmark shapes,
+    all host threads.  Runs `steps` steps, or repeats until `budget_s` has passed."""
+    import FlagOS_mhc as M
+    torch.set_num_threads(os.cpu_count())
+    d = _ref_inputs(T_sample, N_HC, D_HID)
+    with torch.no_grad():
+        for _ in range(warmup):
+            _ref_step(M, d)
+        times = []
+        t_all = time.perf_counter()
+        while True:
+            t0 = time.perf_counter()
+            _ref_step(M, d)
+            times.append(time.perf_counter() - t0)
+            if steps is not None and len(times) >= steps:
                 break
-        elif el >= budget_s or el >= max_s:
-            break
+            if steps is None and time.perf_counter() - t_all >= budget_s:
+                break
     return T_sample * len(times) / sum(times), times
 
 
+def cpu_c0(steps=20, warmup=3):
+    """Config C0 at its full shape: mhc_post_ref forward plus its backward by autograd,
+    fp32 on the host, T=256 (B=2, S=128), N=4, D=1024, torch seed 0."""
+    import FlagOS_mhc as M
+    torch.set_num_threads(os.cpu_count())
+    torch.manual_seed(0)
+    B, S, N, D = 2, 128, 4, 1024
+    x = torch.randn(B, S, N, D, requires_grad=True)
+    h_out = torch.randn(B, S, D, requires_grad=True)
+    h_res = torch.softmax(torch.randn(B, S, N, N), -1).requires_grad_(True)
+    h_post = (2 * torch.sigmoid(torch.randn(B, S, N))).requires_grad_(True)
+    gy = torch.randn(B, S, N, D)
+    times = []
+    for k in range(warmup + steps):
+        t0 = time.perf_counter()
+        y = M.mhc_post_ref(x, h_res, h_out, h_post)
+        torch.autograd.grad(y, (x, h_res, h_out, h_post), gy)
+        if k >= warmup:
+            times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.median(times)
+    return {"config": "C0: mhc_post_ref fwd + autograd bwd, fp32 CPU, B=2 S=128 N=4 D=1024",
+            "ms_per_step": ms, "tokens_per_s": B * S / (ms / 1e3), "steps": steps,
+            "cores": torch.get_num_threads()}
+
+
+REF_SAMPLE_NOTE = ("tokens/s is per-token independent work, so the rate of a T-token slice "
+                   "is the rate of the full T=32768 step; the `*_ref` path is the "
+                   "reference's pure-PyTorch algorithm (fp32 math on bf16 storage), op for op")
+
+
 def reference_arm(args, rank, world):
+    """The reference's CPU implementation of the path (its `*_ref` functions) on this
+    host's cores: each step is one T_s-token slice of the benchmark workload."""
     if rank != 0:
         return 0
-    # calibrate the slice so one step is ~4 s of CPU work
-    rate0, _ = cpu_oracle_rate(64, 0, 60, steps=1)
-    T_s = int(max(64, min(4096, rate0 * 4.0)) // 64 * 64)
-    for _ in range(args.warmup):
-        cpu_oracle_rate(T_s, 0, 600, steps=1)
-    rate, times = cpu_oracle_rate(T_s, 0, 3600, steps=args.steps)
+    # calibrate the slice so one step is ~3 s of CPU work (the run stays a few minutes)
+    rate0, _ = cpu_ref_rate(128, steps=1, warmup=1)
+    T_s = int(max(64, min(4096, rate0 * 3.0)) // 64 * 64)
+    rate, times = cpu_ref_rate(T_s, steps=args.steps, warmup=args.warmup)
     cores = torch.get_num_threads()
-    sample = (f"{T_s}-token slices of the T=32768,N=4,D=7168 workload (pre fwd+bwd and post "
-              f"fwd+bwd, fp32 CPU oracle); per-token independent ops, so tokens/s is linear in T")
+    ms = 1e3 * sum(times) / len(times)
+    sample = (f"{args.steps} steps of a {T_s}-token slice of the T=32768,N=4,D=7168 workload "
+              f"(pre fwd+bwd and post fwd+bwd through the *_ref path); " + REF_SAMPLE_NOTE)
     line = {
         "metric": METRIC, "value": rate, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * T_TOK / rate, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": {"workload": WORKLOAD, "T": T_TOK, "N": N_HC, "D": D_HID,
-                   "parallelism": "rank 0 only (CPU)", "sample_tokens": T_s},
+                   "parallelism": "rank 0 only (CPU)", "sample_tokens": T_s,
+                   "ms_per_step_is": f"one {T_s}-token slice"},
         "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "c0": cpu_c0(),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -367,15 +451,216 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
     return res
 
 
+# ----------------------------------------------------------------------------- end to end
+# outputs of one step that go back to the host in the end-to-end measurement
+def _step_outputs(out, y, pg, grads):
+    d = {"y": out["y"], "post_out": out["post_out"], "comb_frag": out["comb_frag"],
+         "inv_rms": out["inv_rms"], "mixes": out["mixes"], "h_res_logits": out["h_res_logits"],
+         "pre": out["pre"], "post_out_x": y, "post_grad_x": pg[0], "grad_h_res": pg[1],
+         "grad_h_out": pg[2], "grad_h_post": pg[3], "pre_grad_x": grads[0]}
+    if out["x_scaled"].numel():
+        d["x_scaled"] = out["x_scaled"]
+    return d
+
+
+def e2e_measure(M, inp, world, steps, x_scaled, reducer, dist, dev):
+    """The step through the public API with host buffers: every step copies each
+    per-token input from pinned host memory and every output back to pinned host
+    memory.  Tokens are processed in chunks on three streams (H2D, compute, D2H), so
+    the copies of one chunk overlap the kernels of its neighbours; the per-chunk
+    parameter gradients are summed on the device and copied back once per step."""
+    T = inp["x_pre"].shape[0]
+    C = max(256, min(4096, T // 4)) if T >= 1024 else T
+    chunks = [(a, min(T, a + C)) for a in range(0, T, C)]
+    host_in = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, pin_memory=True)
+               for k in HOST_INPUTS}
+    for k in HOST_INPUTS:
+        host_in[k].copy_(inp[k])
+    # output shapes from one chunk-sized call
+    probe = {k: inp[k][:chunks[0][1]] for k in HOST_INPUTS}
+    probe.update(phi=inp["phi"], alpha=inp["alpha"], base=inp["base"])
+    o = _step_outputs(*run_step(M, probe, 1, x_scaled=x_scaled))
+    host_out = {k: torch.empty((T,) + tuple(v.shape[1:]), dtype=v.dtype, pin_memory=True)
+                for k, v in o.items()}
+    n_param = inp["phi"].numel() + 3 + inp["base"].numel()
+    host_grad = torch.empty(n_param, dtype=torch.float32, pin_memory=True)
+    del o, probe
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out.values()) + host_grad.numel() * 4
+    bufs = [{k: torch.empty((C,) + tuple(inp[k].shape[1:]), dtype=inp[k].dtype, device=dev)
+             for k in HOST_INPUTS} for _ in range(2)]
+    s_in, s_c, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
+    gacc = torch.empty(n_param, dtype=torch.float32, device=dev)
+    main = torch.cuda.current_stream(dev)
+
+    def one_step():
+        for i, (a, b) in enumerate(chunks):
+            j, n = i % 2, b - a
+            if i >= 2:
+                s_in.wait_event(ev_free[j])
+            with torch.cuda.stream(s_in):
+                for k in HOST_INPUTS:
+                    bufs[j][k][:n].copy_(host_in[k][a:b], non_blocking=True)
+                ev_in[j].record(s_in)
+            s_c.wait_event(ev_in[j])
+            with torch.cuda.stream(s_c):
+                chunk = {k: bufs[j][k][:n] for k in HOST_INPUTS}
+                chunk.update(phi=inp["phi"], alpha=inp["alpha"], base=inp["base"])
+                out, y, pg, grads = run_step(M, chunk, 1, x_scaled=x_scaled)
+                ev_free[j].record(s_c)
+                g = grads[1].reshape(-1)
+                flat = torch.as_strided(g, (n_param,), (1,))  # packed [phi|alpha|base]
+                if i == 0:
+                    gacc.copy_(flat)
+                else:
+                    gacc.add_(flat)
+                outs = _step_outputs(out, y, pg, grads)
+                done = torch.cuda.Event()
+                done.record(s_c)
+            s_out.wait_event(done)
+            with torch.cuda.stream(s_out):
+                for k, v in outs.items():
+                    host_out[k][a:b].copy_(v.reshape(host_out[k][a:b].shape), non_blocking=True)
+                    v.record_stream(s_out)
+        with torch.cuda.stream(s_c):
+            if world > 1:
+                nph = inp["phi"].numel()
+                reducer(gacc[:nph].view_as(inp["phi"]), gacc[nph:nph + 3], gacc[nph + 3:])
+            done = torch.cuda.Event()
+            done.record(s_c)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            host_grad.copy_(gacc, non_blocking=True)
+            gacc.record_stream(s_out)
+
+    def fence_all(ev_start=None):
+        for s in (s_in, s_c, s_out):
+            if ev_start is not None:
+                s.wait_event(ev_start)
+            else:
+                e = torch.cuda.Event()
+                e.record(s)
+                main.wait_event(e)
+
+    one_step()      # warm-up (allocator, pinned pages)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    fence_all(e0)
+    for _ in range(steps):
+        one_step()
+    fence_all()
+    e1.record(main)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    return {"value": world * T * steps / (e_ms / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "ms_per_step": e_ms / steps, "chunk_tokens": C,
+            "outputs_copied_back": sorted(host_out) + ["grad_phi|grad_alpha|grad_base"],
+            "note": "public API per token chunk; H2D of every per-token input from pinned "
+                    "memory and D2H of every output to pinned memory, each step, inside the "
+                    "CUDA-event-timed region (three streams, PCIe-bound)"}
+
+
 # ----------------------------------------------------------------------------- GPU arm
+def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=None):
+    """K steps between two events (after a barrier and a synchronize), preceded by
+    untimed soak steps for about soak_s seconds.  Returns (max-over-ranks ms, per-step
+    op events, launches)."""
+    from FlagOS_mhc import _C
+    if clocks is not None:
+        clocks.mark_load()
+    t_end = time.perf_counter() + soak_s
+    while time.perf_counter() < t_end:
+        run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+        torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = _C.lib().mhc_kernel_launches()
+    if clocks is not None:
+        clocks.mark_start()
+    start.record()
+    for k in range(K):
+        run_step(M, inp, world, evs[k], x_scaled=x_scaled, reducer=reducer)
+    stop.record()
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.mark_stop()
+    launches = _C.lib().mhc_kernel_launches() - n0
+    if world > 1:
+        dist.barrier()
+    ms_total = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    return ms_total, evs, launches
+
+
+def grad_sum_bench(MD, dist, dev, world, rank, K, W):
+    """Back-to-back calls of the cross-GPU sum of the packed C3 parameter gradients
+    (24 x 28672 + 27 fp32): the fused peer-memory kernel against NCCL's all-reduce.
+    Device time per call, max over ranks."""
+    n = 24 * 28672 + 27
+    buf = torch.randn(n, device=dev)
+    red = MD.PeerGradReducer(n, dev)
+    res = {}
+    for name, fn in (("fused_peer_kernel", red.reduce_),
+                     ("nccl_all_reduce", lambda b: dist.all_reduce(b))):
+        reps = max(K, 50)
+        for _ in range(max(W, 5)):
+            fn(buf)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn(buf)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = {"us_per_call": float(t.item()), "calls": reps}
+    red.close()
+    if rank == 0:
+        print(json.dumps({"grad_sum_bench": res, "n_gpus": world, "floats": n,
+                          "bytes": 4 * n}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--tokens", type=int, default=T_TOK, help="tokens per GPU")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--global-tokens", type=int, default=T_TOK,
+                    help="tokens of the whole job, split evenly over the ranks (strong scaling)")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per GPU instead (weak scaling)")
+    ap.add_argument("--soak-s", type=float, default=1.0,
+                    help="untimed steps right before the timed region (clock sampling under load)")
+    ap.add_argument("--e2e-steps", type=int, default=None, help="default: --steps")
+    ap.add_argument("--collective", default="fused", choices=["fused", "nccl"],
+                    help="cross-GPU gradient sum: the library's peer-memory kernel or NCCL")
+    ap.add_argument("--grad-sum-bench", action="store_true",
+                    help="N>1: time only the cross-GPU gradient sum (fused kernel vs NCCL)")
+    ap.add_argument("--no-weak", action="store_true",
+                    help="N>1: skip the secondary weak-scaling measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="skip the C1 / C4 measurements reported beside the headline")
@@ -394,12 +679,15 @@ def main():
 
     import torch.distributed as dist
     import FlagOS_mhc as M
-    from FlagOS_mhc import _C
+    from FlagOS_mhc import distributed as MD
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", device_id=dev)
+
+    if args.grad_sum_bench:
+        return grad_sum_bench(MD, dist, dev, world, rank, args.steps, args.warmup)
 
     if args.configs_only:
         peak, peak_kind = hbm_peak()
@@ -408,51 +696,33 @@ def main():
                           "peak_kind": peak_kind}), flush=True)
         return 0
 
-    T, N, D = args.tokens, N_HC, D_HID
+    N, D = N_HC, D_HID
+    if args.tokens is not None:
+        T, T_global, scaling = args.tokens, args.tokens * world, "weak"
+    else:
+        a, b = MD.token_range(args.global_tokens, rank, world)
+        T, T_global, scaling = b - a, args.global_tokens, "strong"
     xs_on = not args.skip_x_scaled
-    inp = make_inputs(T, N, D, seed=1000 + rank, dev=dev)
-    torch.cuda.synchronize()
-
-    for _ in range(max(args.warmup, 0)):
-        run_step(M, inp, world, x_scaled=xs_on)
-    torch.cuda.synchronize()
-
     K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(dev).uuid)
-    except Exception:
-        pass
-    clocks = ClockSampler(uuid)
-    clocks.start()
-    # the barrier comes after each rank's sampler is up, right before the timed region:
-    # otherwise a rank that starts early waits for the others inside its first all-reduce
+    inp = make_inputs(T, N, D, seed=1000 + rank, dev=dev)
+    reducer = None
     if world > 1:
-        dist.barrier()
+        reducer = (MD.PeerGradReducer(inp["phi"].numel() + 3 + inp["base"].numel(), dev)
+                   if args.collective == "fused" else MD.allreduce_pre_grads)
     torch.cuda.synchronize()
-    n0 = _C.lib().mhc_kernel_launches()
-    clocks.mark_start()
-    start.record()
-    for k in range(K):
-        run_step(M, inp, world, evs[k], x_scaled=xs_on)
-    stop.record()
+    for _ in range(max(args.warmup, 0)):
+        run_step(M, inp, world, x_scaled=xs_on, reducer=reducer)
     torch.cuda.synchronize()
-    clocks.mark_stop()
-    launches = _C.lib().mhc_kernel_launches() - n0
-    if world > 1:
-        dist.barrier()
-    ck = clocks.stop()
-    ms_total = start.elapsed_time(stop)
-    if world > 1:
-        t = torch.tensor([ms_total], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
-    ms_step = ms_total / K
-    value = world * T * K / (ms_total / 1e3)
 
-    names = ["pre_fwd", "post_fwd", "post_bwd", "pre_bwd", "allreduce"]
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms_total, evs, launches = timed_steps(M, inp, world, K, xs_on, reducer, dist, dev,
+                                          args.soak_s, clocks)
+    ck = clocks.stop()
+    ms_step = ms_total / K
+    value = T_global * K / (ms_total / 1e3)
+
+    names = ["pre_fwd", "post_fwd", "post_bwd", "pre_bwd", "grad_sum"]
     op_ms = {n: statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(K))
              for i, n in enumerate(names)}
     ab = algorithmic_bytes(T, N, D, x_scaled=xs_on)
@@ -462,47 +732,26 @@ def main():
                "frac_of_" + peak_kind + "_peak": ab[n] / (op_ms[n] / 1e3) / 1e9 / peak}
            for n in ab}
     # roofline of one kernel measured live: post_bwd is a single launch between its two
-    # events (the pre ops run several kernels) and holds ~23% of the step in the ncu
-    # launch list, about the same share as the largest kernels
+    # events (the pre ops run several kernels) and the largest share of the step in the
+    # ncu launch list
     dom = "post_bwd"
-    traffic = ncu_traffic().get(dom)
+    tr = ncu_traffic().get(dom + "_per_token")
+    traffic = tr * T if tr else None
     achieved = ab[dom] / (op_ms[dom] / 1e3) / 1e9
 
-    # ---- end to end through the public API, inputs from pinned host memory
+    weak = None
+    if world > 1 and scaling == "strong" and not args.no_weak:
+        inp_w = make_inputs(T_TOK, N, D, seed=2000 + rank, dev=dev)
+        ms_w, _, _ = timed_steps(M, inp_w, world, K, xs_on, reducer, dist, dev, 0.2)
+        weak = {"tokens_per_gpu": T_TOK, "global_tokens": T_TOK * world, "steps": K,
+                "ms_per_step": ms_w / K, "value": world * T_TOK * K / (ms_w / 1e3)}
+        del inp_w
+        torch.cuda.empty_cache()
+
+    e2e_steps = K if args.e2e_steps is None else args.e2e_steps
     e2e = None
-    if args.e2e_steps > 0:
-        big = ["x_pre", "gy_pre", "gpost", "gcomb", "x_post", "h_out", "h_res", "h_post",
-               "gy_post"]
-        host = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, pin_memory=True) for k in big}
-        for k in big:
-            host[k].copy_(inp[k])
-        h2d = sum(host[k].numel() * host[k].element_size() for k in big)
-        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d2h = 0
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e_start.record()
-        for _ in range(args.e2e_steps):
-            for k in big:
-                inp[k].copy_(host[k], non_blocking=True)
-            out, y, pg, grads = run_step(M, inp, world, x_scaled=xs_on)
-            res = [grads[1], grads[2], grads[3], pg[1], pg[3], out["post_out"], out["comb_frag"]]
-            cpu_res = [r.to("cpu", non_blocking=False) for r in res]
-            d2h = sum(r.numel() * r.element_size() for r in cpu_res)
-        e_stop.record()
-        torch.cuda.synchronize()
-        e_ms = e_start.elapsed_time(e_stop)
-        if world > 1:
-            t = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = float(t.item())
-        e2e = {"value": world * T * args.e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "steps": args.e2e_steps,
-               "note": "H2D of every op input from pinned memory; D2H of the parameter grads "
-                       "and the per-token small outputs (activations stay on the device)"}
-        del host
+    if e2e_steps > 0:
+        e2e = e2e_measure(M, inp, world, e2e_steps, xs_on, reducer, dist, dev)
 
     others = None
     if rank == 0 and world == 1 and not args.no_other_configs:
@@ -512,37 +761,45 @@ def main():
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, times = cpu_oracle_rate(256, 10.0, 30.0)
+        rate, times = cpu_ref_rate(256, budget_s=15.0, warmup=1)
         cpu_base = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(),
                     "kind": "port",
-                    "sample": f"{len(times)} x 256-token slices of the same workload (fp32 CPU "
-                              "oracle, pre fwd+bwd + post fwd+bwd); tokens/s is linear in T"}
+                    "sample": f"{len(times)} steps of a 256-token slice of the same workload "
+                              "through the *_ref path; " + REF_SAMPLE_NOTE,
+                    "c0": cpu_c0()}
 
     if rank == 0:
+        coll = {"fused": "one fused peer-memory kernel (grad_phi partial reduce + cross-GPU "
+                         "sum over NVLink)", "nccl": "packed NCCL all-reduce"}[args.collective]
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "global_tokens": world * T,
+            "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "global_tokens": T_global,
                        "N": N, "D": D, "hcMix": N * (N + 2), "clamp": [-10.0, 10.0],
                        "iter_times": 20,
                        "x_scaled": "written (reference contract)" if xs_on
                        else "skipped (opt-in materialize_x_scaled=False)",
                        "parallelism": f"dp{world} token-sharded"
-                       + (", packed grad_phi NCCL all-reduce" if world > 1 else ""),
-                       "l2": "no flush: every step streams ~21 GB, x alone is 1.88 GB > 126 MB L2"},
+                       + (f", gradient sum: {coll}" if world > 1 else ""),
+                       "l2": "no flush: each step streams >= 2.6 GB per GPU (x alone "
+                             f"{T * N * D * 2 / 1e6:.0f} MB) through the 126 MB L2"},
             "hbm_frac_step": step_bytes / (ms_step / 1e3) / 1e9 / peak,
-            "roofline": {"bound": "hbm", "kernel": "post_bwd_n4x2_kernel", "achieved": achieved, "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "algorithmic_bytes": ab[dom], "traffic": traffic},
-            "ops": ops, "allreduce_ms": op_ms["allreduce"],
+            "roofline": {"bound": "hbm", "kernel": "post_bwd_n4x2_kernel", "achieved": achieved,
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": achieved / peak, "algorithmic_bytes": ab[dom],
+                         "traffic": traffic,
+                         "traffic_source": ncu_traffic().get("source")},
+            "ops": ops, "grad_sum_ms": op_ms["grad_sum"],
             "gpu_launches": int(launches),
             "clocks": ck, "e2e": e2e, "cpu_baseline": cpu_base,
-            "other_configs": others,
+            "weak_scaling": weak, "other_configs": others,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if reducer is not None and hasattr(reducer, "close"):
+            reducer.close()
         dist.destroy_process_group()
     return 0
 

@@ -50,6 +50,15 @@ _SIGS = {
     "mhc_pre_bwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp, _i64, _i32,
                                    _i64, _i32, _f32, _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp,
                                    _vp, _sz, _vp]),
+    "mhc_peer_region_bytes": (_sz, [_i64]),
+    "mhc_peer_region_alloc": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_void_p)]),
+    "mhc_peer_region_free": (ctypes.c_int, [_vp]),
+    "mhc_peer_handle_bytes": (ctypes.c_int, []),
+    "mhc_peer_handle": (ctypes.c_int, [_vp, ctypes.c_char_p]),
+    "mhc_peer_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mhc_peer_close": (ctypes.c_int, [_vp]),
+    "mhc_grad_sum_peers": (ctypes.c_int, [_vp, _vp, _i64, ctypes.POINTER(ctypes.c_void_p), _i32,
+                                          _i32, ctypes.c_uint32, ctypes.c_uint64, _vp]),
     "mhc_pre_bwd_accumulate": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp,
                                               _i64, _i32, _i64, _i32, _f32, _f32, _f32, _f32,
                                               _i32, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),

@@ -59,3 +59,90 @@ def allreduce_pre_grads(grad_phi, grad_alpha, grad_base, group=None, average=Fal
         grad_alpha.copy_(buf[n0:n0 + n1].view_as(grad_alpha))
         grad_base.copy_(buf[n0 + n1:].view_as(grad_base))
     return grad_phi, grad_alpha, grad_base
+
+
+class PeerGradReducer:
+    """Sum of the packed parameter gradients over the ranks of a one-node job in ONE
+    kernel over NVLink peer memory (``mhc_grad_sum_peers`` of the C ABI), in place of
+    the NCCL all-reduce of :func:`allreduce_pre_grads`.
+
+    Construction is collective: every rank of `group` allocates its peer region,
+    the CUDA IPC handles are exchanged with ``all_gather_object`` and each rank maps
+    the others' regions.  Calls must then be made by every rank in the same order
+    (the epoch counter advances once per call on every rank).  A wait that runs
+    past `timeout_s` makes the kernel return early with MHC_ERR_TIMEOUT recorded
+    (``_C.lib().mhc_device_status()``); the reducer is then unusable.  The result
+    is bitwise identical on every rank (rank-order sum)."""
+
+    def __init__(self, n: int, device, group=None, timeout_s: float = 2.0):
+        import ctypes
+
+        from . import _C
+        self.L = _C.lib()
+        self.n = int(n)
+        self.device = torch.device(device)
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("PeerGradReducer: at most 8 ranks (one node)")
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.epoch = 0
+        self._opened = []
+        with torch.cuda.device(self.device):
+            reg = ctypes.c_void_p()
+            _C.check(self.L.mhc_peer_region_alloc(self.n, ctypes.byref(reg)), "PeerGradReducer")
+            self.region = reg
+            hb = self.L.mhc_peer_handle_bytes()
+            buf = ctypes.create_string_buffer(hb)
+            _C.check(self.L.mhc_peer_handle(reg, buf), "PeerGradReducer")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, buf.raw, group=group)
+            ptrs = (ctypes.c_void_p * 8)()
+            for p, h in enumerate(handles):
+                if p == self.rank:
+                    ptrs[p] = reg.value
+                    continue
+                q = ctypes.c_void_p()
+                _C.check(self.L.mhc_peer_open(ctypes.create_string_buffer(h, hb), ctypes.byref(q)),
+                         "PeerGradReducer")
+                self._opened.append(q)
+                ptrs[p] = q.value
+            self.ptrs = ptrs
+        dist.barrier(group=group)
+
+    def reduce_(self, buf: torch.Tensor):
+        """In-place sum over the ranks of a contiguous fp32 CUDA vector of n floats."""
+        from . import _C
+        assert buf.dtype == torch.float32 and buf.is_contiguous() and buf.numel() == self.n
+        self.epoch += 1
+        st = self.L.mhc_grad_sum_peers(_C.ptr(buf), _C.ptr(buf), self.n, self.ptrs, self.rank,
+                                       self.world, self.epoch, self.timeout_ns,
+                                       _C.stream_of(buf))
+        _C.check(st, "PeerGradReducer")
+        return buf
+
+    def __call__(self, grad_phi, grad_alpha, grad_base):
+        buf = packed_buffer(grad_phi, grad_alpha, grad_base)
+        if buf is not None:
+            self.reduce_(buf)
+            return grad_phi, grad_alpha, grad_base
+        buf = torch.cat([grad_phi.reshape(-1), grad_alpha.reshape(-1), grad_base.reshape(-1)])
+        self.reduce_(buf)
+        n0, n1 = grad_phi.numel(), grad_alpha.numel()
+        grad_phi.copy_(buf[:n0].view_as(grad_phi))
+        grad_alpha.copy_(buf[n0:n0 + n1].view_as(grad_alpha))
+        grad_base.copy_(buf[n0 + n1:].view_as(grad_base))
+        return grad_phi, grad_alpha, grad_base
+
+    def close(self):
+        """Collective: unmap the peers' regions, wait for every rank, free ours."""
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for q in self._opened:
+                self.L.mhc_peer_close(q)
+            self._opened = []
+            dist.barrier(group=self.group)
+            if self.region is not None:
+                self.L.mhc_peer_region_free(self.region)
+                self.region = None

@@ -19,6 +19,7 @@ int post_bwd_dispatch(int32_t N, int32_t dtype, const void* gy, const void* x,
 int pre_fwd_tc_device_error();
 int pre_bwd_tc_device_error();
 int pre_bwd_tc8_device_error();
+int peer_device_error();
 
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
@@ -110,7 +111,8 @@ int mhc_device_status(void) {
   const int a = pre_fwd_tc_device_error();
   const int b = pre_bwd_tc_device_error();
   const int c = pre_bwd_tc8_device_error();
-  return a != MHC_OK ? a : (b != MHC_OK ? b : c);
+  const int d = peer_device_error();
+  return a != MHC_OK ? a : (b != MHC_OK ? b : (c != MHC_OK ? c : d));
 }
 
 int mhc_post_fwd(const void* x, const float* h_res, const void* h_out, const float* h_post,

@@ -17,9 +17,15 @@
 //     contents.  The pre forward overwrites every scratch word it reads, so
 //     nothing has to start at zero.  Two calls whose kernels overlap on the GPU
 //     (different streams without ordering between them) race on the array.
-//   - The device address of the array is looked up on the first call on each
-//     device (cudaGetSymbolAddress with that device current).  Make that first
-//     call before any stream capture begins.
+//   - The device address of the array is looked up (cudaGetSymbolAddress, with
+//     the caller's device current) on every call that is not being captured into
+//     a CUDA graph; a captured call reuses the address of the last uncaptured call
+//     on that device.  So make one call on each device before any stream capture
+//     begins, and again after a cudaDeviceReset, before capturing.
+//   - Shapes that fit (the need grows with T: per-token partial sums, plus for
+//     bf16/fp16 x the hi/lo split of phi, 2*N*(N+2) rounded up to 16 rows of N*D
+//     bf16): N=4 at D <= 7168 up to T = 167,770 tokens; N=8 at D = 4096 up to
+//     T = 51,780; N=8 at D = 7168 never fits (the split phi alone is 18.4 MB).
 #include <mutex>
 
 #include "common.cuh"
@@ -30,20 +36,28 @@ namespace mhc {
 static __device__ __align__(256) unsigned char g_pre_fwd_scratch[MHC_PRE_FWD_NOALLOC_SCRATCH_BYTES];
 
 static std::mutex g_scratch_mu;
-static void* g_scratch_addr[64];  // per device; the symbol's device address
+static void* g_scratch_addr[64];  // per device: the last address looked up
 
 // The host-side name g_pre_fwd_scratch is only a stand-in for the array; kernels
-// must be given the address returned by cudaGetSymbolAddress for the current device.
-static int scratch_address(void** out) {
+// must be given the address that cudaGetSymbolAddress returns for the current
+// device and context.  The lookup runs on every call made outside stream capture,
+// so a context that was torn down and re-created (cudaDeviceReset, or a caller that
+// switches driver contexts) gets the array of the context that is current now.
+// Inside a capture the address of the last uncaptured call on this device is used.
+static int scratch_address(cudaStream_t stream, void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MHC_ERR_CUDA;
   if (dev < 0 || dev >= 64) return MHC_ERR_DEVICE;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return MHC_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  if (cs == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_pre_fwd_scratch) != cudaSuccess || p == nullptr)
       return MHC_ERR_CUDA;
     g_scratch_addr[dev] = p;
+  } else if (g_scratch_addr[dev] == nullptr) {
+    return MHC_ERR_CUDA;  // first call on this device made inside a capture
   }
   *out = g_scratch_addr[dev];
   return MHC_OK;
@@ -64,7 +78,7 @@ extern "C" int mhc_pre_fwd_noalloc(const void* x, const float* phi, const float*
   if (T > 0) {
     // argument errors are reported by mhc_pre_fwd below; only look the array up
     // once the call would actually launch
-    const int st = mhc::scratch_address(&scratch);
+    const int st = mhc::scratch_address((cudaStream_t)stream, &scratch);
     if (st != MHC_OK) return st;
   }
   return mhc_pre_fwd(x, phi, alpha, base, T, N, D, dtype, norm_eps, hc_eps, clamp_min,

@@ -1,0 +1,274 @@
+// peer.cu -- the cross-GPU sum of the pre operator's parameter gradients
+// (grad_phi | grad_alpha | grad_base, one packed fp32 vector) over NVLink peer
+// memory, in one kernel per rank.
+//
+// Token-sharded data parallelism splits T over the ranks; grad_phi =
+// sum_t (inv*grad_mixes)[t]^T x[t] (the reference's torch.mm(grad_mixes.t(),
+// x_scaled), src/mhc_pre_clamp_sinkhorn_backward.py:1372-1373) is then a sum of
+// one partial per rank.  Every rank owns a "peer region" (cudaMalloc'd here and
+// mapped into the other ranks' address spaces with CUDA IPC):
+//
+//   [ stage: n floats ][ result: n floats ][ flags: 2 x kMaxRanks x kMaxCtas u32 ]
+//
+// The packed vector is cut into `world` slices (rank r owns slice r) and every
+// slice into `G` parts (CTA c of every rank handles part c of every slice), so a
+// CTA only ever waits for the CTAs with its own index on the other GPUs:
+//   1. CTA c copies part c of every slice of its rank's input into its stage and
+//      release-stores `epoch` into flag A[rank][c] of every rank;
+//   2. it waits until flag A[p][c] == epoch for every rank p, reads part c of its
+//      own slice from every rank's stage (NVLink loads), sums them in rank order
+//      0..world-1 (so every rank ends with bitwise the same vector) and stores the
+//      sum into part c of slice `rank` of every rank's result area (NVLink
+//      stores), then release-stores flag B[rank][c] on every rank;
+//   3. it waits until flag B[p][c] == epoch for every p (part c of every slice
+//      of its own result area is then final) and copies those parts to `dst`.
+// Step 3's wait also tells a rank that every peer has finished reading its stage,
+// so the next call may overwrite it.  All waits poll with a deadline taken from
+// the global timer; a CTA that runs out records MHC_ERR_TIMEOUT (read back by
+// mhc_device_status) and returns without touching peer memory again.
+// No TMA and no multicast: plain 16-byte loads and stores through peer pointers.
+#include <string.h>
+
+#include "common.cuh"
+
+namespace mhc {
+
+void note_launch();
+constexpr int kMaxRanks = 8;
+constexpr int kMaxCtas = 128;
+constexpr int kPeerThreads = 256;
+
+struct PeerArgs {
+  float* region[kMaxRanks];  // every rank's peer region, mapped into this process
+  const float* src;          // this rank's packed gradient
+  float* dst;                // where the sum goes (may equal src)
+  int64_t n;                 // floats in the packed vector
+  int64_t cap;               // floats the stage / result areas hold
+  int rank, world, ctas;
+  uint32_t epoch;
+  uint64_t timeout_ns;
+};
+
+static __device__ int g_peer_error;
+
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__host__ __device__ inline int64_t peer_flag_offset(int64_t cap) {
+  return 2 * cap;  // in floats; cap is a multiple of 64, so the flags are 256-byte aligned
+}
+__device__ __forceinline__ uint32_t* flag_ptr(float* region, int64_t cap, int which, int rank,
+                                              int cta) {
+  return reinterpret_cast<uint32_t*>(region + peer_flag_offset(cap)) +
+         (which * kMaxRanks + rank) * kMaxCtas + cta;
+}
+
+// Threads 0..world-1 each poll one rank's flag; the CTA agrees on the outcome.
+__device__ bool cta_wait_flags(const PeerArgs& a, int which, uint64_t deadline) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < a.world) {
+    const uint32_t* f = flag_ptr(a.region[a.rank], a.cap, which, threadIdx.x, blockIdx.x);
+    while ((int32_t)(ld_acquire_sys(f) - a.epoch) < 0) {
+      if (gtimer() > deadline) {
+        ok = 0;
+        atomicExch(&g_peer_error, MHC_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// Units of 4 floats: [u0, u1) of the whole vector is part `c` of slice `s`.
+__device__ __forceinline__ void part_range(const PeerArgs& a, int s, int c, int64_t* u0,
+                                           int64_t* u1) {
+  const int64_t units = (a.n + 3) / 4;
+  const int64_t per_slice = (units + a.world - 1) / a.world;
+  const int64_t s0 = s * per_slice, s1 = min(units, s0 + per_slice);
+  const int64_t per_part = (per_slice + a.ctas - 1) / a.ctas;
+  *u0 = min(s1, s0 + c * per_part);
+  *u1 = min(s1, *u0 + per_part);
+}
+
+__device__ __forceinline__ float4 ld4(const float* p, int64_t u, int64_t n) {
+  if (4 * u + 3 < n) return __ldcg(reinterpret_cast<const float4*>(p) + u);
+  float v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = (4 * u + k < n) ? __ldcg(p + 4 * u + k) : 0.f;
+  return make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void st4(float* p, int64_t u, int64_t n, float4 v) {
+  if (4 * u + 3 < n) {
+    __stcg(reinterpret_cast<float4*>(p) + u, v);
+    return;
+  }
+  const float w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (4 * u + k < n) __stcg(p + 4 * u + k, w[k]);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerArgs a) {
+  const int c = blockIdx.x;
+  const uint64_t deadline = gtimer() + a.timeout_ns;
+  float* mine = a.region[a.rank];
+  // 1. stage part c of every slice, then announce it to every rank
+#pragma unroll
+  for (int s = 0; s < W; ++s) {
+    int64_t u0, u1;
+    part_range(a, s, c, &u0, &u1);
+    for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) st4(mine, u, a.n, ld4(a.src, u, a.n));
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W)
+    st_release_sys(flag_ptr(a.region[threadIdx.x], a.cap, 0, a.rank, c), a.epoch);
+  // 2. sum part c of this rank's slice over the ranks, in rank order; scatter it.
+  // All W loads of a unit are issued before the first add (NVLink latency overlaps).
+  if (!cta_wait_flags(a, 0, deadline)) return;
+  {
+    int64_t u0, u1;
+    part_range(a, a.rank, c, &u0, &u1);
+    for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+      float4 v[W];
+#pragma unroll
+      for (int p = 0; p < W; ++p) v[p] = ld4(a.region[p], u, a.n);
+      float4 acc = v[0];
+#pragma unroll
+      for (int p = 1; p < W; ++p) {
+        acc.x += v[p].x; acc.y += v[p].y; acc.z += v[p].z; acc.w += v[p].w;
+      }
+#pragma unroll
+      for (int p = 0; p < W; ++p) st4(a.region[p] + a.cap, u, a.n, acc);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W)
+    st_release_sys(flag_ptr(a.region[threadIdx.x], a.cap, 1, a.rank, c), a.epoch);
+  // 3. part c of every slice of this rank's result area is final: copy it out
+  if (!cta_wait_flags(a, 1, deadline)) return;
+#pragma unroll
+  for (int s = 0; s < W; ++s) {
+    int64_t u0, u1;
+    part_range(a, s, c, &u0, &u1);
+    for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x)
+      st4(a.dst, u, a.n, ld4(mine + a.cap, u, a.n));
+  }
+}
+
+static int64_t peer_cap(int64_t n) { return (n + 63) / 64 * 64; }
+
+int peer_device_error() {
+  int v = 0, z = 0;
+  if (cudaMemcpyFromSymbol(&v, g_peer_error, sizeof(int)) != cudaSuccess) return MHC_ERR_CUDA;
+  if (v != 0 && cudaMemcpyToSymbol(g_peer_error, &z, sizeof(int)) != cudaSuccess)
+    return MHC_ERR_CUDA;
+  return v;
+}
+
+}  // namespace mhc
+
+using namespace mhc;
+
+extern "C" {
+
+size_t mhc_peer_region_bytes(int64_t n) {
+  if (n <= 0) return 0;
+  return (size_t)(peer_flag_offset(peer_cap(n)) * 4 + 2 * kMaxRanks * kMaxCtas * 4);
+}
+
+int mhc_peer_region_alloc(int64_t n, void** region) {
+  if (!region || n <= 0) return MHC_ERR_INVALID_ARGUMENT;
+  *region = nullptr;
+  const size_t bytes = mhc_peer_region_bytes(n);
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return MHC_ERR_CUDA;
+  // flags start at 0; epochs start at 1
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return MHC_ERR_CUDA;
+  }
+  *region = p;
+  return MHC_OK;
+}
+
+int mhc_peer_region_free(void* region) {
+  if (!region) return MHC_OK;
+  return cudaFree(region) == cudaSuccess ? MHC_OK : MHC_ERR_CUDA;
+}
+
+int mhc_peer_handle(void* region, void* handle_out) {
+  if (!region || !handle_out) return MHC_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, region) != cudaSuccess) return MHC_ERR_CUDA;
+  memcpy(handle_out, &h, sizeof(h));
+  return MHC_OK;
+}
+
+int mhc_peer_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int mhc_peer_open(const void* handle, void** peer_region) {
+  if (!handle || !peer_region) return MHC_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return MHC_ERR_CUDA;
+  *peer_region = p;
+  return MHC_OK;
+}
+
+int mhc_peer_close(void* peer_region) {
+  if (!peer_region) return MHC_OK;
+  return cudaIpcCloseMemHandle(peer_region) == cudaSuccess ? MHC_OK : MHC_ERR_CUDA;
+}
+
+int mhc_grad_sum_peers(const float* src, float* dst, int64_t n, void* const* regions,
+                       int32_t rank, int32_t world, uint32_t epoch, uint64_t timeout_ns,
+                       void* stream) {
+  if (n < 0 || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !regions ||
+      epoch == 0 || timeout_ns == 0)
+    return MHC_ERR_INVALID_ARGUMENT;
+  if (n == 0) return MHC_OK;
+  if (!src || !dst || ((uintptr_t)src & 15) || ((uintptr_t)dst & 15))
+    return MHC_ERR_INVALID_ARGUMENT;
+  PeerArgs a{};
+  for (int p = 0; p < world; ++p) {
+    if (!regions[p] || ((uintptr_t)regions[p] & 255)) return MHC_ERR_INVALID_ARGUMENT;
+    a.region[p] = static_cast<float*>(regions[p]);
+  }
+  a.src = src; a.dst = dst; a.n = n; a.cap = peer_cap(n);
+  a.rank = rank; a.world = world; a.epoch = epoch; a.timeout_ns = timeout_ns;
+  const int64_t units = (n + 3) / 4, per_slice = (units + world - 1) / world;
+  // about one float4 per thread and slice (latency-bound: many requests in flight);
+  // at most kMaxCtas (flag slots)
+  int64_t g = (per_slice + kPeerThreads - 1) / kPeerThreads;
+  a.ctas = (int)(g < 1 ? 1 : (g > kMaxCtas ? kMaxCtas : g));
+  using K = void (*)(const PeerArgs);
+  static const K kernels[kMaxRanks] = {peer_grad_sum_kernel<1>, peer_grad_sum_kernel<2>,
+                                       peer_grad_sum_kernel<3>, peer_grad_sum_kernel<4>,
+                                       peer_grad_sum_kernel<5>, peer_grad_sum_kernel<6>,
+                                       peer_grad_sum_kernel<7>, peer_grad_sum_kernel<8>};
+  kernels[world - 1]<<<a.ctas, kPeerThreads, 0, (cudaStream_t)stream>>>(a);
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? MHC_OK : MHC_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -28,20 +28,7 @@
 #include "pre_common.cuh"
 #include "tc.cuh"
 
-#include <stdlib.h>
 
-#ifdef MHC_PROFILE_WAITS
-// debug-only: accumulate the cycles each role spends in each barrier wait
-#define TW(slot, expr)                                   \
-  ([&]() {                                               \
-    const long long _t0 = clock64();                     \
-    const bool _r = (expr);                              \
-    wcyc[slot] += clock64() - _t0;                       \
-    return _r;                                           \
-  }())
-#else
-#define TW(slot, expr) (expr)
-#endif
 
 namespace mhc {
 
@@ -127,10 +114,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, E* __restrict__ gx,
                   float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
-                  const unsigned* __restrict__ scl,
-                  long long* __restrict__ wdbg) {
-  long long wcyc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  const long long tstart = clock64();
+                  const unsigned* __restrict__ scl) {
   using namespace bwdtc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -214,13 +198,13 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
           // the step's phi operand (4.6 MB in all, L2-resident): ahead of its x tile,
           // since the gxs MMAs need it one step before the x tile is used
           const int pb = xi & 1;
-          if (!TW(0, tc::mbar_wait(&pempty[pb], ((xi >> 1) & 1) ^ 1, abort_flag))) { ok = false; break; }
+          if (!tc::mbar_wait(&pempty[pb], ((xi >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&pfull[pb], P_BYTES);
           uint8_t* pdst = sm + OFF_P + pb * P_BYTES;
           tc::tma_load_2d(pdst, &maps.p0, &pfull[pb], 0, (int)(n * D + d0));
           tc::tma_load_2d(pdst + P0_BYTES, &maps.p1, &pfull[pb], 0, (int)(n * D + d0));
           const int s = xi % XS;
-          if (!TW(2, tc::mbar_wait(&xempty[s], ((xi / XS) & 1) ^ 1, abort_flag))) { ok = false; break; }
+          if (!tc::mbar_wait(&xempty[s], ((xi / XS) & 1) ^ 1, abort_flag)) { ok = false; break; }
           tc::mbar_arrive_expect_tx(&xfull[s], X_BYTES);
           uint8_t* dst = sm + OFF_X + s * X_BYTES;
           const int col = (int)(n * D + d0);
@@ -229,11 +213,11 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
           if (n == 0) {
             // the item's G operands (single buffers): G0/G1 once the previous item's
             // gxs MMAs are done, GP once its grad_phi MMAs are done (one step later)
-            if (!TW(1, tc::mbar_wait(gempty, (gi & 1) ^ 1, abort_flag))) { ok = false; break; }
+            if (!tc::mbar_wait(gempty, (gi & 1) ^ 1, abort_flag)) { ok = false; break; }
             tc::mbar_arrive_expect_tx(gfull, G0_BYTES + G1_BYTES);
             tc::tma_load_2d(sm + OFF_G0, &maps.g0, gfull, 0, (int)(i * 128));
             tc::tma_load_2d(sm + OFF_G1, &maps.g1, gfull, 0, (int)(i * 128));
-            if (!TW(1, tc::mbar_wait(gpempty, (gi & 1) ^ 1, abort_flag))) { ok = false; break; }
+            if (!tc::mbar_wait(gpempty, (gi & 1) ^ 1, abort_flag)) { ok = false; break; }
             tc::mbar_arrive_expect_tx(gpfull, GP_BYTES);
             tc::tma_load_2d(sm + OFF_GP, &maps.gp, gpfull, 0, (int)(i * 128));
             ++gi;
@@ -273,9 +257,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
         // ---- gxs of step st (position A)
         const int n = A.n;
         const int e = (int)(st & 1);
-        if (n == 0 && !TW(0, tc::mbar_wait(gfull, A.gi & 1, abort_flag))) return false;
-        if (!TW(0, tc::mbar_wait(&pfull[e], (uint32_t)(st >> 1) & 1, abort_flag))) return false;
-        if (!TW(1, tc::mbar_wait(&d1empty[e], ((uint32_t)(st >> 1) & 1) ^ 1, abort_flag))) return false;
+        if (n == 0 && !tc::mbar_wait(gfull, A.gi & 1, abort_flag)) return false;
+        if (!tc::mbar_wait(&pfull[e], (uint32_t)(st >> 1) & 1, abort_flag)) return false;
+        if (!tc::mbar_wait(&d1empty[e], ((uint32_t)(st >> 1) & 1) ^ 1, abort_flag)) return false;
         tc::tc_fence_after();
         const uint32_t d1 = tmem + 256 + e * 128;
         const uint64_t a0 = tc::smem_desc(sg0, 16, 1024, tc::kSwizzle128);
@@ -295,9 +279,9 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
         // ---- grad_phi of the step at position B: D2[n] (+)= x_tile^T * Gp
         const int n = B.n, s = B.s;
         const bool seg_start = B.c.seg_start;
-        if (n == 0 && seg_start && !TW(2, tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag))) return false;
-        if (n == 0 && !TW(0, tc::mbar_wait(gpfull, B.gi & 1, abort_flag))) return false;
-        if (!TW(3, tc::mbar_wait(&xfull[s], B.xph, abort_flag))) return false;
+        if (n == 0 && seg_start && !tc::mbar_wait(d2empty, (seg_b & 1) ^ 1, abort_flag)) return false;
+        if (n == 0 && !tc::mbar_wait(gpfull, B.gi & 1, abort_flag)) return false;
+        if (!tc::mbar_wait(&xfull[s], B.xph, abort_flag)) return false;
         tc::tc_fence_after();
         const uint32_t d2 = tmem + n * 64;
         const uint32_t sx = sx0 + s * X_BYTES;
@@ -381,12 +365,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
       const int64_t item = cur.item, i = cur.i;
       const int64_t d0 = cur.g * GC;
       const int64_t row0 = i * 128 + q * 32;  // first token row of this warp's store box
-#ifdef MHC_PROFILE_WAITS
-      const long long _p4 = clock64();
-#endif
-#ifdef MHC_PROFILE_WAITS
-      wcyc[4] += clock64() - _p4;
-#endif
       bool ok = true;
       for (int n = 0; n < N; ++n, ++di) {
         const int e = di & 1, s = di % XS;
@@ -399,18 +377,15 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
           tc::mbar_arrive_expect_tx(mybar, OUT_BYTES);
           tc::tma_load_2d(ob, &maps.gxa, mybar, (int)(n * D + d0 + h * 32), (int)row0);
         }
-        if (!__all_sync(0xffffffffu, TW(0, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag)))) {
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&d1full[e], (di >> 1) & 1, abort_flag))) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        if (!__all_sync(0xffffffffu, TW(1, tc::mbar_wait(&xfull[s], xph, abort_flag)))) {
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&xfull[s], xph, abort_flag))) {
           ok = false;
           break;
         }
-#ifdef MHC_PROFILE_WAITS
-        const long long _p3 = clock64();
-#endif
         // x row r, columns [32h, 32h+32): box h/2, 16-byte chunks 4(h%2)..+3 (swizzled)
         const uint8_t* xrow = sm + OFF_X + s * X_BYTES + (h >> 1) * (X_BYTES / 2) + r * 128;
         uint4 xv[4];
@@ -422,10 +397,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
         tc::fence_proxy_async();        // generic smem reads before the TMA refill
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&xempty[s]);
-#ifdef MHC_PROFILE_WAITS
-        long long _p2 = clock64();
-        wcyc[3] += _p2 - _p3;
-#endif
         // gxs in two halves of 16 columns (keeps the live registers under the 96 that
         // 18 warps per CTA allow).  grad_x goes through this warp's own 2 KB buffer
         // ([32 tok][32 col], 64-byte swizzle: chunk c of row r at (c ^ (r/2 % 4))) and
@@ -491,9 +462,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
           tc::tma_store_2d(&maps.gx, ob, (int)(n * D + d0 + h * 32), (int)row0);
           tc::bulk_commit_group();
         }
-#ifdef MHC_PROFILE_WAITS
-        wcyc[5] += clock64() - _p2;
-#endif
         if (item + 1 < it1 && (n == 0 || n == N - 1)) {
           const bool wrap = cur.i + 1 == ntiles;
           const int64_t gn = wrap ? cur.g + 1 : cur.g, in = wrap ? 0 : i + 1;
@@ -509,7 +477,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
       if (!ok) break;
       if (cur.seg_end) {
         // flush: D2[h] row r = column d0 + r; cols k: hi k, lo 24 + k
-        if (!__all_sync(0xffffffffu, TW(2, tc::mbar_wait(d2full, seg & 1, abort_flag)))) break;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(d2full, seg & 1, abort_flag))) break;
         tc::tc_fence_after();
         // slot 1 iff this CTA's run began inside the cell
         const int64_t slot = (cur.g * geo.cpg + cur.i / cur.subt) * 2 +
@@ -532,16 +500,6 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
   }
   if (warp >= 2 && lane == 0) tc::bulk_wait_all<0>();  // grad_x stores have landed
   if (*abort_flag && threadIdx.x == 0) flag_timeout();
-#ifdef MHC_PROFILE_WAITS
-  // row per CTA: [total, producer x4, mma x4, epilogue warp 2 x4]
-  if (wdbg != nullptr && lane == 0 && (warp <= 2)) {
-    long long* row = wdbg + (int64_t)blockIdx.x * 32;
-    if (warp == 0) row[0] = clock64() - tstart;
-    for (int k = 0; k < 8; ++k) row[1 + warp * 8 + k] = wcyc[k];
-  }
-#else
-  (void)wdbg; (void)tstart; (void)wcyc;
-#endif
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -817,15 +775,7 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
   auto kern = a.grad_x_acc ? pre_bwd_tc_kernel<true, E> : pre_bwd_tc_kernel<false, E>;
   kern<<<geo.ncta, THREADS, SMEM, s>>>(m, (const E*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
-                                                    (E*)a.grad_x, w.part, T, D, geo, scl,
-#ifdef MHC_PROFILE_WAITS
-                                                    getenv("MHC_WAIT_DBG")
-                                                        ? (long long*)strtoull(getenv("MHC_WAIT_DBG"), nullptr, 10)
-                                                        : nullptr
-#else
-                                                    nullptr
-#endif
-  );
+                                                    (E*)a.grad_x, w.part, T, D, geo, scl);
   MHC_LAUNCH_CHECK();
   const int64_t n = (D / GC) * N * HM * GC;
   pre_bwd_gphi_reduce_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.part, a.grad_phi, D, geo,

@@ -161,6 +161,42 @@ int mhc_pre_bwd_accumulate(const void* x, const float* phi, const float* alpha,
                            float* grad_base, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/*
+ * Cross-GPU sum of the pre operator's parameter gradients over NVLink peer
+ * memory (token-sharded data parallelism, one process per GPU).  No
+ * counterpart in the reference, which has no distributed code: it replaces the
+ * NCCL all-reduce of the packed [grad_phi | grad_alpha | grad_base] vector that
+ * a data-parallel caller would run after mhc_pre_bwd (the sum of the per-rank
+ * terms of the reference's grad_phi = torch.mm(grad_mixes.t(), x_scaled),
+ * src/mhc_pre_clamp_sinkhorn_backward.py:1372-1373).
+ *
+ * Set-up, once per job (collective over the ranks, host side):
+ *   each rank  mhc_peer_region_alloc(n, &region)       (cudaMalloc, zeroed)
+ *              mhc_peer_handle(region, handle)           (CUDA IPC handle,
+ *                                                        mhc_peer_handle_bytes())
+ *   exchange the handles (any host channel), then for every other rank p
+ *              mhc_peer_open(handle_p, &regions[p]);    regions[rank] = region
+ * Per call (all ranks, same n, same epoch sequence 1, 2, 3, ...):
+ *   mhc_grad_sum_peers(src, dst, n, regions, rank, world, epoch, timeout_ns, s)
+ * writes the sum over the ranks of src (n floats) into dst (may equal src), in
+ * rank order, so every rank gets bitwise the same vector.  One kernel launch,
+ * stream-ordered.  Every wait for a peer gives up after timeout_ns; the kernel
+ * then records MHC_ERR_TIMEOUT (returned by mhc_device_status), dst is not
+ * valid, and the regions must be re-created before the next call.
+ * Tear-down: mhc_peer_close on every opened peer region, a host barrier, then
+ * mhc_peer_region_free.  world <= 8; src and dst 16-byte aligned.
+ */
+size_t mhc_peer_region_bytes(int64_t n);
+int mhc_peer_region_alloc(int64_t n, void** region);
+int mhc_peer_region_free(void* region);
+int mhc_peer_handle_bytes(void);
+int mhc_peer_handle(void* region, void* handle_out);
+int mhc_peer_open(const void* handle, void** peer_region);
+int mhc_peer_close(void* peer_region);
+int mhc_grad_sum_peers(const float* src, float* dst, int64_t n,
+                       void* const* regions, int32_t rank, int32_t world,
+                       uint32_t epoch, uint64_t timeout_ns, void* stream);
+
 /* Size of the static device scratch array used by mhc_pre_fwd_noalloc. */
 #define MHC_PRE_FWD_NOALLOC_SCRATCH_BYTES (16u << 20)
 
@@ -172,10 +208,14 @@ int mhc_pre_bwd_accumulate(const void* x, const float* phi, const float* alpha,
  * not call cudaMalloc where they run the operator (an arena or pooled
  * allocator that owns the device budget; a cgo/JNI/C binding with no device
  * allocator).  Returns MHC_ERR_SCRATCH_LIMIT when
- * mhc_pre_fwd_workspace_bytes(T,N,D,dtype) exceeds the array.  All calls on a
- * device share the array: calls that overlap on the GPU race.  The first call
- * on each device looks up the array's address; make it before any stream
- * capture begins.
+ * mhc_pre_fwd_workspace_bytes(T,N,D,dtype) exceeds the array: N=4 at D <= 7168
+ * fits up to T = 167,770 tokens, N=8 at D = 4096 up to T = 51,780, and N=8 at
+ * D = 7168 never fits.  All calls on a device share the array: calls that
+ * overlap on the GPU race.  Every call made outside stream capture looks the
+ * array's address up for the current device and context (so a context re-created
+ * after cudaDeviceReset is handled); a call inside a capture reuses the address of
+ * the last uncaptured call on the device, so make one call on each device before
+ * any capture begins, and again after a cudaDeviceReset.
  */
 int mhc_pre_fwd_noalloc(const void* x, const float* phi, const float* alpha,
                         const float* base, int64_t T, int32_t N, int64_t D,

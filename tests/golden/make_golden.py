@@ -42,8 +42,11 @@ def _np(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MHC_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("MHC_REFERENCE"),
+                    help="checkout of liuhycs/FlagOS-mhc (or set MHC_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref <reference checkout> or set MHC_REFERENCE")
     sys.path.insert(0, args.ref)
     from src import (mhc_post_ref, mhc_post_backward_ref, mhc_pre_clamp_sinkhorn_ref,
                      mhc_pre_clamp_sinkhorn_backward_ref)

@@ -81,3 +81,13 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     st = _call(L, "mhc_pre_fwd_noalloc", x, phi, alpha, base, o, T, 4, 7168)
     assert st == _C.MHC_ERR_SCRATCH_LIMIT
     assert b"scratch" in L.mhc_status_string(st)
+    # N=8 at D=7168: the bf16 hi/lo split of phi alone (160 x 57344 bf16) is over
+    # the limit, so even one token is rejected
+    assert L.mhc_pre_fwd_workspace_bytes(1, 8, 7168, _C.MHC_BF16) > limit
+    st = _call(L, "mhc_pre_fwd_noalloc", x, phi, alpha, base, o, 1, 8, 7168)
+    assert st == _C.MHC_ERR_SCRATCH_LIMIT
+    # the documented limits: N=4, D=7168 up to T=167,770; N=8, D=4096 up to T=51,780
+    assert L.mhc_pre_fwd_workspace_bytes(167770, 4, 7168, _C.MHC_BF16) <= limit
+    assert L.mhc_pre_fwd_workspace_bytes(167771, 4, 7168, _C.MHC_BF16) > limit
+    assert L.mhc_pre_fwd_workspace_bytes(51780, 8, 4096, _C.MHC_BF16) <= limit
+    assert L.mhc_pre_fwd_workspace_bytes(51781, 8, 4096, _C.MHC_BF16) > limit
