@@ -36,6 +36,7 @@ _SIGS = {
     "mhc_version": (ctypes.c_int, []),
     "mhc_kernel_launches": (ctypes.c_uint64, []),
     "mhc_device_status": (ctypes.c_int, []),
+    "mhc_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, _vp]),
     "mhc_post_fwd": (ctypes.c_int, [_vp, _fp, _vp, _fp, _vp, _i64, _i32, _i64, _i32, _vp]),
     "mhc_post_bwd": (ctypes.c_int, [_vp, _vp, _fp, _vp, _fp, _vp, _fp, _vp, _fp, _i64, _i32,
                                     _i64, _i32, _vp]),

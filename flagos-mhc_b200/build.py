@@ -42,6 +42,8 @@ def _compile(src, extra, verbose):
     obj = os.path.join(BUILD, f"{base}.{tag}.o")
     if os.path.exists(obj):
         return obj, ""
+    for old in glob.glob(os.path.join(BUILD, f"{base}.*.o")):  # stale objects of this source
+        os.remove(old)
     cmd = [NVCC] + ARCH + FLAGS + extra + ["-c", src, "-o", obj + ".tmp"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

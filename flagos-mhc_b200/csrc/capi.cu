@@ -20,6 +20,7 @@ int pre_fwd_tc_device_error();
 int pre_bwd_tc_device_error();
 int pre_bwd_tc8_device_error();
 int peer_device_error();
+int tc_host_device_error();
 
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
@@ -112,7 +113,11 @@ int mhc_device_status(void) {
   const int b = pre_bwd_tc_device_error();
   const int c = pre_bwd_tc8_device_error();
   const int d = peer_device_error();
-  return a != MHC_OK ? a : (b != MHC_OK ? b : (c != MHC_OK ? c : d));
+  const int e = tc_host_device_error();
+  const int all[5] = {a, b, c, d, e};
+  for (int v : all)
+    if (v != MHC_OK) return v;
+  return MHC_OK;
 }
 
 int mhc_post_fwd(const void* x, const float* h_res, const void* h_out, const float* h_post,

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/mhc_b200.h"
 
 namespace mhc {
@@ -283,6 +285,42 @@ __device__ __forceinline__ void small_forward(const float* mix, const float* bas
   } while (0)
 
 void note_launch();
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of this library is launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization, so its CTAs may become
+// resident while the previous kernel on the stream is still finishing (its last
+// wave); each kernel runs only set-up that reads no global memory (shared-memory
+// carve-up, mbarrier init, TMEM allocation, tensor-map prefetch) before
+// pdl_wait(), which returns once the previous grid has completed and its writes
+// are visible.  pdl_trigger() (issued by every CTA right after its pdl_wait())
+// lets the next kernel launch as soon as all CTAs of this one are running.
+// Without the attribute (or with no kernel in flight before it) both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 #define MHC_DISPATCH_N(N_, FN, ...)                          \
   switch (N_) {                                              \

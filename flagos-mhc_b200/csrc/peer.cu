@@ -87,11 +87,24 @@ __device__ bool cta_wait_flags(const PeerArgs& a, int which, uint64_t deadline) 
         atomicExch(&g_peer_error, MHC_ERR_TIMEOUT);
         break;
       }
-      __nanosleep(128);
+      __nanosleep(32);
     }
   }
   __syncthreads();
   return ok != 0;
+}
+
+// Publishes this CTA's writes (stage or result parts) to every rank: the barrier makes
+// them happen before thread 0's system-scope fence, which orders them before the flag
+// stores (release at system scope is cumulative over what the thread has observed).
+template <int W>
+__device__ __forceinline__ void cta_signal(const PeerArgs& a, int which, int c) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+#pragma unroll
+    for (int p = 0; p < W; ++p) st_release_sys(flag_ptr(a.region[p], a.cap, which, a.rank, c), a.epoch);
+  }
 }
 
 // Units of 4 floats: [u0, u1) of the whole vector is part `c` of slice `s`.
@@ -112,6 +125,26 @@ __device__ __forceinline__ float4 ld4(const float* p, int64_t u, int64_t n) {
   for (int k = 0; k < 4; ++k) v[k] = (4 * u + k < n) ? __ldcg(p + 4 * u + k) : 0.f;
   return make_float4(v[0], v[1], v[2], v[3]);
 }
+// Loads of another rank's stage: system-scope relaxed loads (never served from a stale
+// cached copy of a previous call's values).
+__device__ __forceinline__ float4 ld4_sys(const float* p, int64_t u, int64_t n) {
+  if (4 * u + 3 < n) {
+    float4 v;
+    asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(reinterpret_cast<const float4*>(p) + u)
+                 : "memory");
+    return v;
+  }
+  float v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[k] = 0.f;
+    if (4 * u + k < n)
+      asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v[k]) : "l"(p + 4 * u + k) : "memory");
+  }
+  return make_float4(v[0], v[1], v[2], v[3]);
+}
 __device__ __forceinline__ void st4(float* p, int64_t u, int64_t n, float4 v) {
   if (4 * u + 3 < n) {
     __stcg(reinterpret_cast<float4*>(p) + u, v);
@@ -125,6 +158,7 @@ __device__ __forceinline__ void st4(float* p, int64_t u, int64_t n, float4 v) {
 
 template <int W>
 __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerArgs a) {
+  pdl_enter();
   const int c = blockIdx.x;
   const uint64_t deadline = gtimer() + a.timeout_ns;
   float* mine = a.region[a.rank];
@@ -135,10 +169,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
     part_range(a, s, c, &u0, &u1);
     for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) st4(mine, u, a.n, ld4(a.src, u, a.n));
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < W)
-    st_release_sys(flag_ptr(a.region[threadIdx.x], a.cap, 0, a.rank, c), a.epoch);
+  cta_signal<W>(a, 0, c);
   // 2. sum part c of this rank's slice over the ranks, in rank order; scatter it.
   // All W loads of a unit are issued before the first add (NVLink latency overlaps).
   if (!cta_wait_flags(a, 0, deadline)) return;
@@ -148,7 +179,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
     for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
       float4 v[W];
 #pragma unroll
-      for (int p = 0; p < W; ++p) v[p] = ld4(a.region[p], u, a.n);
+      for (int p = 0; p < W; ++p) v[p] = ld4_sys(a.region[p], u, a.n);
       float4 acc = v[0];
 #pragma unroll
       for (int p = 1; p < W; ++p) {
@@ -158,10 +189,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
       for (int p = 0; p < W; ++p) st4(a.region[p] + a.cap, u, a.n, acc);
     }
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < W)
-    st_release_sys(flag_ptr(a.region[threadIdx.x], a.cap, 1, a.rank, c), a.epoch);
+  cta_signal<W>(a, 1, c);
   // 3. part c of every slice of this rank's result area is final: copy it out
   if (!cta_wait_flags(a, 1, deadline)) return;
 #pragma unroll
@@ -266,7 +294,7 @@ int mhc_grad_sum_peers(const float* src, float* dst, int64_t n, void* const* reg
                                        peer_grad_sum_kernel<3>, peer_grad_sum_kernel<4>,
                                        peer_grad_sum_kernel<5>, peer_grad_sum_kernel<6>,
                                        peer_grad_sum_kernel<7>, peer_grad_sum_kernel<8>};
-  kernels[world - 1]<<<a.ctas, kPeerThreads, 0, (cudaStream_t)stream>>>(a);
+  launch(kernels[world - 1], a.ctas, kPeerThreads, 0, (cudaStream_t)stream, a);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? MHC_OK : MHC_ERR_CUDA;
 }

@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256)
 post_fwd_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                 const E* __restrict__ h_out, const float* __restrict__ h_post,
                 E* __restrict__ out, int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -63,6 +64,7 @@ post_bwd_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                 const float* __restrict__ h_post, E* __restrict__ gx,
                 float* __restrict__ ghres, E* __restrict__ ghout,
                 float* __restrict__ ghpost, int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -169,6 +171,7 @@ __global__ void __launch_bounds__(256, 2)
 post_fwd_x16_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                     const E* __restrict__ h_out, const float* __restrict__ h_post,
                     E* __restrict__ out, int64_t T, int64_t D) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
   const int64_t nchunk = D / 16;
@@ -314,6 +317,7 @@ __global__ void __launch_bounds__(256)
 post_fwd_n8_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                    const E* __restrict__ h_out, const float* __restrict__ h_post,
                    E* __restrict__ out, int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int N = 8, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -356,6 +360,7 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                    const float* __restrict__ h_post, E* __restrict__ gx,
                    float* __restrict__ ghres, E* __restrict__ ghout,
                    float* __restrict__ ghpost, int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int N = 8, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -430,6 +435,7 @@ post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                      const float* __restrict__ h_post, E* __restrict__ gx,
                      float* __restrict__ ghres, E* __restrict__ ghout,
                      float* __restrict__ ghpost, int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int N = 4, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int tb = g >> 2, j = g & 3;            // token of the pair, row of the token
@@ -534,19 +540,19 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 8) {
     if (D % 128 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
-      post_fwd_n8_kernel<E, 4><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
+      launch(post_fwd_n8_kernel<E, 4>, grid, block, 0, s, (const E*)x, h_res, (const E*)h_out,
                                                       h_post, (E*)out, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
     if (D % 64 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
-      post_fwd_n8_kernel<E, 2><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
+      launch(post_fwd_n8_kernel<E, 2>, grid, block, 0, s, (const E*)x, h_res, (const E*)h_out,
                                                       h_post, (E*)out, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
     if (D % 32 == 0 && vec) {
-      post_fwd_n8_kernel<E, 1><<<grid, block, 0, s>>>((const E*)x, h_res, (const E*)h_out,
+      launch(post_fwd_n8_kernel<E, 1>, grid, block, 0, s, (const E*)x, h_res, (const E*)h_out,
                                                       h_post, (E*)out, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
@@ -555,20 +561,20 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
   if constexpr (sizeof(E) == 2 && N <= 4) {
     if (D % 16 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
       if (T < (int64_t)sm_count() * 8)  // small T (fewer than 8 tokens per SM): a block per token
-        post_fwd_x16_kernel<E, N, true><<<(unsigned)T, block, 0, s>>>(
+        launch(post_fwd_x16_kernel<E, N, true>, (unsigned)T, block, 0, s, 
             (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
       else
-        post_fwd_x16_kernel<E, N, false><<<grid, block, 0, s>>>(
+        launch(post_fwd_x16_kernel<E, N, false>, grid, block, 0, s, 
             (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
   }
   if (vec)
-    post_fwd_kernel<E, N, true><<<grid, block, 0, s>>>(
+    launch(post_fwd_kernel<E, N, true>, grid, block, 0, s, 
         (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
   else
-    post_fwd_kernel<E, N, false><<<grid, block, 0, s>>>(
+    launch(post_fwd_kernel<E, N, false>, grid, block, 0, s, 
         (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
@@ -592,11 +598,11 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
 #define MHC_N4X2(VV)                                                                        \
   do {                                                                                      \
     if (split)                                                                              \
-      post_bwd_n4x2_kernel<E, VV, true><<<sgrid, block, 0, s>>>(                            \
+      launch(post_bwd_n4x2_kernel<E, VV, true>, sgrid, block, 0, s,                             \
           (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,         \
           (E*)ghout, ghpost, T, D);                                                         \
     else                                                                                    \
-      post_bwd_n4x2_kernel<E, VV, false><<<pgrid, block, 0, s>>>(                           \
+      launch(post_bwd_n4x2_kernel<E, VV, false>, pgrid, block, 0, s,                            \
           (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,         \
           (E*)ghout, ghpost, T, D);                                                         \
     MHC_LAUNCH_CHECK();                                                                     \
@@ -609,7 +615,7 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
   if constexpr (sizeof(E) == 2 && N == 8) {
     if (D % 128 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
         aligned32(ghout)) {
-      post_bwd_n8_kernel<E, 4><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+      launch(post_bwd_n8_kernel<E, 4>, grid, block, 0, s, (const E*)gy, (const E*)x, h_res,
                                                       (const E*)h_out, h_post, (E*)gx, ghres,
                                                       (E*)ghout, ghpost, T, D);
       MHC_LAUNCH_CHECK();
@@ -617,14 +623,14 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
     }
     if (D % 64 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
         aligned32(ghout)) {
-      post_bwd_n8_kernel<E, 2><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+      launch(post_bwd_n8_kernel<E, 2>, grid, block, 0, s, (const E*)gy, (const E*)x, h_res,
                                                       (const E*)h_out, h_post, (E*)gx, ghres,
                                                       (E*)ghout, ghpost, T, D);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
     if (D % 32 == 0 && vec) {
-      post_bwd_n8_kernel<E, 1><<<grid, block, 0, s>>>((const E*)gy, (const E*)x, h_res,
+      launch(post_bwd_n8_kernel<E, 1>, grid, block, 0, s, (const E*)gy, (const E*)x, h_res,
                                                       (const E*)h_out, h_post, (E*)gx, ghres,
                                                       (E*)ghout, ghpost, T, D);
       MHC_LAUNCH_CHECK();
@@ -632,11 +638,11 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
     }
   }
   if (vec)
-    post_bwd_kernel<E, N, true><<<grid, block, 0, s>>>(
+    launch(post_bwd_kernel<E, N, true>, grid, block, 0, s, 
         (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,
         (E*)ghout, ghpost, T, D);
   else
-    post_bwd_kernel<E, N, false><<<grid, block, 0, s>>>(
+    launch(post_bwd_kernel<E, N, false>, grid, block, 0, s, 
         (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,
         (E*)ghout, ghpost, T, D);
   MHC_LAUNCH_CHECK();

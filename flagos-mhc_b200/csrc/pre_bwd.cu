@@ -28,6 +28,7 @@ template <typename E, int N, bool VEC, bool SPLIT>
 __global__ void __launch_bounds__(256)
 pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                     float* __restrict__ gpre, int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
@@ -126,6 +127,7 @@ pre_small_bwd_kernel(const float* __restrict__ mixes, const float* __restrict__ 
                      float* __restrict__ coef_out, float* __restrict__ partials,
                      __nv_bfloat16* __restrict__ g0, __nv_bfloat16* __restrict__ g1,
                      __nv_bfloat16* __restrict__ gp) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   constexpr int NN = N * N;
   constexpr int NP = 3 + HM;
@@ -287,6 +289,7 @@ pre_small_bwd_rows_kernel(const float* __restrict__ mixes, const float* __restri
                           float* __restrict__ coef_out, float* __restrict__ partials,
                           __nv_bfloat16* __restrict__ g0, __nv_bfloat16* __restrict__ g1,
                           __nv_bfloat16* __restrict__ gp) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   constexpr int NN = N * N;
   constexpr int NP = 3 + HM;
@@ -490,6 +493,7 @@ pre_small_bwd_rows_kernel(const float* __restrict__ mixes, const float* __restri
 __global__ void pre_reduce_ab_kernel(const float* __restrict__ partials, int nblk, int HM,
                                      float* __restrict__ grad_alpha,
                                      float* __restrict__ grad_base) {
+  pdl_enter();
   const int NP = 3 + HM;
   const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (w >= NP) return;
@@ -512,6 +516,7 @@ pre_bwd_gx_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, const E* acc, E* gx,  // may alias
                   int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   const int64_t HC = (int64_t)N * D;
   __shared__ float sgm[kGxTT][HM];
@@ -561,6 +566,7 @@ __global__ void __launch_bounds__(kGpCC)
 pre_bwd_gphi_kernel(const E* __restrict__ x, const float* __restrict__ gm,
                     const float* __restrict__ inv_rms, float* __restrict__ part, int64_t T,
                     int64_t HC, int64_t tokens_per_split) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   __shared__ float sg[kGpTS][HM];
   const int64_t c = (int64_t)blockIdx.x * kGpCC + threadIdx.x;
@@ -593,6 +599,7 @@ pre_bwd_gphi_kernel(const E* __restrict__ x, const float* __restrict__ gm,
 
 __global__ void pre_reduce_gphi_kernel(const float* __restrict__ part, int nsplit, int64_t n,
                                        float* __restrict__ out) {
+  pdl_enter();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float s = 0.f;
@@ -688,13 +695,13 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   // small T (fewer than 8 tokens per SM): a block per token, its warps split the row
   const bool dsplit = T < cap;
   if (vec && dsplit)
-    pre_bwd_dots_kernel<E, N, true, true><<<(unsigned)T, 256, 0, s>>>(
+    launch(pre_bwd_dots_kernel<E, N, true, true>, (unsigned)T, 256, 0, s, 
         (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
   else if (vec)
-    pre_bwd_dots_kernel<E, N, true, false><<<sgrid, 256, 0, s>>>(
+    launch(pre_bwd_dots_kernel<E, N, true, false>, sgrid, 256, 0, s, 
         (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
   else
-    pre_bwd_dots_kernel<E, N, false, false><<<sgrid, 256, 0, s>>>(
+    launch(pre_bwd_dots_kernel<E, N, false, false>, sgrid, 256, 0, s, 
         (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
   MHC_LAUNCH_CHECK();
   // small-stage VJP.  Row-parallel (N lanes per token, N = 4, 8) while a thread per token
@@ -705,32 +712,32 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const bool rows = rows_ok && cdiv(T, 128) < sm_count();
   const int nblk = (int)cdiv(T, rows ? 128 / N : 128);
   if (rows)
-    pre_small_bwd_rows_kernel<rows_ok ? N : 4><<<nblk, 128, 0, s>>>(
+    launch(pre_small_bwd_rows_kernel<rows_ok ? N : 4>, nblk, 128, 0, s, 
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   else
-    pre_small_bwd_kernel<N><<<nblk, 128, 0, s>>>(
+    launch(pre_small_bwd_kernel<N>, nblk, 128, 0, s, 
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   MHC_LAUNCH_CHECK();
-  pre_reduce_ab_kernel<<<(unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s>>>(w.partials, nblk, HM,
+  launch(pre_reduce_ab_kernel, (unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s, w.partials, nblk, HM,
                                                                        a.grad_alpha, a.grad_base);
   MHC_LAUNCH_CHECK();
   if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.gm, w.coef, s);
   if (use_tc8) return pre_bwd_tc8_main(a, tc_ws, w.gm, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
-  pre_bwd_gx_kernel<E, N><<<ggrid, kGxCC, 0, s>>>((const E*)a.x, (const E*)a.grad_y, a.phi,
+  launch(pre_bwd_gx_kernel<E, N>, ggrid, kGxCC, 0, s, (const E*)a.x, (const E*)a.grad_y, a.phi,
                                                   w.gm, a.inv_rms, w.coef, a.pre,
                                                   (const E*)a.grad_x_acc, (E*)a.grad_x, T, D);
   MHC_LAUNCH_CHECK();
   const int ns = gphi_splits(T);
   const int64_t tps = cdiv(T, ns);
   dim3 pgrid((unsigned)cdiv(HC, kGpCC), (unsigned)ns);
-  pre_bwd_gphi_kernel<E, N><<<pgrid, kGpCC, 0, s>>>((const E*)a.x, w.gm, a.inv_rms,
+  launch(pre_bwd_gphi_kernel<E, N>, pgrid, kGpCC, 0, s, (const E*)a.x, w.gm, a.inv_rms,
                                                     w.gphi_part, T, HC, tps);
   MHC_LAUNCH_CHECK();
   const int64_t n = (int64_t)HM * HC;
-  pre_reduce_gphi_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.gphi_part, ns, n, a.grad_phi);
+  launch(pre_reduce_gphi_kernel, (unsigned)cdiv(n, 256), 256, 0, s, w.gphi_part, ns, n, a.grad_phi);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
 }

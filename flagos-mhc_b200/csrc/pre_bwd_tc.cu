@@ -115,6 +115,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
                   const float* __restrict__ pre, E* __restrict__ gx,
                   float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
                   const unsigned* __restrict__ scl) {
+  pdl_enter();
   using namespace bwdtc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -510,32 +511,38 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
 
 // phi (fp32 [HM][HC]) -> per-column bf16 operand rows P' = [phi_hi | phi_hi | phi_lo | 0]
 // split into P0 [HC][64] and P1 [HC][16].
+// P0 [HC][64] = [phi_hi 0..23 | phi_hi 0..23 | phi_lo 0..15], P1 [HC][16] = [phi_lo 16..23 |
+// 0 x 8].  Thread (c, g) handles column c and mixes 8g..8g+7 (three threads per column).
 template <typename E>
 __global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi, E* __restrict__ p0,
                                         E* __restrict__ p1, int64_t HC,
                                         const unsigned* __restrict__ scl) {
+  pdl_enter();
   using namespace bwdtc;
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  static_assert(HM == 24, "three groups of eight mixes");
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t c = idx / 3;
+  const int g = (int)(idx - c * 3);
   if (c >= HC) return;
   const float sc = scl ? f16_operand_scale(scl[0]) : 1.f;
-  E row[KG];
+  float hi[8], lo[8];
 #pragma unroll
-  for (int k = 0; k < HM; ++k) {
-    const float p = phi[(int64_t)k * HC + c] * sc;
-    const E hi = to_e<E>(p);
-    row[k] = hi;
-    row[HM + k] = hi;
-    row[2 * HM + k] = to_e<E>(p - from_e(hi));
+  for (int k = 0; k < 8; ++k) {
+    const float p = phi[(int64_t)(8 * g + k) * HC + c] * sc;
+    hi[k] = from_e(to_e<E>(p));
+    lo[k] = p - hi[k];
   }
-#pragma unroll
-  for (int k = 3 * HM; k < KG; ++k) row[k] = to_e<E>(0.f);
-  const uint4* rv = reinterpret_cast<const uint4*>(row);
   uint4* d0 = reinterpret_cast<uint4*>(p0 + c * 64);
-  uint4* d1 = reinterpret_cast<uint4*>(p1 + c * 16);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) d0[j] = rv[j];
-  d1[0] = rv[8];
-  d1[1] = rv[9];
+  const uint4 vh = narrow<E>(hi), vl = narrow<E>(lo);
+  d0[g] = vh;
+  d0[3 + g] = vh;
+  if (g < 2) {
+    d0[6 + g] = vl;
+  } else {
+    uint4* d1 = reinterpret_cast<uint4*>(p1 + c * 16);
+    d1[0] = vl;
+    d1[1] = make_uint4(0u, 0u, 0u, 0u);
+  }
 }
 
 // grad_phi[k][n*D + g*128 + c] = sum over the cells of group g (in order) of slot 0,
@@ -546,6 +553,7 @@ constexpr int kMaxCellsPerGroup = 4096;
 __global__ void __launch_bounds__(256)
 pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ grad_phi,
                            int64_t D, BwdGeom geo, const unsigned* __restrict__ scl) {
+  pdl_enter();
   using namespace bwdtc;
   constexpr int64_t SLOT = (int64_t)N * HM * GC;
   static_assert(SLOT % 256 == 0, "a block must not straddle two groups");
@@ -585,6 +593,7 @@ __global__ void pre_bwd_f16_max_kernel(const float* __restrict__ phi, int64_t np
                                        const float* __restrict__ gm,
                                        const float* __restrict__ inv_rms, int64_t T,
                                        unsigned* __restrict__ scl) {
+  pdl_enter();
   using namespace bwdtc;
   float mp = 0.f, mg = 0.f, mgp = 0.f;
   const int64_t ng = T * HM, n = nphi > ng ? nphi : ng;
@@ -617,6 +626,7 @@ __global__ void pre_bwd_g_prep_f16_kernel(const float* __restrict__ gm,
                                           const float* __restrict__ inv_rms, __half* __restrict__ g0,
                                           __half* __restrict__ g1, __half* __restrict__ gp,
                                           int64_t T, const unsigned* __restrict__ scl) {
+  pdl_enter();
   using namespace bwdtc;
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
@@ -726,14 +736,13 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
   if (f16) {
     MHC_CUDA_CHECK(cudaMemsetAsync(w.scl, 0, 3 * sizeof(unsigned), s));
     const int64_t n = std::max<int64_t>((int64_t)HM * HC, T * HM);
-    pre_bwd_f16_max_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 4),
-                             256, 0, s>>>(a.phi, (int64_t)HM * HC, gm, a.inv_rms, T, w.scl);
+    launch(pre_bwd_f16_max_kernel, (unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 4), 256, 0, s, a.phi, (int64_t)HM * HC, gm, a.inv_rms, T, w.scl);
     MHC_LAUNCH_CHECK();
-    pre_bwd_g_prep_f16_kernel<<<(unsigned)cdiv(T, 128), 128, 0, s>>>(
+    launch(pre_bwd_g_prep_f16_kernel, (unsigned)cdiv(T, 128), 128, 0, s, 
         gm, a.inv_rms, (__half*)w.g0, (__half*)w.g1, (__half*)w.gp, T, w.scl);
     MHC_LAUNCH_CHECK();
   }
-  pre_bwd_phi_prep_kernel<E><<<(unsigned)cdiv(HC, 256), 256, 0, s>>>(a.phi, (E*)w.p0, (E*)w.p1,
+  launch(pre_bwd_phi_prep_kernel<E>, (unsigned)cdiv(3 * HC, 256), 256, 0, s, a.phi, (E*)w.p0, (E*)w.p1,
                                                                      HC, scl);
   MHC_LAUNCH_CHECK();
   BwdTcMaps m;
@@ -773,12 +782,12 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
     attr_set[dev] = true;
   }
   auto kern = a.grad_x_acc ? pre_bwd_tc_kernel<true, E> : pre_bwd_tc_kernel<false, E>;
-  kern<<<geo.ncta, THREADS, SMEM, s>>>(m, (const E*)a.grad_y,
+  launch(kern, geo.ncta, THREADS, SMEM, s, m, (const E*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
                                                     (E*)a.grad_x, w.part, T, D, geo, scl);
   MHC_LAUNCH_CHECK();
   const int64_t n = (D / GC) * N * HM * GC;
-  pre_bwd_gphi_reduce_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(w.part, a.grad_phi, D, geo,
+  launch(pre_bwd_gphi_reduce_kernel, (unsigned)cdiv(n, 256), 256, 0, s, w.part, a.grad_phi, D, geo,
                                                                    scl);
   MHC_LAUNCH_CHECK();
   return MHC_OK;

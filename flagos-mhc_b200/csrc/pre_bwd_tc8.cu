@@ -83,6 +83,7 @@ static_assert(SMEM <= 232448, "shared memory");
 // Thread per (column, 8-element chunk): the 16-byte stores of a warp are contiguous.
 __global__ void bwd8_phi_prep_kernel(const float* __restrict__ phi, __nv_bfloat16* __restrict__ p,
                                      int64_t HC) {
+  pdl_enter();
   using namespace bwd8;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= HC * (KG / 8)) return;
@@ -109,6 +110,7 @@ __global__ void bwd8_phi_prep_kernel(const float* __restrict__ phi, __nv_bfloat1
 __global__ void bwd8_g_prep_kernel(const float* __restrict__ gm, const float* __restrict__ inv_rms,
                                    __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ gpo,
                                    int64_t T) {
+  pdl_enter();
   using namespace bwd8;
   constexpr int CH = KG / 8 + GPW / 8;  // 56 chunks per token
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(bwd8::gx::THREADS, 1)
 bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict__ inv_rms,
                const float* __restrict__ coef, const float* __restrict__ pre, int64_t T,
                int64_t D, int64_t total_steps) {
+  pdl_enter();
   using namespace bwd8;
   using namespace bwd8::gx;
   extern __shared__ uint8_t smem_raw[];
@@ -448,6 +451,7 @@ __host__ __device__ inline int64_t bwd8_cta_of_step(int64_t s, int64_t total, in
 __global__ void __launch_bounds__(bwd8::gp::THREADS, 1)
 bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ part,
                  int64_t ntiles, int64_t total_steps, int maxslot) {
+  pdl_enter();
   using namespace bwd8;
   using namespace bwd8::gp;
   extern __shared__ uint8_t smem_raw[];
@@ -608,6 +612,7 @@ bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ pa
 __global__ void bwd8_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ gphi,
                                         int64_t HC, int64_t ntiles, int64_t total_steps,
                                         int64_t G, int maxslot) {
+  pdl_enter();
   using namespace bwd8;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)HM * HC) return;
@@ -683,9 +688,9 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   const int64_t T = a.T, D = a.D, HC = N * D;
   const Bwd8Geom geo = bwd8_geometry(T, D);
   Bwd8Ws w = bwd8_layout((char*)ws, T, D);
-  bwd8_phi_prep_kernel<<<(unsigned)cdiv(HC * (KG / 8), 256), 256, 0, s>>>(a.phi, w.p, HC);
+  launch(bwd8_phi_prep_kernel, (unsigned)cdiv(HC * (KG / 8), 256), 256, 0, s, a.phi, w.p, HC);
   MHC_LAUNCH_CHECK();
-  bwd8_g_prep_kernel<<<(unsigned)cdiv(T * (KG / 8 + GPW / 8), 256), 256, 0, s>>>(
+  launch(bwd8_g_prep_kernel, (unsigned)cdiv(T * (KG / 8 + GPW / 8), 256), 256, 0, s, 
       gm, a.inv_rms, w.g, w.gp, T);
   MHC_LAUNCH_CHECK();
 
@@ -732,12 +737,12 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   int ngx = sm_count();
   if (total_gx < ngx) ngx = (int)total_gx;
   auto kgx = a.grad_x_acc ? bwd8_gx_kernel<true> : bwd8_gx_kernel<false>;
-  kgx<<<ngx, gx::THREADS, gx::SMEM, s>>>(mx, a.inv_rms, coef, a.pre, T, D, total_gx);
+  launch(kgx, ngx, gx::THREADS, gx::SMEM, s, mx, a.inv_rms, coef, a.pre, T, D, total_gx);
   MHC_LAUNCH_CHECK();
-  bwd8_gphi_kernel<<<geo.grid_gp, gp::THREADS, gp::SMEM, s>>>(mp, w.part, geo.ntiles,
+  launch(bwd8_gphi_kernel, geo.grid_gp, gp::THREADS, gp::SMEM, s, mp, w.part, geo.ntiles,
                                                               geo.total_gp, geo.maxslot);
   MHC_LAUNCH_CHECK();
-  bwd8_gphi_reduce_kernel<<<(unsigned)cdiv((int64_t)HM * HC, 256), 256, 0, s>>>(
+  launch(bwd8_gphi_reduce_kernel, (unsigned)cdiv((int64_t)HM * HC, 256), 256, 0, s, 
       w.part, a.grad_phi, HC, geo.ntiles, geo.total_gp, geo.grid_gp, geo.maxslot);
   MHC_LAUNCH_CHECK();
   return MHC_OK;

@@ -22,6 +22,7 @@ template <typename E, int N>
 __global__ void __launch_bounds__(256)
 pre_mix_kernel(const E* __restrict__ x, const float* __restrict__ phi,
                float* __restrict__ raw, float* __restrict__ sumsq, int64_t T, int64_t HC) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   extern __shared__ float smem[];
   float* xs = smem;                              // [kMixTT][kMixKC + 1]
@@ -75,6 +76,7 @@ pre_small_kernel(const float* __restrict__ raw, const float* __restrict__ sumsq,
                  int64_t HC, float norm_eps, SmallParams sp, float* __restrict__ inv_rms,
                  float* __restrict__ mixes, float* __restrict__ pre, float* __restrict__ post,
                  float* __restrict__ comb, float* __restrict__ logits_out) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   __shared__ float sbase[HM];
   for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
@@ -94,6 +96,7 @@ __global__ void __launch_bounds__(256)
 pre_apply_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
                  const float* __restrict__ pre, E* __restrict__ y, float* __restrict__ x_scaled,
                  int64_t T, int64_t D) {
+  pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -146,6 +149,7 @@ __global__ void __launch_bounds__(256)
 pre_apply_x16_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
                      const float* __restrict__ pre, E* __restrict__ y,
                      float* __restrict__ x_scaled, int64_t T, int64_t D) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t nchunk = D / 16;
@@ -218,10 +222,10 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
     const size_t smem = (size_t)(kMixTT * (kMixKC + 1) + HM * kMixKC) * sizeof(float);
     MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_kernel<E, N>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    pre_mix_kernel<E, N><<<(unsigned)cdiv(T, kMixTT), 256, smem, s>>>(
+    launch(pre_mix_kernel<E, N>, (unsigned)cdiv(T, kMixTT), 256, smem, s, 
         (const E*)a.x, a.phi, raw, sumsq, T, HC);
     MHC_LAUNCH_CHECK();
-    pre_small_kernel<N><<<(unsigned)cdiv(T, 128), 128, 0, s>>>(
+    launch(pre_small_kernel<N>, (unsigned)cdiv(T, 128), 128, 0, s, 
         raw, sumsq, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
         a.post_out, a.comb_frag, a.h_res_logits);
     MHC_LAUNCH_CHECK();
@@ -237,17 +241,17 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
                      (a.x_scaled == nullptr || (reinterpret_cast<uintptr_t>(a.x_scaled) & 31) == 0);
     if constexpr (sizeof(E) == 2) {
       if (v16) {
-        pre_apply_x16_kernel<E, N><<<grid, 256, 0, s>>>((const E*)a.x, a.inv_rms, a.pre, (E*)a.y,
+        launch(pre_apply_x16_kernel<E, N>, grid, 256, 0, s, (const E*)a.x, a.inv_rms, a.pre, (E*)a.y,
                                                         a.x_scaled, T, D);
         MHC_LAUNCH_CHECK();
         return MHC_OK;
       }
     }
     if (vec)
-      pre_apply_kernel<E, N, true><<<grid, 256, 0, s>>>((const E*)a.x, a.inv_rms, a.pre,
+      launch(pre_apply_kernel<E, N, true>, grid, 256, 0, s, (const E*)a.x, a.inv_rms, a.pre,
                                                         (E*)a.y, a.x_scaled, T, D);
     else
-      pre_apply_kernel<E, N, false><<<grid, 256, 0, s>>>((const E*)a.x, a.inv_rms, a.pre,
+      launch(pre_apply_kernel<E, N, false>, grid, 256, 0, s, (const E*)a.x, a.inv_rms, a.pre,
                                                          (E*)a.y, a.x_scaled, T, D);
     MHC_LAUNCH_CHECK();
   }

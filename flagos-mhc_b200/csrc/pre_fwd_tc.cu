@@ -54,6 +54,7 @@ struct MixCfg {
 // of non-negative floats order like the floats).
 __global__ void pre_phi_maxabs_kernel(const float* __restrict__ phi, int64_t n,
                                       unsigned* __restrict__ slot) {
+  pdl_enter();
   float m = 0.f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -69,6 +70,7 @@ template <typename E>
 __global__ void pre_phi_split_kernel(const float* __restrict__ phi, E* __restrict__ hl, int HM,
                                      int NP, int64_t HC, const unsigned* __restrict__ maxslot,
                                      float* __restrict__ descale) {
+  pdl_enter();
   float scale = 1.f;
   if (maxslot != nullptr) {
     scale = f16_operand_scale(*maxslot);
@@ -89,6 +91,42 @@ __global__ void pre_phi_split_kernel(const float* __restrict__ phi, E* __restric
   }
 }
 
+// Vectorised split for HC % 8 == 0: blockIdx.y = source row r < HM (writes hi row r and
+// lo row HM + r, 8 columns per thread and step) or one of the zero rows [2HM, NP).
+template <typename E>
+__global__ void pre_phi_split8_kernel(const float* __restrict__ phi, E* __restrict__ hl, int HM,
+                                      int NP, int64_t HC, const unsigned* __restrict__ maxslot,
+                                      float* __restrict__ descale) {
+  pdl_enter();
+  float scale = 1.f;
+  if (maxslot != nullptr) {
+    scale = f16_operand_scale(*maxslot);
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *descale = 1.f / scale;
+  }
+  const int r = blockIdx.y;
+  const int64_t n8 = HC / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (r < HM) {
+    const float4* src = reinterpret_cast<const float4*>(phi + (int64_t)r * HC);
+    uint4* dhi = reinterpret_cast<uint4*>(hl + (int64_t)r * HC);
+    uint4* dlo = reinterpret_cast<uint4*>(hl + (int64_t)(HM + r) * HC);
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n8; j += stride) {
+      const float4 a = __ldg(src + 2 * j), b = __ldg(src + 2 * j + 1);
+      float p[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                    b.x * scale, b.y * scale, b.z * scale, b.w * scale};
+      float lo[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) lo[k] = p[k] - from_e(to_e<E>(p[k]));
+      dhi[j] = narrow<E>(p);
+      dlo[j] = narrow<E>(lo);
+    }
+  } else {
+    uint4* dz = reinterpret_cast<uint4*>(hl + (int64_t)(HM + r) * HC);  // rows 2HM .. NP-1
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n8; j += stride)
+      dz[j] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 template <int N, int NB, typename E>
 __global__ void __launch_bounds__(MixCfg<N, NB>::THREADS, 1)
 pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
@@ -98,6 +136,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                   float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
                   float* __restrict__ logits_out, int ksplit, float* __restrict__ part,
                   const float* __restrict__ descale) {
+  pdl_enter();
   using C = MixCfg<N, NB>;
   constexpr int HM = C::HM, S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -395,6 +434,7 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
                       SmallParams sp, float* __restrict__ inv_rms, float* __restrict__ mixes,
                       float* __restrict__ pre, float* __restrict__ post, float* __restrict__ comb,
                       float* __restrict__ logits_out, const float* __restrict__ descale) {
+  pdl_enter();
   constexpr int HM = hc_mix(N);
   static_assert((N & (N - 1)) == 0 && N > 1 && N <= 8, "row groups of N lanes");
   __shared__ float sbase[HM];
@@ -501,12 +541,17 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
     if (f16) {
       MHC_CUDA_CHECK(cudaMemsetAsync(maxslot, 0, sizeof(unsigned), s));
       const int64_t m = (int64_t)C::HM * HC;
-      pre_phi_maxabs_kernel<<<(int)std::min<int64_t>(cdiv(m, 256), (int64_t)sm_count() * 4), 256,
-                              0, s>>>(a.phi, m, maxslot);
+      launch(pre_phi_maxabs_kernel, (int)std::min<int64_t>(cdiv(m, 256), (int64_t)sm_count() * 4), 256, 0, s, a.phi, m, maxslot);
       MHC_LAUNCH_CHECK();
     }
-    pre_phi_split_kernel<E><<<grid, 256, 0, s>>>(a.phi, phi_hl, C::HM, C::NP, HC, maxslot,
-                                                 descale);
+    if (HC % 8 == 0 && aligned16(a.phi)) {
+      const int64_t bx = std::min<int64_t>(cdiv(HC / 8, 256), 64);
+      launch(pre_phi_split8_kernel<E>, dim3((unsigned)bx, (unsigned)(C::NP - C::HM)), 256, 0, s,
+             a.phi, phi_hl, C::HM, C::NP, HC, maxslot, descale);
+    } else {
+      launch(pre_phi_split_kernel<E>, grid, 256, 0, s, a.phi, phi_hl, C::HM, C::NP, HC, maxslot,
+             descale);
+    }
     MHC_LAUNCH_CHECK();
   }
   const CUtensorMapDataType dt =
@@ -527,7 +572,7 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
   }
   const int64_t ntiles = cdiv(T, 128);
   const int grid = (int)std::min<int64_t>(ntiles * ks, sm_count());
-  pre_mix_tc_kernel<N, NB, E><<<grid, C::THREADS, C::SMEM, s>>>(
+  launch(pre_mix_tc_kernel<N, NB, E>, grid, C::THREADS, C::SMEM, s, 
       tx, tp, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
       a.comb_frag, a.h_res_logits, ks, part, descale);
   MHC_LAUNCH_CHECK();
@@ -535,7 +580,7 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
     // a warp per token only for many K ranges (few tokens): lanes then share the loads
     const bool warp_tok = ks > 16;
     auto fin = warp_tok ? pre_mix_finish_kernel<N, true> : pre_mix_finish_kernel<N, false>;
-    fin<<<(unsigned)cdiv(T, warp_tok ? 4 : 128 / N), 128, 0, s>>>(
+    launch(fin, (unsigned)cdiv(T, warp_tok ? 4 : 128 / N), 128, 0, s, 
         part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
         a.post_out, a.comb_frag, a.h_res_logits, descale);
     MHC_LAUNCH_CHECK();

@@ -59,8 +59,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: true when the phase with `parity` completed; false on timeout or
 // when another role of the CTA has already given up (*abort != 0).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+                                          volatile int* abort, uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255) == 255 && *abort) return false;
   }

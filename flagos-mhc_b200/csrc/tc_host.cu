@@ -43,4 +43,29 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return r == CUDA_SUCCESS ? MHC_OK : MHC_ERR_CUDA;
 }
 
+// Exercises the bounded mbarrier wait every tensor-core kernel uses, on a phase
+// that nothing ever completes: the wait gives up after `limit` polls, the CTA
+// records MHC_ERR_TIMEOUT in this unit's error word and returns.
+__global__ void wait_selftest_kernel(uint32_t limit) {
+  pdl_enter();
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !tc::mbar_wait(&bar, 0, &abort_flag, limit)) flag_timeout();
+}
+
+int tc_host_device_error() { return read_and_clear_tu_error(); }
+
 }  // namespace mhc
+
+extern "C" int mhc_selftest_wait_timeout(uint32_t spin_limit, void* stream) {
+  if (spin_limit == 0) return MHC_ERR_INVALID_ARGUMENT;
+  mhc::launch(mhc::wait_selftest_kernel, 1, 32, 0, (cudaStream_t)stream, spin_limit);
+  MHC_LAUNCH_CHECK();
+  return MHC_OK;
+}

@@ -62,6 +62,13 @@ uint64_t mhc_kernel_launches(void);
  * counterpart in the reference. */
 int mhc_device_status(void);
 
+/* Self-test of the failure path: launches one CTA that waits on an mbarrier
+ * phase nothing completes, with the bounded wait every tensor-core kernel of
+ * this library uses, cut to `spin_limit` polls.  The wait gives up, the kernel
+ * records MHC_ERR_TIMEOUT and returns; the next mhc_device_status() reports it
+ * and the context stays usable.  Diagnostic; no counterpart in the reference. */
+int mhc_selftest_wait_timeout(uint32_t spin_limit, void* stream);
+
 /*
  * mhc_post forward.  Replaces the device work of `mhc_post`
  * (src/mhc_post.py:296-341, kernels :24-96 and :207-271):

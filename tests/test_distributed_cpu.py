@@ -90,3 +90,48 @@ def test_packed_buffer_detects_views():
     pb = packed_buffer(*v)
     assert pb is not None and pb.data_ptr() == buf.data_ptr() and pb.numel() == 17
     assert packed_buffer(torch.zeros(2, 5), torch.zeros(3), torch.zeros(4)) is None
+
+
+def _failing_worker(rank, world, port, mode, result_q):
+    """Rank 1 fails before the gradient sum (raises, or stalls past the process-group
+    timeout); rank 0 must get an error from its collective, not hang."""
+    import datetime
+    import sys
+    import time
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "flagos-mhc_b200")]
+    from FlagOS_mhc.distributed import allreduce_pre_grads
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    buf = torch.ones(24 * 16 + 27)
+    views = (buf[:24 * 16].view(24, 16), buf[24 * 16:24 * 16 + 3], buf[24 * 16 + 3:])
+    if rank == 1:
+        if mode == "raise":
+            os._exit(3)          # the rank dies between steps, with nothing in flight
+        time.sleep(8)            # "never joins": stalls past the group timeout
+        os._exit(0)
+    t0 = time.time()
+    try:
+        allreduce_pre_grads(*views)
+        result_q.put(("no error", time.time() - t0))
+    except Exception as e:  # noqa: BLE001 -- any error from the collective is the point
+        result_q.put((type(e).__name__, time.time() - t0))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["raise", "stall"])
+def test_failed_rank_gives_error_not_hang(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    what, dt = q.get(timeout=60)
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert what != "no error"
+    assert dt < 30
