@@ -389,6 +389,39 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
                          "frac_of_peak": nbytes / (ms / 1e3) / 1e9 / peak}
     del x, phi
     torch.cuda.empty_cache()
+    # ---- layer boundary at C3 shapes: post forward of layer l, then the pre forward of
+    # layer l+1 on its output; unfused (two passes over x_{l+1}) against the fused pair
+    # (post forward writing the next layer's mix partials, pre forward from them)
+    T, N, D = 32768, 4, 7168
+    g = torch.Generator(device=dev).manual_seed(3)
+    xl = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+    ho = torch.randn(T, D, generator=g, device=dev).to(bf)
+    hr = torch.softmax(torch.randn(T, N, N, generator=g, device=dev), -1)
+    hp = 2 * torch.sigmoid(torch.randn(T, N, generator=g, device=dev))
+    phi = torch.randn(24, N * D, generator=g, device=dev) / (N * D) ** 0.5
+    alpha = torch.rand(3, generator=g, device=dev) + 0.5
+    base = torch.randn(24, generator=g, device=dev) * 0.1
+
+    def boundary(ev, fused):
+        ev[0].record() if ev is not None else None
+        if fused:
+            x1, pm = M.mhc_post(xl, hr, ho, hp, next_phi=phi)
+        else:
+            x1, pm = M.mhc_post(xl, hr, ho, hp), None
+        ev[1].record() if ev is not None else None
+        M.mhc_pre_clamp_sinkhorn(x1, phi, alpha, base, need_backward=True, premix=pm, **KW)
+        ev[2].record() if ev is not None else None
+    tu = _timed(lambda ev: boundary(ev, False), steps, warmup, 3)
+    tf = _timed(lambda ev: boundary(ev, True), steps, warmup, 3)
+    res["C3_layer_boundary_fwd"] = {
+        "shape": [T, N, D],
+        "unfused_ms": {"post_fwd": tu[0], "pre_fwd": tu[1], "total": tu[0] + tu[1]},
+        "fused_ms": {"post_fwd_with_next_mix": tf[0], "pre_fwd_from_premix": tf[1],
+                     "total": tf[0] + tf[1]},
+        "saves_ms": (tu[0] + tu[1]) - (tf[0] + tf[1]),
+        "note": "x_{l+1} is read once instead of twice across the layer boundary"}
+    del xl, ho, hr, hp, phi
+    torch.cuda.empty_cache()
     # ---- C4: T=65536, N=8, D=4096 layer step
     T, N, D = 65536, 8, 4096
     HM = N * (N + 2)

@@ -51,6 +51,24 @@ _SIGS = {
     "mhc_pre_bwd": (ctypes.c_int, [_vp, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _fp, _fp, _i64, _i32,
                                    _i64, _i32, _f32, _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp,
                                    _vp, _sz, _vp]),
+    "mhc_post_fwd_strided": (ctypes.c_int, [_vp, _i64, _fp, _vp, _i64, _fp, _vp, _i64, _i32, _i64,
+                                            _i32, _vp]),
+    "mhc_post_bwd_strided": (ctypes.c_int, [_vp, _i64, _vp, _i64, _fp, _vp, _i64, _fp, _vp, _fp,
+                                            _vp, _fp, _i64, _i32, _i64, _i32, _vp]),
+    "mhc_pre_fwd_strided": (ctypes.c_int, [_vp, _i64, _fp, _fp, _fp, _i64, _i32, _i64, _i32, _f32,
+                                           _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp, _fp, _fp,
+                                           _fp, _fp, _vp, _sz, _vp]),
+    "mhc_pre_bwd_strided": (ctypes.c_int, [_vp, _i64, _fp, _fp, _fp, _fp, _fp, _fp, _vp, _i64, _fp,
+                                           _fp, _i64, _i32, _i64, _i32, _f32, _f32, _f32, _f32,
+                                           _i32, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
+    "mhc_post_fwd_mix_supported": (ctypes.c_int, [_i64, _i32, _i64, _i32]),
+    "mhc_post_fwd_mix_layers": (_i32, [_i64, _i32, _i64, _i32]),
+    "mhc_post_fwd_mix_workspace_bytes": (_sz, [_i64, _i32, _i64, _i32]),
+    "mhc_post_fwd_mix": (ctypes.c_int, [_vp, _fp, _vp, _fp, _vp, _i64, _i32, _i64, _i32, _fp, _fp,
+                                        _vp, _sz, _vp]),
+    "mhc_pre_fwd_premixed": (ctypes.c_int, [_vp, _fp, _i32, _fp, _fp, _i64, _i32, _i64, _i32,
+                                            _f32, _f32, _f32, _f32, _i32, _vp, _fp, _fp, _fp,
+                                            _fp, _fp, _fp, _fp, _vp]),
     "mhc_peer_region_bytes": (_sz, [_i64]),
     "mhc_peer_region_alloc": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_void_p)]),
     "mhc_peer_region_free": (ctypes.c_int, [_vp]),
@@ -87,6 +105,33 @@ def lib():
                     fn.argtypes = args
                 _lib = h
     return _lib
+
+
+def token_view(t, inner_dims, inner_numel):
+    """Token stride (in elements) of t viewed as (tokens, *inner) without a copy, or None.
+
+    t is (T, *inner) or (B, S, *inner) with the `inner_dims` trailing dims packed
+    (their numel is `inner_numel`); for 4D/3D-with-B,S the B stride must equal S times
+    the S stride so that the B*S tokens share one stride."""
+    lead = t.dim() - inner_dims
+    if lead not in (1, 2) or t.numel() == 0:
+        return None
+    inner = t.shape[lead:]
+    expect = 1
+    for d in range(t.dim() - 1, lead - 1, -1):
+        if inner[d - lead] != 1 and t.stride(d) != expect:
+            return None
+        expect *= t.shape[d]
+    if lead == 1:
+        ts = t.stride(0)
+    else:
+        B, S = t.shape[0], t.shape[1]
+        ts = t.stride(1) if S > 1 else t.stride(0)
+        if B > 1 and S > 1 and t.stride(0) != S * t.stride(1):
+            return None
+    if t.shape[0] * (t.shape[1] if lead == 2 else 1) > 1 and ts < inner_numel:
+        return None
+    return max(int(ts), inner_numel)
 
 
 def ptr(t):

@@ -14,23 +14,41 @@ from .mhc_pre_clamp_sinkhorn_backward import mhc_pre_clamp_sinkhorn_backward
 
 
 class MhcPostFn(torch.autograd.Function):
-    """src/autograd.py:14-27."""
+    """src/autograd.py:14-27.  With ``next_phi`` (optional) the forward also computes the
+    next layer's mix partials and appends them to ``premix_sink`` (they carry no
+    gradient)."""
 
     @staticmethod
-    def forward(ctx, x, h_res, h_out, h_post):
-        y = mhc_post(x, h_res, h_out, h_post)
+    def forward(ctx, x, h_res, h_out, h_post, next_phi=None, premix_sink=None):
+        if next_phi is not None:
+            y, pm = mhc_post(x, h_res, h_out, h_post, next_phi=next_phi.detach())
+            if premix_sink is not None:
+                premix_sink.append(pm)
+        else:
+            y = mhc_post(x, h_res, h_out, h_post)
         ctx.save_for_backward(x, h_res, h_out, h_post)
         return y
 
     @staticmethod
     def backward(ctx, grad_y):
         x, h_res, h_out, h_post = ctx.saved_tensors
-        return mhc_post_backward(grad_y.contiguous(), x, h_res, h_out, h_post)
+        return mhc_post_backward(grad_y.contiguous(), x, h_res, h_out, h_post) + (None, None)
 
 
-def mhc_post_fn(x, h_res, h_out, h_post):
-    """Autograd-aware mhc_post."""
-    return MhcPostFn.apply(x, h_res, h_out, h_post)
+def mhc_post_fn(x, h_res, h_out, h_post, next_phi=None):
+    """Autograd-aware mhc_post.
+
+    ``next_phi`` (optional, not in the reference API): the next layer's phi; the call
+    then returns ``(out, premix)`` for ``mhc_pre_clamp_sinkhorn_fn(out, next_phi, ...,
+    premix=premix)`` (see :func:`FlagOS_mhc.mhc_post`).  premix carries no gradient."""
+    if next_phi is None:
+        return MhcPostFn.apply(x, h_res, h_out, h_post)
+    sink = []
+    y = MhcPostFn.apply(x, h_res, h_out, h_post, next_phi, sink)
+    pm = sink[0] if sink else None
+    if pm is not None:  # key it to the tensor autograd hands back
+        pm._key = (y.data_ptr(), y._version, tuple(y.shape)) + pm._key[3:]
+    return y, pm
 
 
 class MhcPreClampSinkhornFn(torch.autograd.Function):
@@ -39,11 +57,11 @@ class MhcPreClampSinkhornFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, phi, alpha, base, norm_eps, hc_eps, clamp_min, clamp_max, iter_times,
-                materialize_x_scaled=True):
+                materialize_x_scaled=True, premix=None):
         out = mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=norm_eps, hc_eps=hc_eps,
                                      clamp_min=clamp_min, clamp_max=clamp_max,
                                      iter_times=iter_times, need_backward=True,
-                                     materialize_x_scaled=materialize_x_scaled)
+                                     materialize_x_scaled=materialize_x_scaled, premix=premix)
         ctx.save_for_backward(x, phi, alpha, base, out["inv_rms"], out["x_scaled"],
                               out["mixes"], out["h_res_logits"], out["pre"])
         ctx.norm_eps = norm_eps
@@ -69,14 +87,17 @@ class MhcPreClampSinkhornFn(torch.autograd.Function):
             norm_eps=ctx.norm_eps, hc_eps=ctx.hc_eps, clamp_min=ctx.clamp_min,
             clamp_max=ctx.clamp_max, iter_times=ctx.iter_times)
         return (gx, gphi.to(phi.dtype), galpha.to(alpha.dtype), gbase.to(base.dtype),
-                None, None, None, None, None, None)
+                None, None, None, None, None, None, None)
 
 
 def mhc_pre_clamp_sinkhorn_fn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clamp_min=0.0,
-                              clamp_max=0.0, iter_times=20, materialize_x_scaled=True):
+                              clamp_max=0.0, iter_times=20, materialize_x_scaled=True,
+                              premix=None):
     """Autograd-aware mhc_pre_clamp_sinkhorn. Returns (y, post_out, comb_frag).
 
     ``materialize_x_scaled=False`` (opt-in, not in the reference API) saves an empty
-    x_scaled instead of the fp32 copy of x; the backward does not need it."""
+    x_scaled instead of the fp32 copy of x; the backward does not need it.
+    ``premix`` (optional, not in the reference API): the mix partials that
+    ``mhc_post_fn(..., next_phi=phi)`` returned with x."""
     return MhcPreClampSinkhornFn.apply(x, phi, alpha, base, norm_eps, hc_eps, clamp_min,
-                                       clamp_max, iter_times, materialize_x_scaled)
+                                       clamp_max, iter_times, materialize_x_scaled, premix)

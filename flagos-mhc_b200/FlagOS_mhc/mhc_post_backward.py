@@ -34,6 +34,30 @@ def mhc_post_backward(grad_y, x, h_res, h_out, h_post):
     the shapes and dtypes of h_res / h_out / h_post (``torch.empty_like`` in
     the reference, :599-602).
     """
+    if grad_y.dim() in (3, 4) and grad_y.is_cuda and x.is_cuda and h_out.is_cuda:
+        N, D = grad_y.shape[-2], grad_y.shape[-1]
+        gs = _C.token_view(grad_y, 2, N * D)
+        xs = _C.token_view(x, 2, N * D)
+        hs = _C.token_view(h_out, 1, D)
+        if (gs is not None and xs is not None and hs is not None and 1 <= N <= 8
+                and grad_y.dtype == x.dtype == h_out.dtype and x.shape == grad_y.shape):
+            T = grad_y.numel() // (N * D)
+            hr32 = h_res.reshape(T, N, N).float().contiguous()
+            hp32 = h_post.reshape(T, N).float().contiguous()
+            _C.require_cuda(hr32, hp32)
+            lead = grad_y.shape[:-2]
+            grad_x = torch.empty(grad_y.shape, dtype=x.dtype, device=x.device)
+            grad_hout = torch.empty(lead + (D,), dtype=h_out.dtype, device=x.device)
+            grad_hres = torch.empty(T, N, N, dtype=torch.float32, device=x.device)
+            grad_hpost = torch.empty(T, N, dtype=torch.float32, device=x.device)
+            with torch.cuda.device(x.device):
+                st = _C.lib().mhc_post_bwd_strided(
+                    _C.ptr(grad_y), gs, _C.ptr(x), xs, _C.ptr(hr32), _C.ptr(h_out), hs,
+                    _C.ptr(hp32), _C.ptr(grad_x), _C.ptr(grad_hres), _C.ptr(grad_hout),
+                    _C.ptr(grad_hpost), T, N, D, _C.dtype_code(x.dtype), _C.stream_of(x))
+            _C.check(st, "mhc_post_backward")
+            return (grad_x, grad_hres.to(h_res.dtype).reshape(h_res.shape), grad_hout,
+                    grad_hpost.to(h_post.dtype).reshape(h_post.shape))
     gy, xf, hr, ho, hp, shape4, shape_out, T, N, D = _flatten(grad_y, x, h_res, h_out, h_post)
     _C.require_cuda(gy, xf, hr, ho, hp)
     if not 1 <= N <= 8:

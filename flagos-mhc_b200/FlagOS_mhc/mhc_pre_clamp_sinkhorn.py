@@ -35,7 +35,7 @@ def _check_params(N, D, phi, alpha, base):
 
 def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clamp_min=0.0,
                            clamp_max=0.0, iter_times=20, need_backward=False,
-                           materialize_x_scaled=True):
+                           materialize_x_scaled=True, premix=None):
     """Fused RMSNorm + x.phi^T + heads + clamp + softmax + Sinkhorn + y.
 
     Reference: ``mhc_pre_clamp_sinkhorn`` (src/mhc_pre_clamp_sinkhorn.py:857-971).
@@ -49,9 +49,24 @@ def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clam
     ``materialize_x_scaled=False`` (an addition to the reference API, opt-in) skips
     writing the fp32 ``x_scaled`` (4*N*D bytes per token, the largest output) and
     returns an empty tensor in its place; the backward of this package never reads it.
+
+    ``premix`` (an addition to the reference API, optional): the :class:`PreMix` that
+    ``mhc_post(..., next_phi=phi)`` returned along with this ``x``; the mix is then not
+    recomputed from x.  Ignored unless it was made from this very x and phi.
     """
-    xf, y_shape = _flatten(x)
-    T, N, D = xf.shape
+    if x.dim() not in (3, 4):
+        raise ValueError(f"unsupported x.dim()={x.dim()}")
+    # a token-strided x (slice of a larger buffer, regular (B,S) view) is read in place
+    xts = _C.token_view(x, 2, x.shape[-2] * x.shape[-1]) if x.is_cuda else None
+    if xts is not None:
+        N, D = x.shape[-2], x.shape[-1]
+        T = x.numel() // (N * D)
+        xf = x
+        y_shape = tuple(x.shape[:-2]) + (D,)
+    else:
+        xf, y_shape = _flatten(x)
+        T, N, D = xf.shape
+        xts = N * D
     hc_mix, hc_d = _check_params(N, D, phi, alpha, base)
     _C.require_cuda(xf, phi, alpha, base)
     dev = xf.device
@@ -69,15 +84,25 @@ def mhc_pre_clamp_sinkhorn(x, phi, alpha, base, norm_eps=1e-6, hc_eps=1e-6, clam
     h_res_logits = torch.empty(T, N, N, **f32) if need_backward else None
     L = _C.lib()
     code = _C.dtype_code(xf.dtype)
+    use_premix = (premix is not None and premix.matches(x, phi) and xts == N * D
+                  and premix.part.shape[1] == T)
     with torch.cuda.device(dev):
-        ws_bytes = L.mhc_pre_fwd_workspace_bytes(T, N, D, code)
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-        st = L.mhc_pre_fwd(_C.ptr(xf), _C.ptr(phi_f), _C.ptr(alpha_f), _C.ptr(base_f), T, N, D,
-                           code, float(norm_eps), float(hc_eps), float(clamp_min),
-                           float(clamp_max), int(iter_times), _C.ptr(y), _C.ptr(post_out),
-                           _C.ptr(comb_frag), _C.ptr(inv_rms), _C.ptr(x_scaled), _C.ptr(mixes),
-                           _C.ptr(h_res_logits), _C.ptr(pre), _C.ptr(ws), ws_bytes,
-                           _C.stream_of(xf))
+        if use_premix:
+            st = L.mhc_pre_fwd_premixed(
+                _C.ptr(xf), _C.ptr(premix.part), premix.layers, _C.ptr(alpha_f), _C.ptr(base_f),
+                T, N, D, code, float(norm_eps), float(hc_eps), float(clamp_min),
+                float(clamp_max), int(iter_times), _C.ptr(y), _C.ptr(post_out),
+                _C.ptr(comb_frag), _C.ptr(inv_rms), _C.ptr(x_scaled), _C.ptr(mixes),
+                _C.ptr(h_res_logits), _C.ptr(pre), _C.stream_of(xf))
+        else:
+            ws_bytes = L.mhc_pre_fwd_workspace_bytes(T, N, D, code)
+            ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+            st = L.mhc_pre_fwd_strided(
+                _C.ptr(xf), xts, _C.ptr(phi_f), _C.ptr(alpha_f), _C.ptr(base_f), T, N, D, code,
+                float(norm_eps), float(hc_eps), float(clamp_min), float(clamp_max),
+                int(iter_times), _C.ptr(y), _C.ptr(post_out), _C.ptr(comb_frag),
+                _C.ptr(inv_rms), _C.ptr(x_scaled), _C.ptr(mixes), _C.ptr(h_res_logits),
+                _C.ptr(pre), _C.ptr(ws), ws_bytes, _C.stream_of(xf))
     _C.check(st, "mhc_pre_clamp_sinkhorn")
     result = {"y": y.reshape(y_shape), "post_out": post_out, "comb_frag": comb_frag}
     if need_backward:

@@ -46,13 +46,22 @@ def mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, inv_rms, x_scaled, mixe
     else:
         raise ValueError(f"unsupported grad_y.dim()={grad_y.dim()}")
     hc_mix, hc_d = _check_params(N, D, phi, alpha, base)
-    xf = x.reshape(T, N, D).contiguous()
-    gy = grad_y.reshape(T, D).contiguous()
+    # token-strided x / grad_y (slices of larger buffers, regular (B,S) views) are read in
+    # place, as the reference's kernels read them through x.stride(1) / grad_y.stride(1)
+    xts = _C.token_view(x, 2, N * D) if x.is_cuda else None
+    gts = _C.token_view(grad_y, 1, D) if grad_y.is_cuda else None
+    if xts is not None and gts is not None and grad_y.dtype == x.dtype:
+        xf, gy = x, grad_y
+    else:
+        xf = x.reshape(T, N, D).contiguous()
+        gy = grad_y.reshape(T, D).contiguous()
+        xts, gts = N * D, D
     _C.require_cuda(xf, gy, phi, alpha, base, inv_rms, mixes, pre, grad_post_out, grad_comb_frag)
     dev = xf.device
     gx_dtype = x.dtype
     if gy.dtype != xf.dtype:
-        xf, gy = xf.float(), gy.float()
+        xf, gy = xf.reshape(T, N, D).float(), gy.reshape(T, D).float()
+        xts, gts = N * D, D
     f = lambda t: t.to(torch.float32).contiguous()  # noqa: E731
     phi_f, alpha_f, base_f = f(phi), f(alpha), f(base)
     inv_f, mixes_f, pre_f = f(inv_rms.reshape(T)), f(mixes.reshape(T, hc_mix)), f(pre.reshape(T, N))
@@ -73,16 +82,12 @@ def mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, inv_rms, x_scaled, mixe
     with torch.cuda.device(dev):
         ws_bytes = L.mhc_pre_bwd_workspace_bytes(T, N, D, code, int(iter_times))
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-        head = (_C.ptr(xf), _C.ptr(phi_f), _C.ptr(alpha_f), _C.ptr(base_f), _C.ptr(inv_f),
-                _C.ptr(mixes_f), _C.ptr(pre_f), _C.ptr(gy), _C.ptr(gpost_f), _C.ptr(gcomb_f),
-                T, N, D, code, float(norm_eps), float(hc_eps), float(clamp_min),
-                float(clamp_max), int(iter_times))
-        tail = (_C.ptr(grad_x), _C.ptr(grad_phi), _C.ptr(grad_alpha), _C.ptr(grad_base),
-                _C.ptr(ws), ws_bytes, _C.stream_of(xf))
-        if acc is None:
-            st = L.mhc_pre_bwd(*head, *tail)
-        else:
-            st = L.mhc_pre_bwd_accumulate(*head, _C.ptr(acc), *tail)
+        st = L.mhc_pre_bwd_strided(
+            _C.ptr(xf), xts, _C.ptr(phi_f), _C.ptr(alpha_f), _C.ptr(base_f), _C.ptr(inv_f),
+            _C.ptr(mixes_f), _C.ptr(pre_f), _C.ptr(gy), gts, _C.ptr(gpost_f), _C.ptr(gcomb_f),
+            T, N, D, code, float(norm_eps), float(hc_eps), float(clamp_min), float(clamp_max),
+            int(iter_times), _C.ptr(acc), _C.ptr(grad_x), _C.ptr(grad_phi), _C.ptr(grad_alpha),
+            _C.ptr(grad_base), _C.ptr(ws), ws_bytes, _C.stream_of(xf))
     _C.check(st, "mhc_pre_clamp_sinkhorn_backward")
     return (grad_x.to(gx_dtype).view(x.shape), grad_phi.view(phi.shape), grad_alpha, grad_base)
 

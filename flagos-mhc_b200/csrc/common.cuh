@@ -14,6 +14,13 @@
 namespace mhc {
 
 constexpr int kMaxN = 8;                       // hcMult supported: 1..8
+
+// Elements between consecutive tokens of the token-major inputs (x: N*D when packed;
+// grad_y of the post backward: N*D; h_out and grad_y of the pre backward: D).  Within a
+// token the (N, D) block is contiguous.  Outputs are always packed.
+struct TokStride {
+  int64_t x, gy, ho;
+};
 __host__ __device__ constexpr int hc_mix(int n) { return n * (n + 2); }
 
 // ---------------------------------------------------------------------------

@@ -35,7 +35,7 @@ namespace mhc {
 
 void note_launch();
 constexpr int kMaxRanks = 8;
-constexpr int kMaxCtas = 128;
+constexpr int kMaxCtas = 256;
 constexpr int kPeerThreads = 256;
 
 struct PeerArgs {
@@ -125,26 +125,6 @@ __device__ __forceinline__ float4 ld4(const float* p, int64_t u, int64_t n) {
   for (int k = 0; k < 4; ++k) v[k] = (4 * u + k < n) ? __ldcg(p + 4 * u + k) : 0.f;
   return make_float4(v[0], v[1], v[2], v[3]);
 }
-// Loads of another rank's stage: system-scope relaxed loads (never served from a stale
-// cached copy of a previous call's values).
-__device__ __forceinline__ float4 ld4_sys(const float* p, int64_t u, int64_t n) {
-  if (4 * u + 3 < n) {
-    float4 v;
-    asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(reinterpret_cast<const float4*>(p) + u)
-                 : "memory");
-    return v;
-  }
-  float v[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    v[k] = 0.f;
-    if (4 * u + k < n)
-      asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v[k]) : "l"(p + 4 * u + k) : "memory");
-  }
-  return make_float4(v[0], v[1], v[2], v[3]);
-}
 __device__ __forceinline__ void st4(float* p, int64_t u, int64_t n, float4 v) {
   if (4 * u + 3 < n) {
     __stcg(reinterpret_cast<float4*>(p) + u, v);
@@ -171,22 +151,34 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
   }
   cta_signal<W>(a, 0, c);
   // 2. sum part c of this rank's slice over the ranks, in rank order; scatter it.
-  // All W loads of a unit are issued before the first add (NVLink latency overlaps).
+  // U units per thread and pass, all W*U loads issued before the first add, so many
+  // NVLink requests are in flight per thread.
   if (!cta_wait_flags(a, 0, deadline)) return;
   {
+    constexpr int U = W <= 4 ? 4 : 2;
     int64_t u0, u1;
     part_range(a, a.rank, c, &u0, &u1);
-    for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
-      float4 v[W];
+    for (int64_t ub = u0 + threadIdx.x; ub < u1; ub += U * blockDim.x) {
+      float4 v[U][W];
 #pragma unroll
-      for (int p = 0; p < W; ++p) v[p] = ld4_sys(a.region[p], u, a.n);
-      float4 acc = v[0];
+      for (int q = 0; q < U; ++q) {
+        const int64_t u = ub + (int64_t)q * blockDim.x;
 #pragma unroll
-      for (int p = 1; p < W; ++p) {
-        acc.x += v[p].x; acc.y += v[p].y; acc.z += v[p].z; acc.w += v[p].w;
+        for (int p = 0; p < W; ++p)
+          v[q][p] = u < u1 ? ld4(a.region[p], u, a.n) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int p = 0; p < W; ++p) st4(a.region[p] + a.cap, u, a.n, acc);
+      for (int q = 0; q < U; ++q) {
+        const int64_t u = ub + (int64_t)q * blockDim.x;
+        if (u >= u1) break;
+        float4 acc = v[q][0];
+#pragma unroll
+        for (int p = 1; p < W; ++p) {
+          acc.x += v[q][p].x; acc.y += v[q][p].y; acc.z += v[q][p].z; acc.w += v[q][p].w;
+        }
+#pragma unroll
+        for (int p = 0; p < W; ++p) st4(a.region[p] + a.cap, u, a.n, acc);
+      }
     }
   }
   cta_signal<W>(a, 1, c);

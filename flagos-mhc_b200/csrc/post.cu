@@ -17,7 +17,7 @@ template <typename E, int N, bool VEC>
 __global__ void __launch_bounds__(256)
 post_fwd_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                 const E* __restrict__ h_out, const float* __restrict__ h_post,
-                E* __restrict__ out, int64_t T, int64_t D) {
+                E* __restrict__ out, int64_t T, int64_t D, TokStride st) {
   pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
@@ -30,8 +30,8 @@ post_fwd_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
     for (int e = 0; e < N * N; ++e) hr[e] = __ldg(h_res + t * N * N + e);
 #pragma unroll
     for (int i = 0; i < N; ++i) hp[i] = __ldg(h_post + t * N + i);
-    const E* xt = x + t * N * D;
-    const E* ht = h_out + t * D;
+    const E* xt = x + t * st.x;
+    const E* ht = h_out + t * st.ho;
     E* ot = out + t * N * D;
 #pragma unroll 2
     for (int64_t c = lane; c < nchunk; c += 32) {
@@ -63,7 +63,7 @@ post_bwd_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                 const float* __restrict__ h_res, const E* __restrict__ h_out,
                 const float* __restrict__ h_post, E* __restrict__ gx,
                 float* __restrict__ ghres, E* __restrict__ ghout,
-                float* __restrict__ ghpost, int64_t T, int64_t D) {
+                float* __restrict__ ghpost, int64_t T, int64_t D, TokStride st) {
   pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
@@ -81,9 +81,9 @@ post_bwd_kernel(const E* __restrict__ gy, const E* __restrict__ x,
     for (int e = 0; e < N * N; ++e) acc_r[e] = 0.f;
 #pragma unroll
     for (int i = 0; i < N; ++i) acc_p[i] = 0.f;
-    const E* gyt = gy + t * N * D;
-    const E* xt = x + t * N * D;
-    const E* ht = h_out + t * D;
+    const E* gyt = gy + t * st.gy;
+    const E* xt = x + t * st.x;
+    const E* ht = h_out + t * st.ho;
     E* gxt = gx + t * N * D;
     E* ghot = ghout + t * D;
 #pragma unroll 2
@@ -170,7 +170,7 @@ template <typename E, int N, bool SPLIT>
 __global__ void __launch_bounds__(256, 2)
 post_fwd_x16_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                     const E* __restrict__ h_out, const float* __restrict__ h_post,
-                    E* __restrict__ out, int64_t T, int64_t D) {
+                    E* __restrict__ out, int64_t T, int64_t D, TokStride st) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
@@ -186,8 +186,8 @@ post_fwd_x16_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
     for (int e = 0; e < N * N; ++e) hr[e] = __ldg(h_res + t * N * N + e);
 #pragma unroll
     for (int i = 0; i < N; ++i) hp[i] = __ldg(h_post + t * N + i);
-    const E* xt = x + t * N * D;
-    const E* ht = h_out + t * D;
+    const E* xt = x + t * st.x;
+    const E* ht = h_out + t * st.ho;
     E* ot = out + t * N * D;
     for (int64_t c = clo + lane; c < chi; c += 32) {
       U8 xv[N];
@@ -316,7 +316,7 @@ template <typename E, int V>
 __global__ void __launch_bounds__(256)
 post_fwd_n8_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
                    const E* __restrict__ h_out, const float* __restrict__ h_post,
-                   E* __restrict__ out, int64_t T, int64_t D) {
+                   E* __restrict__ out, int64_t T, int64_t D, TokStride st) {
   pdl_enter();
   constexpr int N = 8, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -329,8 +329,8 @@ post_fwd_n8_kernel(const E* __restrict__ x, const float* __restrict__ h_res,
     split_e2<E>(__ldg(hr + (2 * c) * N + g), __ldg(hr + (2 * c + 1) * N + g), a[0], a[2]);
     a[1] = a[3] = 0u;
     const float hp = __ldg(h_post + t * N + g);
-    const E* xr = x + (t * N + g) * D;
-    const E* ht = h_out + t * D;
+    const E* xr = x + t * st.x + g * D;
+    const E* ht = h_out + t * st.ho;
     E* orow = out + (t * N + g) * D;
 #pragma unroll 2
     for (int64_t d0 = 8 * V * c; d0 < D; d0 += 32 * V) {
@@ -359,7 +359,7 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                    const float* __restrict__ h_res, const E* __restrict__ h_out,
                    const float* __restrict__ h_post, E* __restrict__ gx,
                    float* __restrict__ ghres, E* __restrict__ ghout,
-                   float* __restrict__ ghpost, int64_t T, int64_t D) {
+                   float* __restrict__ ghpost, int64_t T, int64_t D, TokStride st) {
   pdl_enter();
   constexpr int N = 8, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -376,9 +376,9 @@ post_bwd_n8_kernel(const E* __restrict__ gy, const E* __restrict__ x,
       a[1] = a[3] = 0u;
     }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const E* xr = x + (t * N + g) * D;
-    const E* gyr = gy + (t * N + g) * D;
-    const E* ht = h_out + t * D;
+    const E* xr = x + t * st.x + g * D;
+    const E* gyr = gy + t * st.gy + g * D;
+    const E* ht = h_out + t * st.ho;
     E* gxr = gx + (t * N + g) * D;
     E* ght = ghout + t * D;
 #pragma unroll 2
@@ -434,7 +434,7 @@ post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
                      const float* __restrict__ h_res, const E* __restrict__ h_out,
                      const float* __restrict__ h_post, E* __restrict__ gx,
                      float* __restrict__ ghres, E* __restrict__ ghout,
-                     float* __restrict__ ghpost, int64_t T, int64_t D) {
+                     float* __restrict__ ghpost, int64_t T, int64_t D, TokStride st) {
   pdl_enter();
   constexpr int N = 4, R = 4 * V;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -461,9 +461,9 @@ post_bwd_n4x2_kernel(const E* __restrict__ gy, const E* __restrict__ x,
     }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const int64_t row = live ? (t * N + j) * D : 0;
-    const E* xr = x + row;
-    const E* gyr = gy + row;
-    const E* ht = h_out + (live ? t * D : 0);
+    const E* xr = x + (live ? t * st.x + j * D : 0);
+    const E* gyr = gy + (live ? t * st.gy + j * D : 0);
+    const E* ht = h_out + (live ? t * st.ho : 0);
     E* gxr = gx + row;
     E* ght = ghout + (live ? t * D : 0);
 #pragma unroll 2
@@ -535,47 +535,51 @@ static int post_grid(int64_t T) {
 template <typename E, int N>
 static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
                            const float* h_post, void* out, int64_t T, int64_t D,
-                           cudaStream_t s) {
-  const bool vec = (D % Pack<E>::n == 0) && aligned16(x) && aligned16(h_out) && aligned16(out);
+                           TokStride st, cudaStream_t s) {
+  // a strided input counts as aligned to A bytes when every token's row start is
+  const auto al = [](const void* p, int64_t ts, uintptr_t A) {
+    return (reinterpret_cast<uintptr_t>(p) % A) == 0 && ((uint64_t)ts * sizeof(E)) % A == 0;
+  };
+  const bool vec = (D % Pack<E>::n == 0) && al(x, st.x, 16) && al(h_out, st.ho, 16) && aligned16(out);
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 8) {
-    if (D % 128 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
+    if (D % 128 == 0 && al(x, st.x, 32) && al(h_out, st.ho, 32) && aligned32(out)) {
       launch(post_fwd_n8_kernel<E, 4>, grid, block, 0, s, (const E*)x, h_res, (const E*)h_out,
-                                                      h_post, (E*)out, T, D);
+                                                      h_post, (E*)out, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
-    if (D % 64 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
+    if (D % 64 == 0 && al(x, st.x, 32) && al(h_out, st.ho, 32) && aligned32(out)) {
       launch(post_fwd_n8_kernel<E, 2>, grid, block, 0, s, (const E*)x, h_res, (const E*)h_out,
-                                                      h_post, (E*)out, T, D);
+                                                      h_post, (E*)out, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
     if (D % 32 == 0 && vec) {
       launch(post_fwd_n8_kernel<E, 1>, grid, block, 0, s, (const E*)x, h_res, (const E*)h_out,
-                                                      h_post, (E*)out, T, D);
+                                                      h_post, (E*)out, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
   }
   if constexpr (sizeof(E) == 2 && N <= 4) {
-    if (D % 16 == 0 && aligned32(x) && aligned32(h_out) && aligned32(out)) {
+    if (D % 16 == 0 && al(x, st.x, 32) && al(h_out, st.ho, 32) && aligned32(out)) {
       if (T < (int64_t)sm_count() * 8)  // small T (fewer than 8 tokens per SM): a block per token
         launch(post_fwd_x16_kernel<E, N, true>, (unsigned)T, block, 0, s, 
-            (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
+            (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D, st);
       else
         launch(post_fwd_x16_kernel<E, N, false>, grid, block, 0, s, 
-            (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
+            (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
   }
   if (vec)
     launch(post_fwd_kernel<E, N, true>, grid, block, 0, s, 
-        (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
+        (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D, st);
   else
     launch(post_fwd_kernel<E, N, false>, grid, block, 0, s, 
-        (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D);
+        (const E*)x, h_res, (const E*)h_out, h_post, (E*)out, T, D, st);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
 }
@@ -583,12 +587,16 @@ static int post_fwd_launch(const void* x, const float* h_res, const void* h_out,
 template <typename E, int N>
 static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
                            const void* h_out, const float* h_post, void* gx, float* ghres,
-                           void* ghout, float* ghpost, int64_t T, int64_t D, cudaStream_t s) {
-  const bool vec = (D % Pack<E>::n == 0) && aligned16(gy) && aligned16(x) &&
-                   aligned16(h_out) && aligned16(gx) && aligned16(ghout);
+                           void* ghout, float* ghpost, int64_t T, int64_t D, TokStride st,
+                           cudaStream_t s) {
+  const auto al = [](const void* p, int64_t ts, uintptr_t A) {
+    return (reinterpret_cast<uintptr_t>(p) % A) == 0 && ((uint64_t)ts * sizeof(E)) % A == 0;
+  };
+  const bool vec = (D % Pack<E>::n == 0) && al(gy, st.gy, 16) && al(x, st.x, 16) &&
+                   al(h_out, st.ho, 16) && aligned16(gx) && aligned16(ghout);
   dim3 grid(post_grid(T)), block(256);
   if constexpr (sizeof(E) == 2 && N == 4) {
-    const bool a32 = aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
+    const bool a32 = al(gy, st.gy, 32) && al(x, st.x, 32) && al(h_out, st.ho, 32) && aligned32(gx) &&
                      aligned32(ghout);
     const int64_t npairs = (T + 1) / 2;
     dim3 pgrid(post_grid(npairs));
@@ -600,11 +608,11 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
     if (split)                                                                              \
       launch(post_bwd_n4x2_kernel<E, VV, true>, sgrid, block, 0, s,                             \
           (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,         \
-          (E*)ghout, ghpost, T, D);                                                         \
+          (E*)ghout, ghpost, T, D, st);                                                         \
     else                                                                                    \
       launch(post_bwd_n4x2_kernel<E, VV, false>, pgrid, block, 0, s,                            \
           (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,         \
-          (E*)ghout, ghpost, T, D);                                                         \
+          (E*)ghout, ghpost, T, D, st);                                                         \
     MHC_LAUNCH_CHECK();                                                                     \
     return MHC_OK;                                                                          \
   } while (0)
@@ -613,26 +621,26 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
 #undef MHC_N4X2
   }
   if constexpr (sizeof(E) == 2 && N == 8) {
-    if (D % 128 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
+    if (D % 128 == 0 && al(gy, st.gy, 32) && al(x, st.x, 32) && al(h_out, st.ho, 32) && aligned32(gx) &&
         aligned32(ghout)) {
       launch(post_bwd_n8_kernel<E, 4>, grid, block, 0, s, (const E*)gy, (const E*)x, h_res,
                                                       (const E*)h_out, h_post, (E*)gx, ghres,
-                                                      (E*)ghout, ghpost, T, D);
+                                                      (E*)ghout, ghpost, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
-    if (D % 64 == 0 && aligned32(gy) && aligned32(x) && aligned32(h_out) && aligned32(gx) &&
+    if (D % 64 == 0 && al(gy, st.gy, 32) && al(x, st.x, 32) && al(h_out, st.ho, 32) && aligned32(gx) &&
         aligned32(ghout)) {
       launch(post_bwd_n8_kernel<E, 2>, grid, block, 0, s, (const E*)gy, (const E*)x, h_res,
                                                       (const E*)h_out, h_post, (E*)gx, ghres,
-                                                      (E*)ghout, ghpost, T, D);
+                                                      (E*)ghout, ghpost, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
     if (D % 32 == 0 && vec) {
       launch(post_bwd_n8_kernel<E, 1>, grid, block, 0, s, (const E*)gy, (const E*)x, h_res,
                                                       (const E*)h_out, h_post, (E*)gx, ghres,
-                                                      (E*)ghout, ghpost, T, D);
+                                                      (E*)ghout, ghpost, T, D, st);
       MHC_LAUNCH_CHECK();
       return MHC_OK;
     }
@@ -640,23 +648,24 @@ static int post_bwd_launch(const void* gy, const void* x, const float* h_res,
   if (vec)
     launch(post_bwd_kernel<E, N, true>, grid, block, 0, s, 
         (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,
-        (E*)ghout, ghpost, T, D);
+        (E*)ghout, ghpost, T, D, st);
   else
     launch(post_bwd_kernel<E, N, false>, grid, block, 0, s, 
         (const E*)gy, (const E*)x, h_res, (const E*)h_out, h_post, (E*)gx, ghres,
-        (E*)ghout, ghpost, T, D);
+        (E*)ghout, ghpost, T, D, st);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
 }
 
 template <int N>
 static int post_fwd_n(int32_t dtype, const void* x, const float* h_res, const void* h_out,
-                      const float* h_post, void* out, int64_t T, int64_t D, cudaStream_t s) {
+                      const float* h_post, void* out, int64_t T, int64_t D, TokStride st,
+                      cudaStream_t s) {
   switch (dtype) {
-    case MHC_F32: return post_fwd_launch<float, N>(x, h_res, h_out, h_post, out, T, D, s);
-    case MHC_F16: return post_fwd_launch<__half, N>(x, h_res, h_out, h_post, out, T, D, s);
+    case MHC_F32: return post_fwd_launch<float, N>(x, h_res, h_out, h_post, out, T, D, st, s);
+    case MHC_F16: return post_fwd_launch<__half, N>(x, h_res, h_out, h_post, out, T, D, st, s);
     case MHC_BF16:
-      return post_fwd_launch<__nv_bfloat16, N>(x, h_res, h_out, h_post, out, T, D, s);
+      return post_fwd_launch<__nv_bfloat16, N>(x, h_res, h_out, h_post, out, T, D, st, s);
     default: return MHC_ERR_UNSUPPORTED_DTYPE;
   }
 }
@@ -664,33 +673,34 @@ static int post_fwd_n(int32_t dtype, const void* x, const float* h_res, const vo
 template <int N>
 static int post_bwd_n(int32_t dtype, const void* gy, const void* x, const float* h_res,
                       const void* h_out, const float* h_post, void* gx, float* ghres,
-                      void* ghout, float* ghpost, int64_t T, int64_t D, cudaStream_t s) {
+                      void* ghout, float* ghpost, int64_t T, int64_t D, TokStride st,
+                      cudaStream_t s) {
   switch (dtype) {
     case MHC_F32:
       return post_bwd_launch<float, N>(gy, x, h_res, h_out, h_post, gx, ghres, ghout, ghpost,
-                                       T, D, s);
+                                       T, D, st, s);
     case MHC_F16:
       return post_bwd_launch<__half, N>(gy, x, h_res, h_out, h_post, gx, ghres, ghout, ghpost,
-                                        T, D, s);
+                                        T, D, st, s);
     case MHC_BF16:
       return post_bwd_launch<__nv_bfloat16, N>(gy, x, h_res, h_out, h_post, gx, ghres, ghout,
-                                               ghpost, T, D, s);
+                                               ghpost, T, D, st, s);
     default: return MHC_ERR_UNSUPPORTED_DTYPE;
   }
 }
 
 int post_fwd_dispatch(int32_t N, int32_t dtype, const void* x, const float* h_res,
                       const void* h_out, const float* h_post, void* out, int64_t T, int64_t D,
-                      cudaStream_t s) {
-  MHC_DISPATCH_N(N, post_fwd_n, dtype, x, h_res, h_out, h_post, out, T, D, s);
+                      TokStride st, cudaStream_t s) {
+  MHC_DISPATCH_N(N, post_fwd_n, dtype, x, h_res, h_out, h_post, out, T, D, st, s);
 }
 
 int post_bwd_dispatch(int32_t N, int32_t dtype, const void* gy, const void* x,
                       const float* h_res, const void* h_out, const float* h_post, void* gx,
                       float* ghres, void* ghout, float* ghpost, int64_t T, int64_t D,
-                      cudaStream_t s) {
+                      TokStride st, cudaStream_t s) {
   MHC_DISPATCH_N(N, post_bwd_n, dtype, gy, x, h_res, h_out, h_post, gx, ghres, ghout, ghpost,
-                 T, D, s);
+                 T, D, st, s);
 }
 
 }  // namespace mhc

@@ -27,7 +27,7 @@ namespace mhc {
 template <typename E, int N, bool VEC, bool SPLIT>
 __global__ void __launch_bounds__(256)
 pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
-                    float* __restrict__ gpre, int64_t T, int64_t D) {
+                    float* __restrict__ gpre, int64_t T, int64_t D, int64_t xs, int64_t gys) {
   pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
@@ -37,26 +37,34 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
   const int64_t clo = SPLIT ? nst * w / nw * 32 : 0;
   const int64_t chi_ = SPLIT ? nst * (w + 1) / nw * 32 : nchunk;
   const int64_t chi = chi_ < nchunk ? chi_ : nchunk;
-  __shared__ float red[SPLIT ? 8 : 1][N];
+  __shared__ double red[SPLIT ? 8 : 1][N];
   const int64_t tstride = SPLIT ? gridDim.x : (int64_t)gridDim.x * nw;
   for (int64_t t = SPLIT ? blockIdx.x : (int64_t)blockIdx.x * nw + w; t < T; t += tstride) {
-    float acc[N];
+    // <gy, x[n]> cancels heavily (its terms have random signs), so each pack's fp32 sum
+    // is added into an fp64 accumulator: the rounding of the long chain no longer
+    // dominates the result's relative error (one fp64 add per pack)
+    double acc[N];
 #pragma unroll
-    for (int n = 0; n < N; ++n) acc[n] = 0.f;
-    const E* xt = x + t * N * D;
-    const E* gt = gy + t * D;
+    for (int n = 0; n < N; ++n) acc[n] = 0.0;
+    const E* xt = x + t * xs;
+    const E* gt = gy + t * gys;
     for (int64_t c = clo + lane; c < chi; c += 32) {
       float g[P], xv[N][P];
       load_pack<E, VEC>(gt + c * P, g);
 #pragma unroll
       for (int n = 0; n < N; ++n) load_pack<E, VEC>(xt + n * D + c * P, xv[n]);
 #pragma unroll
-      for (int n = 0; n < N; ++n)
+      for (int n = 0; n < N; ++n) {
+        float part = 0.f;
 #pragma unroll
-        for (int e = 0; e < P; ++e) acc[n] = fmaf(g[e], xv[n][e], acc[n]);
+        for (int e = 0; e < P; ++e) part = fmaf(g[e], xv[n][e], part);
+        acc[n] += (double)part;
+      }
     }
 #pragma unroll
-    for (int n = 0; n < N; ++n) acc[n] = warp_sum(acc[n]);
+    for (int n = 0; n < N; ++n)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], o);
     if constexpr (SPLIT) {
       if (lane == 0)
 #pragma unroll
@@ -65,7 +73,7 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
       if (w == 0)
 #pragma unroll
         for (int n = 0; n < N; ++n) {
-          acc[n] = 0.f;
+          acc[n] = 0.0;
           for (int ww = 0; ww < nw; ++ww) acc[n] += red[ww][n];
         }
       __syncthreads();
@@ -73,7 +81,7 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
     }
 #pragma unroll
     for (int n = 0; n < N; ++n)
-      if (lane == n) gpre[t * N + n] = acc[n];
+      if (lane == n) gpre[t * N + n] = (float)acc[n];
   }
 }
 
@@ -488,6 +496,177 @@ pre_small_bwd_rows_kernel(const float* __restrict__ mixes, const float* __restri
     partials[(int64_t)blockIdx.x * NP + i] = ((wred[0][i] + wred[1][i]) + wred[2][i]) + wred[3][i];
 }
 
+// Element-parallel small-stage VJP (N = 4): N*N = 16 lanes per token (two tokens per
+// warp), lane (n, j) owning element [n][j] of the Sinkhorn matrices.  Every row or column
+// sum gathers its N values by shuffles and adds them in index order -- the operations and
+// the order of pre_small_bwd_rows_kernel -- but each lane carries one element instead of
+// a row, so a token's dependent chain is about N times shorter and four times as many
+// warps share the latency.  Used while the GPU would otherwise be short of warps (small
+// T).  The grad_alpha / grad_base contributions of a block's tokens are added in token
+// order through shared memory (deterministic), then by pre_reduce_ab_kernel.
+template <int N>
+__global__ void __launch_bounds__(128)
+pre_small_bwd_elems_kernel(const float* __restrict__ mixes, const float* __restrict__ alpha,
+                           const float* __restrict__ base, const float* __restrict__ gpre,
+                           const float* __restrict__ gpost, const float* __restrict__ gcomb,
+                           const float* __restrict__ inv_rms, int64_t T, int64_t HC,
+                           SmallParams sp, float* __restrict__ hist, float* __restrict__ gm_out,
+                           float* __restrict__ coef_out, float* __restrict__ partials,
+                           __nv_bfloat16* __restrict__ g0, __nv_bfloat16* __restrict__ g1,
+                           __nv_bfloat16* __restrict__ gp) {
+  pdl_enter();
+  constexpr int HM = hc_mix(N);
+  constexpr int NN = N * N;
+  constexpr int NP = 3 + HM;
+  constexpr int TPB = 128 / NN;  // tokens per block
+  static_assert(N == 4, "16 lanes per token");
+  __shared__ float sbase[HM];
+  __shared__ float sg[TPB][HM];
+  __shared__ float sc[TPB][NP];  // per-token contributions to grad_alpha | grad_base
+  for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
+  __syncthreads();
+  sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
+  const int lane = threadIdx.x & 31;
+  const int e = lane % NN, n = e / N, j = e % N;
+  const int gl0 = (lane / NN) * NN;  // first lane of this token's group
+  const int tl = threadIdx.x / NN;
+  const int64_t t = (int64_t)blockIdx.x * TPB + tl;
+  const bool valid = t < T;
+  const int64_t tc = valid ? t : T - 1;  // invalid lanes still take part in the shuffles
+  auto at = [&](float v, int src) { return __shfl_sync(0xffffffffu, v, gl0 + src); };
+  auto rowsum = [&](float v) {  // sum of row n, column order
+    float r = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) r += at(v, n * N + jj);
+    return r;
+  };
+  auto colsum = [&](float v) {  // sum of column j, row order
+    float c = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) c += at(v, i * N + j);
+    return c;
+  };
+  const float* mx = mixes + tc * HM;
+  const float ml = mx[2 * N + n * N + j];
+  // forward recompute: logit, clamp, softmax row, +eps, Sinkhorn
+  const float logit = ml * sp.a2 + sbase[2 * N + n * N + j];
+  float P = sp.clamp_on ? fminf(fmaxf(logit, sp.clamp_min), sp.clamp_max) : logit;
+  {
+    float m = at(P, n * N);
+#pragma unroll
+    for (int jj = 1; jj < N; ++jj) m = fmaxf(m, at(P, n * N + jj));
+    const float ex = expf(P - m);
+    const float rs = 1.0f / rowsum(ex);
+    P = ex * rs;
+  }
+  float M = P + sp.hc_eps;
+  M *= 1.0f / (colsum(M) + sp.hc_eps);
+  for (int it = 1; it < sp.iters; ++it) {
+    if (valid) hist[((int64_t)(it - 1) * T + t) * NN + e] = M;
+    M *= 1.0f / (rowsum(M) + sp.hc_eps);
+    M *= 1.0f / (colsum(M) + sp.hc_eps);
+  }
+  // backward through the Sinkhorn iterations (the next older iterate is loaded ahead)
+  float g = gcomb[tc * NN + e];
+  auto load_el = [&](int it) {
+    return valid ? hist[((int64_t)(it - 1) * T + tc) * NN + e] : 0.f;
+  };
+  float Qn = sp.iters > 1 ? load_el(sp.iters - 1) : 0.f;
+  auto col_vjp = [&](float U, float cs) {  // dQ = (g - sum_i g*U) / colsum
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) s = fmaf(at(g, i * N + j), at(U, i * N + j), s);
+    g = (g - s) * cs;
+  };
+  for (int it = sp.iters - 1; it >= 1; --it) {
+    float Q = Qn;
+    if (it > 1) Qn = load_el(it - 1);
+    const float rs = 1.0f / (rowsum(Q) + sp.hc_eps);
+    Q *= rs;                                   // Q = M_in / (rowsum + eps)
+    const float cs = 1.0f / (colsum(Q) + sp.hc_eps);
+    const float U = Q * cs;                    // U = Q / (colsum + eps)
+    col_vjp(U, cs);
+    float s = 0.f;                             // row-norm VJP
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) s = fmaf(at(g, n * N + jj), at(Q, n * N + jj), s);
+    g = (g - s) * rs;
+  }
+  {  // iteration 0: U0 = M0 / cs0, M0 = P + eps
+    const float U0 = P + sp.hc_eps;
+    const float cs = 1.0f / (colsum(U0) + sp.hc_eps);
+    col_vjp(U0 * cs, cs);
+  }
+  // softmax VJP of row n: dl = P * (dP - sum_j dP*P); clamp passes where min <= l <= max
+  float d;
+  {
+    float s = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) s = fmaf(at(g, n * N + jj), at(P, n * N + jj), s);
+    d = P * (g - s);
+    if (sp.clamp_on && !(logit >= sp.clamp_min && logit <= sp.clamp_max)) d = 0.f;
+  }
+  const float gl = d * sp.a2;
+  float c2 = 0.f;  // this row's fma chain over j, as the row-parallel kernel forms it
+#pragma unroll
+  for (int jj = 0; jj < N; ++jj) c2 = fmaf(at(d, n * N + jj), at(ml, n * N + jj), c2);
+  const float m_pre = mx[n], m_post = mx[N + n];
+  const float s0 = sigmoidf_(m_pre * sp.a0 + sbase[n]);
+  const float s1 = sigmoidf_(m_post * sp.a1 + sbase[N + n]);
+  const float dz0 = gpre[tc * N + n] * s0 * (1.0f - s0);
+  const float dz1 = gpost[tc * N + n] * 2.0f * s1 * (1.0f - s1);
+  // per-token contributions (rows add in row order)
+  sc[tl][3 + 2 * N + e] = valid ? d : 0.f;
+  if (j == 0) {
+    sc[tl][3 + n] = valid ? dz0 : 0.f;
+    sc[tl][3 + N + n] = valid ? dz1 : 0.f;
+  }
+  float a0c = valid ? dz0 * m_pre : 0.f, a1c = valid ? dz1 * m_post : 0.f,
+        a2c = valid ? c2 : 0.f;
+  float r0 = 0.f, r1 = 0.f, r2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    r0 += at(a0c, i * N);
+    r1 += at(a1c, i * N);
+    r2 += at(a2c, i * N);
+  }
+  if (e == 0) {
+    sc[tl][0] = r0;
+    sc[tl][1] = r1;
+    sc[tl][2] = r2;
+  }
+  if (j == 0) {
+    sg[tl][n] = dz0 * sp.a0;
+    sg[tl][N + n] = dz1 * sp.a1;
+  }
+  sg[tl][2 * N + e] = gl;
+  if (valid && gm_out) {
+    if (j == 0) {
+      gm_out[t * HM + n] = dz0 * sp.a0;
+      gm_out[t * HM + N + n] = dz1 * sp.a1;
+    }
+    gm_out[t * HM + 2 * N + e] = gl;
+  }
+  __syncwarp();
+  if (e == 0 && valid) {
+    float gmx[HM], dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < HM; ++k) {
+      gmx[k] = sg[tl][k];
+      dot = fmaf(gmx[k], mx[k], dot);
+    }
+    const float inv = inv_rms[t];
+    coef_out[t] = inv * inv / (float)HC * dot;
+    if (g0) write_tc_operand_rows(gmx, inv, t, g0, g1, gp);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NP; i += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < TPB; ++k) acc += sc[k][i];
+    partials[(int64_t)blockIdx.x * NP + i] = acc;
+  }
+}
+
 // One warp per output value: lanes take strided partials, then a fixed-shape tree
 // (warp_sum) -- deterministic for a given number of blocks.
 __global__ void pre_reduce_ab_kernel(const float* __restrict__ partials, int nblk, int HM,
@@ -515,7 +694,7 @@ pre_bwd_gx_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                   const float* __restrict__ phi, const float* __restrict__ gm,
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, const E* acc, E* gx,  // may alias
-                  int64_t T, int64_t D) {
+                  int64_t T, int64_t D, int64_t xs, int64_t gys) {
   pdl_enter();
   constexpr int HM = hc_mix(N);
   const int64_t HC = (int64_t)N * D;
@@ -549,8 +728,8 @@ pre_bwd_gx_kernel(const E* __restrict__ x, const E* __restrict__ gy,
     float gxs = 0.f;
 #pragma unroll
     for (int k = 0; k < HM; ++k) gxs = fmaf(sgm[tt][k], ph[k], gxs);
-    const float xv = ld1<E>(x + t * HC + c);
-    const float g = ld1<E>(gy + t * D + d);
+    const float xv = ld1<E>(x + t * xs + c);
+    const float g = ld1<E>(gy + t * gys + d);
     const float r = fmaf(sinv[tt], gxs, -scoef[tt] * xv);
     float v = fmaf(g, spre[tt][n], r);
     if (acc) v += ld1<E>(acc + t * HC + c);
@@ -565,7 +744,7 @@ template <typename E, int N>
 __global__ void __launch_bounds__(kGpCC)
 pre_bwd_gphi_kernel(const E* __restrict__ x, const float* __restrict__ gm,
                     const float* __restrict__ inv_rms, float* __restrict__ part, int64_t T,
-                    int64_t HC, int64_t tokens_per_split) {
+                    int64_t HC, int64_t tokens_per_split, int64_t xs) {
   pdl_enter();
   constexpr int HM = hc_mix(N);
   __shared__ float sg[kGpTS][HM];
@@ -585,7 +764,7 @@ pre_bwd_gphi_kernel(const E* __restrict__ x, const float* __restrict__ gm,
     if (c < HC) {
       const int nt = (int)min((int64_t)kGpTS, te - ts);
       for (int tt = 0; tt < nt; ++tt) {
-        const float xv = ld1<E>(x + (ts + tt) * HC + c);
+        const float xv = ld1<E>(x + (ts + tt) * xs + c);
 #pragma unroll
         for (int k = 0; k < HM; ++k) acc[k] = fmaf(sg[tt][k], xv, acc[k]);
       }
@@ -615,15 +794,13 @@ static int gphi_splits(int64_t T) {
   return (int)(s < 1 ? 1 : (s > 16 ? 16 : s));
 }
 
-bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
-                         const void* gy, const void* gx);
+bool pre_bwd_tc_eligible(const PreBwdArgs& a);
 size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D);
 void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
                              __nv_bfloat16** g1, __nv_bfloat16** gp);
 int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
                     cudaStream_t s);
-bool pre_bwd_tc8_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
-                          const void* gy, const void* gx);
+bool pre_bwd_tc8_eligible(const PreBwdArgs& a);
 size_t pre_bwd_tc8_ws_bytes(int64_t T, int64_t D);
 int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
                      cudaStream_t s);
@@ -636,7 +813,7 @@ struct BwdWs {
 static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t iters) {
   const int HM = hc_mix(N);
   const int64_t HC = (int64_t)N * D;
-  const int64_t nblk = cdiv(T, 16);  // blocks of the small-stage VJP (>= 16 tokens each)
+  const int64_t nblk = cdiv(T, 8);  // blocks of the small-stage VJP (>= 8 tokens each)
   const int64_t hist_n = (int64_t)(iters > 1 ? iters - 1 : 0) * N * N * T;
   BwdWs w;
   size_t off = 0;
@@ -675,9 +852,9 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const bool acc_ok = a.grad_x_acc == nullptr || aligned16(a.grad_x_acc);
   constexpr bool is_bf16 = std::is_same<E, __nv_bfloat16>::value;
   const bool use_tc = sizeof(E) == 2 && acc_ok &&
-                      pre_bwd_tc_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
+                      pre_bwd_tc_eligible(a);
   const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
-                       pre_bwd_tc8_eligible(T, N, D, a.dtype, a.x, a.grad_y, a.grad_x);
+                       pre_bwd_tc8_eligible(a);
   char* tc_ws = (char*)a.workspace + w.total;
   __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr;
   // bf16: pass 1 writes the operand rows; fp16: they need the maxima first (written from
@@ -689,20 +866,21 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_phi, 0, (size_t)HM * HC * sizeof(float), s));
     return MHC_OK;
   }
-  const bool vec = (D % Pack<E>::n == 0) && aligned16(a.x) && aligned16(a.grad_y);
+  const bool vec = (D % Pack<E>::n == 0) && rows_aligned(a.x, a.x_ts, sizeof(E), 16) &&
+                   rows_aligned(a.grad_y, a.gy_ts, sizeof(E), 16);
   const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;
   dim3 sgrid((unsigned)(want < cap ? want : cap));
   // small T (fewer than 8 tokens per SM): a block per token, its warps split the row
   const bool dsplit = T < cap;
   if (vec && dsplit)
     launch(pre_bwd_dots_kernel<E, N, true, true>, (unsigned)T, 256, 0, s, 
-        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
+        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts);
   else if (vec)
     launch(pre_bwd_dots_kernel<E, N, true, false>, sgrid, 256, 0, s, 
-        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
+        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts);
   else
     launch(pre_bwd_dots_kernel<E, N, false, false>, sgrid, 256, 0, s, 
-        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D);
+        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts);
   MHC_LAUNCH_CHECK();
   // small-stage VJP.  Row-parallel (N lanes per token, N = 4, 8) while a thread per token
   // would not give every SM a block: its chain is N times shorter but it issues ~3N^2
@@ -710,8 +888,13 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   // (T=32768, N=4: 1.169 vs 1.191 ms pre backward; T=1: 56 vs 49.5 us).
   constexpr bool rows_ok = N == 4 || N == 8;
   const bool rows = rows_ok && cdiv(T, 128) < sm_count();
-  const int nblk = (int)cdiv(T, rows ? 128 / N : 128);
-  if (rows)
+  const bool elems = rows && N == 4;  // 16 lanes per token: shorter chain, more warps
+  const int nblk = (int)cdiv(T, elems ? 128 / (N * N) : rows ? 128 / N : 128);
+  if (elems)
+    launch(pre_small_bwd_elems_kernel<4>, nblk, 128, 0, s,
+        a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
+        w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
+  else if (rows)
     launch(pre_small_bwd_rows_kernel<rows_ok ? N : 4>, nblk, 128, 0, s, 
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
@@ -728,13 +911,14 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   launch(pre_bwd_gx_kernel<E, N>, ggrid, kGxCC, 0, s, (const E*)a.x, (const E*)a.grad_y, a.phi,
                                                   w.gm, a.inv_rms, w.coef, a.pre,
-                                                  (const E*)a.grad_x_acc, (E*)a.grad_x, T, D);
+                                                  (const E*)a.grad_x_acc, (E*)a.grad_x, T, D, a.x_ts,
+                                                  a.gy_ts);
   MHC_LAUNCH_CHECK();
   const int ns = gphi_splits(T);
   const int64_t tps = cdiv(T, ns);
   dim3 pgrid((unsigned)cdiv(HC, kGpCC), (unsigned)ns);
   launch(pre_bwd_gphi_kernel<E, N>, pgrid, kGpCC, 0, s, (const E*)a.x, w.gm, a.inv_rms,
-                                                    w.gphi_part, T, HC, tps);
+                                                    w.gphi_part, T, HC, tps, a.x_ts);
   MHC_LAUNCH_CHECK();
   const int64_t n = (int64_t)HM * HC;
   launch(pre_reduce_gphi_kernel, (unsigned)cdiv(n, 256), 256, 0, s, w.gphi_part, ns, n, a.grad_phi);

@@ -114,7 +114,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
                   const float* __restrict__ inv_rms, const float* __restrict__ coef,
                   const float* __restrict__ pre, E* __restrict__ gx,
                   float* __restrict__ gphi_part, int64_t T, int64_t D, BwdGeom geo,
-                  const unsigned* __restrict__ scl) {
+                  const unsigned* __restrict__ scl, int64_t gys) {
   pdl_enter();
   using namespace bwdtc;
   extern __shared__ uint8_t smem_raw[];
@@ -349,7 +349,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
         cf = coef[tt];
 #pragma unroll
         for (int n = 0; n < N; ++n) pr[n] = pre[tt * N + n];
-        const E* gyr = gy + tt * D + g_ * GC + h * 32;
+        const E* gyr = gy + tt * gys + g_ * GC + h * 32;
         const U8 g01 = ld_global_32B(gyr), g23 = ld_global_32B(gyr + 16);
         gyv[0] = g01.a; gyv[1] = g01.b; gyv[2] = g23.a; gyv[3] = g23.b;
       } else {
@@ -469,7 +469,7 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
           if (n == 0) {
             // pull the next item's grad_y row segment into L2 while this item runs
             const int64_t tn = in * 128 + r;
-            if (tn < T) prefetch_l2(gy + tn * D + gn * GC + h * 32);
+            if (tn < T) prefetch_l2(gy + tn * gys + gn * GC + h * 32);
           } else {
             load_item(gn, in);  // this item's operands are dead after its last step
           }
@@ -666,12 +666,14 @@ __global__ void pre_bwd_g_prep_f16_kernel(const float* __restrict__ gm,
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-bool pre_bwd_tc_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
-                         const void* gy, const void* gx) {
-  return (dtype == MHC_BF16 || dtype == MHC_F16) && N == 4 && D % bwdtc::GC == 0 && T > 0 &&
+bool pre_bwd_tc_eligible(const PreBwdArgs& a) {
+  const int64_t T = a.T, D = a.D;
+  const int32_t N = a.N;
+  return (a.dtype == MHC_BF16 || a.dtype == MHC_F16) && N == 4 && D % bwdtc::GC == 0 && T > 0 &&
 
-         T <= (int64_t)INT32_MAX - 256 && (int64_t)N * D <= INT32_MAX && aligned16(x) &&
-         aligned16(gy) && aligned16(gx);
+         T <= (int64_t)INT32_MAX - 256 && (int64_t)N * D <= INT32_MAX &&
+         rows_aligned(a.x, a.x_ts, 2, 16) && rows_aligned(a.grad_y, a.gy_ts, 2, 16) &&
+         aligned16(a.grad_x);
 }
 
 static BwdGeom bwd_tc_geometry(int64_t T, int64_t D) {
@@ -750,7 +752,8 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
       f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int st;
   // operand rows: row extent T, so rows of the last tile beyond T read as zeros
-  if ((st = make_tmap_2d(&m.x, a.x, bf, 2, HC, T, HC * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((st = make_tmap_2d(&m.x, a.x, bf, 2, HC, T, a.x_ts * 2, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   if ((st = make_tmap_2d(&m.g0, w.g0, bf, 2, 64, T, 128, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
@@ -784,7 +787,7 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
   auto kern = a.grad_x_acc ? pre_bwd_tc_kernel<true, E> : pre_bwd_tc_kernel<false, E>;
   launch(kern, geo.ncta, THREADS, SMEM, s, m, (const E*)a.grad_y,
                                                     a.inv_rms, coef, a.pre,
-                                                    (E*)a.grad_x, w.part, T, D, geo, scl);
+                                                    (E*)a.grad_x, w.part, T, D, geo, scl, a.gy_ts);
   MHC_LAUNCH_CHECK();
   const int64_t n = (D / GC) * N * HM * GC;
   launch(pre_bwd_gphi_reduce_kernel, (unsigned)cdiv(n, 256), 256, 0, s, w.part, a.grad_phi, D, geo,

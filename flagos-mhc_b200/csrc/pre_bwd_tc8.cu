@@ -629,11 +629,12 @@ __global__ void bwd8_gphi_reduce_kernel(const float* __restrict__ part, float* _
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-bool pre_bwd_tc8_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
-                          const void* gy, const void* gx) {
-  return dtype == MHC_BF16 && N == 8 && D % bwd8::CB == 0 && T > 0 &&
-         T <= (int64_t)INT32_MAX - 256 && (int64_t)N * D <= INT32_MAX && aligned16(x) &&
-         aligned16(gy) && aligned16(gx);
+bool pre_bwd_tc8_eligible(const PreBwdArgs& a) {
+  const int64_t T = a.T, D = a.D;
+  return a.dtype == MHC_BF16 && a.N == 8 && D % bwd8::CB == 0 && T > 0 &&
+         T <= (int64_t)INT32_MAX - 256 && (int64_t)a.N * D <= INT32_MAX &&
+         rows_aligned(a.x, a.x_ts, 2, 16) && rows_aligned(a.grad_y, a.gy_ts, 2, 16) &&
+         aligned16(a.grad_x);
 }
 
 struct Bwd8Geom {
@@ -697,9 +698,10 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int st;
   Bwd8GxMaps mx;
-  if ((st = make_tmap_2d(&mx.x, a.x, bf, 2, HC, T, HC * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((st = make_tmap_2d(&mx.x, a.x, bf, 2, HC, T, a.x_ts * 2, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
-  if ((st = make_tmap_2d(&mx.gy, a.grad_y, bf, 2, D, T, D * 2, 64, 128,
+  if ((st = make_tmap_2d(&mx.gy, a.grad_y, bf, 2, D, T, a.gy_ts * 2, 64, 128,
                          CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   if ((st = make_tmap_2d(&mx.g, w.g, bf, 2, KG, T, KG * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -715,7 +717,8 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
                          CU_TENSOR_MAP_SWIZZLE_64B)))
     return st;
   Bwd8GpMaps mp;
-  if ((st = make_tmap_2d(&mp.x, a.x, bf, 2, HC, T, HC * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((st = make_tmap_2d(&mp.x, a.x, bf, 2, HC, T, a.x_ts * 2, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   if ((st = make_tmap_2d(&mp.gp, w.gp, bf, 2, GPW, T, GPW * 2, 64, 128,
                          CU_TENSOR_MAP_SWIZZLE_128B)))

@@ -10,6 +10,7 @@ struct PreFwdArgs {
   const float* alpha;
   const float* base;
   int64_t T, D;
+  int64_t x_ts;          // elements between consecutive tokens of x (>= N*D)
   int32_t N, dtype;
   float norm_eps;
   SmallParams sp;
@@ -23,6 +24,8 @@ struct PreFwdArgs {
   float* pre;
   void* workspace;
   size_t workspace_bytes;
+  const float* premix;    // optional: mix partials from the layer-fused post forward
+  int32_t premix_layers;  // K ranges in premix
 };
 
 struct PreBwdArgs {
@@ -37,6 +40,7 @@ struct PreBwdArgs {
   const float* grad_post;
   const float* grad_comb;
   int64_t T, D;
+  int64_t x_ts, gy_ts;    // token strides of x (>= N*D) and grad_y (>= D), in elements
   int32_t N, dtype;
   SmallParams sp;
   void* grad_x;
@@ -47,6 +51,11 @@ struct PreBwdArgs {
   void* workspace;
   size_t workspace_bytes;
 };
+
+// a token-strided input whose every row start is aligned to A bytes
+inline bool rows_aligned(const void* p, int64_t ts, size_t esize, uintptr_t A) {
+  return (reinterpret_cast<uintptr_t>(p) % A) == 0 && ((uint64_t)ts * esize) % A == 0;
+}
 
 // inv_rms = rsqrt(mean(x^2) + eps) over the N*D row (src/mhc_pre_clamp_sinkhorn.py:987-988)
 __device__ __forceinline__ float inv_rms_from_sumsq(float sumsq, int64_t HC, float eps) {

@@ -21,7 +21,8 @@ constexpr int kMixKC = 128;  // columns per K chunk
 template <typename E, int N>
 __global__ void __launch_bounds__(256)
 pre_mix_kernel(const E* __restrict__ x, const float* __restrict__ phi,
-               float* __restrict__ raw, float* __restrict__ sumsq, int64_t T, int64_t HC) {
+               float* __restrict__ raw, float* __restrict__ sumsq, int64_t T, int64_t HC,
+               int64_t x_ts) {
   pdl_enter();
   constexpr int HM = hc_mix(N);
   extern __shared__ float smem[];
@@ -38,7 +39,7 @@ pre_mix_kernel(const E* __restrict__ x, const float* __restrict__ phi,
     for (int idx = tid; idx < kMixTT * kMixKC; idx += 256) {
       const int r = idx / kMixKC, c = idx % kMixKC;
       const int64_t t = t0 + r;
-      xs[r * (kMixKC + 1) + c] = (t < T && kc + c < HC) ? ld1<E>(x + t * HC + kc + c) : 0.f;
+      xs[r * (kMixKC + 1) + c] = (t < T && kc + c < HC) ? ld1<E>(x + t * x_ts + kc + c) : 0.f;
     }
     for (int idx = tid; idx < HM * kMixKC; idx += 256) {
       const int k = idx / kMixKC, c = idx % kMixKC;
@@ -95,7 +96,7 @@ template <typename E, int N, bool VEC>
 __global__ void __launch_bounds__(256)
 pre_apply_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
                  const float* __restrict__ pre, E* __restrict__ y, float* __restrict__ x_scaled,
-                 int64_t T, int64_t D) {
+                 int64_t T, int64_t D, int64_t xs) {
   pdl_enter();
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
@@ -107,7 +108,7 @@ pre_apply_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
     float pr[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
-    const E* xt = x + t * N * D;
+    const E* xt = x + t * xs;
     float* xst = x_scaled ? x_scaled + t * N * D : nullptr;
     for (int64_t c = lane; c < nchunk; c += 32) {
       float xv[N][P];
@@ -148,7 +149,7 @@ template <typename E, int N>
 __global__ void __launch_bounds__(256)
 pre_apply_x16_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
                      const float* __restrict__ pre, E* __restrict__ y,
-                     float* __restrict__ x_scaled, int64_t T, int64_t D) {
+                     float* __restrict__ x_scaled, int64_t T, int64_t D, int64_t xs) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -159,7 +160,7 @@ pre_apply_x16_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
     float pr[N];
 #pragma unroll
     for (int n = 0; n < N; ++n) pr[n] = pre[t * N + n];
-    const E* xt = x + t * N * D;
+    const E* xt = x + t * xs;
     float* xst = x_scaled ? x_scaled + t * N * D : nullptr;
     for (int64_t c = lane; c < nchunk; c += 32) {
       U8 xv[N];
@@ -198,6 +199,7 @@ pre_apply_x16_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
 bool pre_fwd_tc_eligible(const PreFwdArgs& a);
 size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D);
 int pre_fwd_tc_mix(const PreFwdArgs& a, cudaStream_t s);
+int pre_fwd_finish_premix(const PreFwdArgs& a, cudaStream_t s);
 
 // the generic path and the tensor-core path use the workspace differently; size for both
 size_t pre_fwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype) {
@@ -215,7 +217,10 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
   char* ws = (char*)a.workspace;
   float* raw = (float*)ws;
   float* sumsq = (float*)(ws + align_up((size_t)T * HM * 4));
-  if (T > 0 && sizeof(E) == 2 && pre_fwd_tc_eligible(a)) {
+  if (T > 0 && a.premix != nullptr) {
+    const int st = pre_fwd_finish_premix(a, s);
+    if (st != MHC_OK) return st;
+  } else if (T > 0 && sizeof(E) == 2 && pre_fwd_tc_eligible(a)) {
     const int st = pre_fwd_tc_mix(a, s);
     if (st != MHC_OK) return st;
   } else if (T > 0) {
@@ -223,7 +228,7 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
     MHC_CUDA_CHECK(cudaFuncSetAttribute(pre_mix_kernel<E, N>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     launch(pre_mix_kernel<E, N>, (unsigned)cdiv(T, kMixTT), 256, smem, s, 
-        (const E*)a.x, a.phi, raw, sumsq, T, HC);
+        (const E*)a.x, a.phi, raw, sumsq, T, HC, a.x_ts);
     MHC_LAUNCH_CHECK();
     launch(pre_small_kernel<N>, (unsigned)cdiv(T, 128), 128, 0, s, 
         raw, sumsq, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
@@ -231,28 +236,29 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
     MHC_LAUNCH_CHECK();
   }
   if (T > 0) {
-    const bool vec = (D % Pack<E>::n == 0) && aligned16(a.x) && aligned16(a.y) &&
+    const bool vec = (D % Pack<E>::n == 0) && rows_aligned(a.x, a.x_ts, sizeof(E), 16) &&
+                     aligned16(a.y) &&
                      (a.x_scaled == nullptr || aligned16(a.x_scaled));
     const int64_t want = cdiv(T, 8), cap = (int64_t)sm_count() * 8;
     dim3 grid((unsigned)(want < cap ? want : cap));
     const bool v16 = sizeof(E) == 2 && D % 16 == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.x) & 31) == 0 &&
+                     rows_aligned(a.x, a.x_ts, sizeof(E), 32) &&
                      (reinterpret_cast<uintptr_t>(a.y) & 31) == 0 &&
                      (a.x_scaled == nullptr || (reinterpret_cast<uintptr_t>(a.x_scaled) & 31) == 0);
     if constexpr (sizeof(E) == 2) {
       if (v16) {
         launch(pre_apply_x16_kernel<E, N>, grid, 256, 0, s, (const E*)a.x, a.inv_rms, a.pre, (E*)a.y,
-                                                        a.x_scaled, T, D);
+                                                        a.x_scaled, T, D, a.x_ts);
         MHC_LAUNCH_CHECK();
         return MHC_OK;
       }
     }
     if (vec)
       launch(pre_apply_kernel<E, N, true>, grid, 256, 0, s, (const E*)a.x, a.inv_rms, a.pre,
-                                                        (E*)a.y, a.x_scaled, T, D);
+                                                        (E*)a.y, a.x_scaled, T, D, a.x_ts);
     else
       launch(pre_apply_kernel<E, N, false>, grid, 256, 0, s, (const E*)a.x, a.inv_rms, a.pre,
-                                                         (E*)a.y, a.x_scaled, T, D);
+                                                         (E*)a.y, a.x_scaled, T, D, a.x_ts);
     MHC_LAUNCH_CHECK();
   }
   return MHC_OK;

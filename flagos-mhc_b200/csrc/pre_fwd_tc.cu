@@ -493,13 +493,94 @@ pre_mix_finish_kernel(const float* __restrict__ part, int ksplit, const float* _
                         post, comb, logits_out);
 }
 
+// Split-K finish for N = 4 with N*N = 16 lanes per token, lane (n, j) owning element
+// [n][j]: the lane adds the K-range partials of the components it needs in range order,
+// then runs the small stage with one matrix element per lane.  Row and column sums gather
+// their N values by shuffles and add them in index order, as small_rows_outputs does, so
+// every output is bitwise that kernel's; the chain of a token is about N times shorter.
+__global__ void __launch_bounds__(128)
+pre_mix_finish_elems_kernel(const float* __restrict__ part, int ksplit,
+                            const float* __restrict__ alpha, const float* __restrict__ base,
+                            int64_t T, int64_t HC, float norm_eps, SmallParams sp,
+                            float* __restrict__ inv_rms, float* __restrict__ mixes,
+                            float* __restrict__ pre, float* __restrict__ post,
+                            float* __restrict__ comb, float* __restrict__ logits_out,
+                            const float* __restrict__ descale) {
+  pdl_enter();
+  constexpr int N = 4, NN = 16, HM = hc_mix(N);
+  __shared__ float sbase[HM];
+  for (int i = threadIdx.x; i < HM; i += blockDim.x) sbase[i] = base[i];
+  __syncthreads();
+  sp.a0 = alpha[0]; sp.a1 = alpha[1]; sp.a2 = alpha[2];
+  const int lane = threadIdx.x & 31, e = lane % NN, n = e / N, j = e % N;
+  const int gl0 = (lane / NN) * NN;
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / NN;
+  const bool valid = t < T;
+  const int64_t tc = valid ? t : T - 1;  // invalid lanes still take part in the shuffles
+  auto at = [&](float v, int src) { return __shfl_sync(0xffffffffu, v, gl0 + src); };
+  // components of this lane: the logit mix of element e; row heads (j == 0); sum of squares
+  float mlog = 0.f, mpre = 0.f, mpost = 0.f, sq = 0.f;
+  for (int p = 0; p < ksplit; ++p) {
+    const float* src = part + ((int64_t)p * T + tc) * (HM + 1);
+    mlog += src[2 * N + e];
+    if (j == 0) {
+      mpre += src[n];
+      mpost += src[N + n];
+    }
+    if (e == 0) sq += src[HM];
+  }
+  const float inv = at(e == 0 ? inv_rms_from_sumsq(sq, HC, norm_eps) : 0.f, 0);
+  const float sc = descale ? inv * *descale : inv;
+  mlog *= sc;
+  mpre *= sc;
+  mpost *= sc;
+  const float pr = sigmoidf_(mpre * sp.a0 + sbase[n]) + sp.hc_eps;
+  const float po = 2.0f * sigmoidf_(mpost * sp.a1 + sbase[N + n]);
+  const float l = mlog * sp.a2 + sbase[2 * N + e];
+  float M = sp.clamp_on ? fminf(fmaxf(l, sp.clamp_min), sp.clamp_max) : l;
+  float m = at(M, n * N);
+#pragma unroll
+  for (int jj = 1; jj < N; ++jj) m = fmaxf(m, at(M, n * N + jj));
+  M = expf(M - m);
+  float s = 0.f;
+#pragma unroll
+  for (int jj = 0; jj < N; ++jj) s += at(M, n * N + jj);
+  M *= 1.0f / s;
+  M += sp.hc_eps;
+  auto col_norm = [&]() {
+    float c = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) c += at(M, i * N + j);
+    M *= 1.0f / (c + sp.hc_eps);
+  };
+  col_norm();
+  for (int it = 1; it < sp.iters; ++it) {
+    float r = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) r += at(M, n * N + jj);
+    M *= 1.0f / (r + sp.hc_eps);
+    col_norm();
+  }
+  if (!valid) return;
+  if (e == 0) inv_rms[t] = inv;
+  if (j == 0) {
+    mixes[t * HM + n] = mpre;
+    mixes[t * HM + N + n] = mpost;
+    pre[t * N + n] = pr;
+    post[t * N + n] = po;
+  }
+  mixes[t * HM + 2 * N + e] = mlog;
+  comb[t * NN + e] = M;
+  if (logits_out) logits_out[t * NN + e] = l;
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 bool pre_fwd_tc_eligible(const PreFwdArgs& a) {
   const int64_t HC = (int64_t)a.N * a.D;
   return (a.dtype == MHC_BF16 || a.dtype == MHC_F16) && (a.N == 4 || a.N == 8) && HC % 8 == 0 &&
-         aligned16(a.x) &&
+         rows_aligned(a.x, a.x_ts, 2, 16) &&
          a.T > 0 && a.T <= (int64_t)INT32_MAX - 256;
 }
 
@@ -557,7 +638,8 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
   const CUtensorMapDataType dt =
       f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tx, tp;
-  int st = make_tmap_2d(&tx, a.x, dt, 2, HC, T, HC * 2, C::BOX, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  int st = make_tmap_2d(&tx, a.x, dt, 2, HC, T, a.x_ts * 2, C::BOX, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
   st = make_tmap_2d(&tp, phi_hl, dt, 2, HC, C::NP, HC * 2, C::BOX, C::NP,
                     CU_TENSOR_MAP_SWIZZLE_128B);
@@ -579,10 +661,16 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
   if (part) {
     // a warp per token only for many K ranges (few tokens): lanes then share the loads
     const bool warp_tok = ks > 16;
-    auto fin = warp_tok ? pre_mix_finish_kernel<N, true> : pre_mix_finish_kernel<N, false>;
-    launch(fin, (unsigned)cdiv(T, warp_tok ? 4 : 128 / N), 128, 0, s, 
-        part, ks, a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre,
-        a.post_out, a.comb_frag, a.h_res_logits, descale);
+    if (!warp_tok && N == 4) {
+      launch(pre_mix_finish_elems_kernel, (unsigned)cdiv(T, 128 / 16), 128, 0, s, part, ks,
+             a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
+             a.comb_frag, a.h_res_logits, descale);
+    } else {
+      auto fin = warp_tok ? pre_mix_finish_kernel<N, true> : pre_mix_finish_kernel<N, false>;
+      launch(fin, (unsigned)cdiv(T, warp_tok ? 4 : 128 / N), 128, 0, s, part, ks, a.alpha,
+             a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
+             a.comb_frag, a.h_res_logits, descale);
+    }
     MHC_LAUNCH_CHECK();
   }
   return MHC_OK;
@@ -599,6 +687,53 @@ static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
 }
 
 // Runs the tensor-core mix (+ fused small stage); the caller then runs pre_apply.
+// phi (fp32, N*(N+2) rows) -> phi_hl [NP][HC] (16-bit hi / lo rows, zero rows) for the
+// layer-fused post forward; fp16: max|phi| and the descale factor go to slots / slots+16.
+int pre_phi_split_launch(const float* phi, void* phi_hl, int32_t N, int64_t HC, bool f16,
+                         void* slots, cudaStream_t s) {
+  if (N != 4 || HC % 8 != 0 || !aligned16(phi)) return MHC_ERR_INVALID_ARGUMENT;
+  using C = MixCfg<4, 2>;
+  unsigned* maxslot = f16 ? (unsigned*)slots : nullptr;
+  float* descale = f16 ? (float*)((char*)slots + 16) : nullptr;
+  if (f16) {
+    MHC_CUDA_CHECK(cudaMemsetAsync(maxslot, 0, sizeof(unsigned), s));
+    const int64_t m = (int64_t)C::HM * HC;
+    launch(pre_phi_maxabs_kernel, (int)std::min<int64_t>(cdiv(m, 256), (int64_t)sm_count() * 4),
+           256, 0, s, phi, m, maxslot);
+    MHC_LAUNCH_CHECK();
+  }
+  const int64_t bx = std::min<int64_t>(cdiv(HC / 8, 256), 64);
+  if (f16)
+    launch(pre_phi_split8_kernel<__half>, dim3((unsigned)bx, (unsigned)(C::NP - C::HM)), 256, 0,
+           s, phi, (__half*)phi_hl, C::HM, C::NP, HC, maxslot, descale);
+  else
+    launch(pre_phi_split8_kernel<__nv_bfloat16>, dim3((unsigned)bx, (unsigned)(C::NP - C::HM)),
+           256, 0, s, phi, (__nv_bfloat16*)phi_hl, C::HM, C::NP, HC, maxslot, descale);
+  MHC_LAUNCH_CHECK();
+  return MHC_OK;
+}
+
+// The pre operator's small stage from precomputed mix partials ([layers][T][HM+1]: raw
+// mix of each K range, already descaled, and its sum of squares) -- the input written by
+// the layer-fused post forward.
+int pre_fwd_finish_premix(const PreFwdArgs& a, cudaStream_t s) {
+  const int64_t T = a.T, HC = (int64_t)a.N * a.D;
+  const int ks = a.premix_layers;
+  if (a.N == 4 && ks <= 16) {
+    launch(pre_mix_finish_elems_kernel, (unsigned)cdiv(T, 128 / 16), 128, 0, s, a.premix, ks,
+           a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
+           a.comb_frag, a.h_res_logits, (const float*)nullptr);
+  } else if (a.N == 4) {
+    launch(pre_mix_finish_kernel<4, true>, (unsigned)cdiv(T, 4), 128, 0, s, a.premix, ks,
+           a.alpha, a.base, T, HC, a.norm_eps, a.sp, a.inv_rms, a.mixes, a.pre, a.post_out,
+           a.comb_frag, a.h_res_logits, (const float*)nullptr);
+  } else {
+    return MHC_ERR_UNSUPPORTED_N;
+  }
+  MHC_LAUNCH_CHECK();
+  return MHC_OK;
+}
+
 int pre_fwd_tc_mix(const PreFwdArgs& a, cudaStream_t s) {
   switch (a.N) {
     case 4: return pre_fwd_tc_n<4>(a, s);

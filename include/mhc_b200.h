@@ -204,6 +204,85 @@ int mhc_grad_sum_peers(const float* src, float* dst, int64_t n,
                        void* const* regions, int32_t rank, int32_t world,
                        uint32_t epoch, uint64_t timeout_ns, void* stream);
 
+/*
+ * Token-strided forms of the four operators.  Same computation, arguments and
+ * outputs as the entry points above, plus the number of ELEMENTS between the
+ * first elements of consecutive tokens of the named inputs (x: >= N*D;
+ * grad_y of mhc_post_bwd: >= N*D; h_out and the pre operator's grad_y: >= D).
+ * Within a token the (N, D) block (or the D row) must be contiguous; outputs are
+ * always packed.  This is how a (B,S,N,D) view whose B and S strides are
+ * jointly regular (stride_B == S * stride_S), or a (T,N,D) slice of a larger
+ * buffer, runs without a copy: the reference's backward passes x.stride(1) /
+ * grad_y.stride(1) to its kernels the same way
+ * (src/mhc_pre_clamp_sinkhorn_backward.py:1320-1344).  Tensor-core paths need
+ * every token row 16-byte aligned (stride * element size a multiple of 16);
+ * other strides run the general kernels.
+ */
+int mhc_post_fwd_strided(const void* x, int64_t x_token_stride, const float* h_res,
+                         const void* h_out, int64_t h_out_token_stride,
+                         const float* h_post, void* out, int64_t T, int32_t N,
+                         int64_t D, int32_t dtype, void* stream);
+int mhc_post_bwd_strided(const void* grad_y, int64_t grad_y_token_stride,
+                         const void* x, int64_t x_token_stride,
+                         const float* h_res, const void* h_out,
+                         int64_t h_out_token_stride, const float* h_post,
+                         void* grad_x, float* grad_h_res, void* grad_h_out,
+                         float* grad_h_post, int64_t T, int32_t N, int64_t D,
+                         int32_t dtype, void* stream);
+int mhc_pre_fwd_strided(const void* x, int64_t x_token_stride, const float* phi,
+                        const float* alpha, const float* base, int64_t T,
+                        int32_t N, int64_t D, int32_t dtype, float norm_eps,
+                        float hc_eps, float clamp_min, float clamp_max,
+                        int32_t iter_times, void* y, float* post_out,
+                        float* comb_frag, float* inv_rms, float* x_scaled,
+                        float* mixes, float* h_res_logits, float* pre,
+                        void* workspace, size_t workspace_bytes, void* stream);
+/* grad_x_accumulate may be NULL (then this is mhc_pre_bwd with strides). */
+int mhc_pre_bwd_strided(const void* x, int64_t x_token_stride, const float* phi,
+                        const float* alpha, const float* base,
+                        const float* inv_rms, const float* mixes,
+                        const float* pre, const void* grad_y,
+                        int64_t grad_y_token_stride, const float* grad_post_out,
+                        const float* grad_comb_frag, int64_t T, int32_t N,
+                        int64_t D, int32_t dtype, float norm_eps, float hc_eps,
+                        float clamp_min, float clamp_max, int32_t iter_times,
+                        const void* grad_x_accumulate, void* grad_x,
+                        float* grad_phi, float* grad_alpha, float* grad_base,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Layer-level fusion of the forward pass (N = 4, bf16 / fp16, D % 64 == 0, packed
+ * tensors).  No counterpart in the reference: in a stack of layers its callers
+ * (src/autograd.py:14-87) run mhc_post for layer l, whose output x_{l+1} the
+ * pre operator of layer l+1 then reads again for x.phi^T and sum(x^2)
+ * (src/mhc_pre_clamp_sinkhorn.py:897-903).
+ *
+ * mhc_post_fwd_mix is mhc_post_fwd (out is bitwise the same) that also writes
+ * `premix`, [layers][T][N*(N+2)+1] fp32: per K range (layers =
+ * mhc_post_fwd_mix_layers) and token, the raw mix x_{l+1}.phi_next^T and the sum
+ * of squares, computed from out while it is written.  mhc_pre_fwd_premixed is
+ * mhc_pre_fwd of layer l+1 given those partials instead of phi: it reads x only
+ * for y / x_scaled.  phi_next must be the phi that layer l+1 uses.
+ * mhc_post_fwd_mix_supported says whether the fused path applies to a shape.
+ */
+int mhc_post_fwd_mix_supported(int64_t T, int32_t N, int64_t D, int32_t dtype);
+int32_t mhc_post_fwd_mix_layers(int64_t T, int32_t N, int64_t D, int32_t dtype);
+size_t mhc_post_fwd_mix_workspace_bytes(int64_t T, int32_t N, int64_t D,
+                                        int32_t dtype);
+int mhc_post_fwd_mix(const void* x, const float* h_res, const void* h_out,
+                     const float* h_post, void* out, int64_t T, int32_t N,
+                     int64_t D, int32_t dtype, const float* phi_next,
+                     float* premix, void* workspace, size_t workspace_bytes,
+                     void* stream);
+int mhc_pre_fwd_premixed(const void* x, const float* premix,
+                         int32_t premix_layers, const float* alpha,
+                         const float* base, int64_t T, int32_t N, int64_t D,
+                         int32_t dtype, float norm_eps, float hc_eps,
+                         float clamp_min, float clamp_max, int32_t iter_times,
+                         void* y, float* post_out, float* comb_frag,
+                         float* inv_rms, float* x_scaled, float* mixes,
+                         float* h_res_logits, float* pre, void* stream);
+
 /* Size of the static device scratch array used by mhc_pre_fwd_noalloc. */
 #define MHC_PRE_FWD_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -576,3 +576,98 @@ def test_config_c4_layer_chain_autograd():
     for got, want, name in zip((pl.grad, al.grad, bl.grad), acc,
                                ("grad_phi", "grad_alpha", "grad_base")):
         assert rel_err(got, want) <= TOL_FP32, name
+
+
+# ---------------------------------------------------------------- token-strided views
+def _kernels_launched(fn):
+    """Names of the CUDA kernels fn() launches (torch profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        out = fn()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+    return out, names
+
+
+def _ours(names):
+    return all(n.startswith(("void mhc::", "mhc::")) or "mhc::" in n for n in names)
+
+
+@pytest.mark.parametrize("pad", [64, 3])   # 16-byte aligned token rows / misaligned rows
+def test_strided_views_in_place(pad):
+    """Token-strided x / h_out / grad_y (slices of larger buffers) run in place -- every
+    kernel launched is one of this library's.  With 16-byte aligned token rows the same
+    kernels run as for packed tensors (bitwise equal results); misaligned rows take the
+    general kernels (checked against the oracle)."""
+    T, N, D = 300, 4, 256
+    dt = torch.bfloat16
+    same = pad % 8 == 0
+
+    def close(a, b, tol):
+        return torch.equal(a, b) if same else rel_err(a, b) <= tol
+
+    x, hr, ho, hp, gy = (t.to(DEV) for t in post_inputs(T, N, D, dt, seed=pad))
+
+    def strided(t, inner):
+        big = torch.zeros(t.shape[0], inner + pad, dtype=t.dtype, device=DEV)
+        big[:, :inner] = t.reshape(t.shape[0], inner)
+        return big[:, :inner].view(t.shape)
+
+    xv, hv, gv = strided(x, N * D), strided(ho, D), strided(gy, N * D)
+    assert not xv.is_contiguous() and xv.stride(0) == N * D + pad
+    y_ref = M.mhc_post(x, hr, ho, hp)
+    y, names = _kernels_launched(lambda: M.mhc_post(xv, hr, hv, hp))
+    assert _ours(names), names
+    assert close(y, y_ref, TOL_BF16)
+    g_ref = M.mhc_post_backward(gy, x, hr, ho, hp)
+    g, names = _kernels_launched(lambda: M.mhc_post_backward(gv, xv, hr, hv, hp))
+    assert _ours(names), names
+    for a, b, tol in zip(g, g_ref, (TOL_BF16, TOL_FP32, TOL_BF16, TOL_FP32)):
+        assert close(a, b, tol)
+    # pre forward / backward
+    xp, phi, alpha, base, gyp, gpost, gcomb = (t.to(DEV) for t in pre_inputs(T, N, D, dt, seed=7))
+    xpv, gyv = strided(xp, N * D), strided(gyp, D)
+    kw = dict(clamp_min=-5.0, clamp_max=5.0)
+    o_ref = M.mhc_pre_clamp_sinkhorn(xp, phi, alpha, base, need_backward=True, **kw)
+    o, names = _kernels_launched(
+        lambda: M.mhc_pre_clamp_sinkhorn(xpv, phi, alpha, base, need_backward=True, **kw))
+    assert _ours(names), names
+    for k in o_ref:
+        tol = TOL_BF16 if k == "y" else TOL_FP32
+        if k == "comb_frag" and not same:
+            assert abs_err(o[k], o_ref[k]) <= TOL_SINKHORN_ABS
+        else:
+            assert close(o[k], o_ref[k], tol), k
+    sv = [o_ref[k] for k in ("inv_rms", "x_scaled", "mixes", "h_res_logits", "pre")]
+    b_ref = M.mhc_pre_clamp_sinkhorn_backward(xp, phi, alpha, base, *sv, gyp, gpost, gcomb, **kw)
+    b, names = _kernels_launched(
+        lambda: M.mhc_pre_clamp_sinkhorn_backward(xpv, phi, alpha, base, *sv, gyv, gpost, gcomb,
+                                                  **kw))
+    assert _ours(names), names
+    for u, v, tol in zip(b, b_ref, (TOL_BF16, TOL_FP32, TOL_FP32, TOL_FP32)):
+        assert close(u, v, tol)
+
+
+def test_strided_bsnd_view_and_irregular_fallback():
+    """(B,S,N,D) views: every other token of a packed buffer (regular B/S strides) is
+    read in place; a view whose B stride is not S times its S stride is packed first
+    (as the reference's x.stride(1) assumption cannot hold there); both match the
+    oracle."""
+    B, S, N, D = 3, 40, 4, 128
+    dt = torch.bfloat16
+    big = torch.randn(B * S * 2, N, D, generator=torch.Generator().manual_seed(3)).to(dt).to(DEV)
+    xv = big[::2].view(B, S, N, D)                     # stride_B == S * stride_S
+    assert xv.stride(0) == S * xv.stride(1) and not xv.is_contiguous()
+    x2 = torch.randn(B, S + 2, N, D, generator=torch.Generator().manual_seed(4)).to(dt)
+    x2 = x2.to(DEV)[:, 1:S + 1]                        # stride_B != S * stride_S
+    assert x2.stride(0) != S * x2.stride(1)
+    _, phi, alpha, base, _, _, _ = pre_inputs(B * S, N, D, dt, seed=9)
+    phi, alpha, base = phi.to(DEV), alpha.to(DEV), base.to(DEV)
+    for xx in (xv, x2):
+        out = M.mhc_pre_clamp_sinkhorn(xx, phi, alpha, base, need_backward=True)
+        ref = O.pre_fwd(xx.cpu(), phi.cpu(), alpha.cpu(), base.cpu(), dtype=F64)
+        assert out["y"].shape == (B, S, D)
+        assert rel_err(out["y"], ref["y"]) <= TOL_BF16
+        for k in ("mixes", "inv_rms", "pre", "post_out"):
+            assert rel_err(out[k], ref[k]) <= TOL_FP32, k
