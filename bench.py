@@ -612,10 +612,18 @@ def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=N
     from FlagOS_mhc import _C
     if clocks is not None:
         clocks.mark_load()
-    t_end = time.perf_counter() + soak_s
-    while time.perf_counter() < t_end:
+    # soak: the same number of steps on every rank (each step holds a collective), about
+    # soak_s seconds' worth as timed from one step
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+    torch.cuda.synchronize()
+    n = torch.tensor([int(soak_s / max(time.perf_counter() - t0, 1e-4))], device=dev)
+    if world > 1:
+        dist.all_reduce(n, op=dist.ReduceOp.MAX)
+    for _ in range(min(int(n.item()), 20000)):
         run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:

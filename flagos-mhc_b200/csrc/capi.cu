@@ -1,5 +1,6 @@
 // capi.cu -- the extern "C" boundary: argument checks, then dispatch.
 #include <math.h>
+#include <stdlib.h>
 
 #include <atomic>
 
@@ -32,6 +33,14 @@ int tc_host_device_error();
 
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("MHC_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 // Per-device cache of the SM count and of the sm_100 check (set once per device).
 static int g_sms[64];

@@ -313,6 +313,9 @@ __device__ __forceinline__ void pdl_enter() {
   pdl_trigger();
 }
 
+// MHC_PDL=0 in the environment launches without the attribute (A/B measurements).
+bool pdl_enabled();
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                           cudaStream_t stream, Args&&... args) {
@@ -325,7 +328,7 @@ inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -10,23 +10,31 @@
 //
 //   [ stage: n floats ][ result: n floats ][ flags: 2 x kMaxRanks x kMaxCtas u32 ]
 //
+// (stage: this rank's input; result: the sum over the ranks of the slice it owns)
+//
 // The packed vector is cut into `world` slices (rank r owns slice r) and every
 // slice into `G` parts (CTA c of every rank handles part c of every slice), so a
 // CTA only ever waits for the CTAs with its own index on the other GPUs:
 //   1. CTA c copies part c of every slice of its rank's input into its stage and
-//      release-stores `epoch` into flag A[rank][c] of every rank;
+//      stores `epoch` into flag A[rank][c] of every rank;
 //   2. it waits until flag A[p][c] == epoch for every rank p, reads part c of its
 //      own slice from every rank's stage (NVLink loads), sums them in rank order
-//      0..world-1 (so every rank ends with bitwise the same vector) and stores the
-//      sum into part c of slice `rank` of every rank's result area (NVLink
-//      stores), then release-stores flag B[rank][c] on every rank;
-//   3. it waits until flag B[p][c] == epoch for every p (part c of every slice
-//      of its own result area is then final) and copies those parts to `dst`.
-// Step 3's wait also tells a rank that every peer has finished reading its stage,
-// so the next call may overwrite it.  All waits poll with a deadline taken from
-// the global timer; a CTA that runs out records MHC_ERR_TIMEOUT (read back by
-// mhc_device_status) and returns without touching peer memory again.
-// No TMA and no multicast: plain 16-byte loads and stores through peer pointers.
+//      0..world-1 (so every rank ends with bitwise the same vector), writes the sum
+//      into part c of its own result area and stores flag B[rank][c] on every rank;
+//   3. it waits until flag B[p][c] == epoch for every p and copies part c of every
+//      slice s from rank s's result area (NVLink loads for s != rank) to `dst`.
+// Every data write goes to the writer's own memory; only flags cross NVLink as stores.
+// A writer orders its data before its flags with a GPU-scope fence: a GPU's L2 is the
+// point of coherence for its memory, remote NVLink reads included, so data that is in
+// the writer's L2 when a reader sees the flag is what the reader loads.  (A system-scope
+// fence, which also drains towards the host, cost ~20 us per signal on B200.)
+// Reuse: a rank's stage is reread only after every peer signalled B for the previous
+// call, and its result area is rewritten only after every peer signalled A for the next
+// call (a peer signals A after its own previous call, phase-3 reads included, has ended).
+// All waits poll with a deadline taken from the global timer; a CTA that runs out
+// records MHC_ERR_TIMEOUT (read back by mhc_device_status) and returns without
+// touching peer memory again.  No TMA and no multicast: plain 16-byte loads through
+// peer pointers and 4-byte flag stores.
 #include <string.h>
 
 #include "common.cuh"
@@ -61,8 +69,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __host__ __device__ inline int64_t peer_flag_offset(int64_t cap) {
@@ -94,16 +102,15 @@ __device__ bool cta_wait_flags(const PeerArgs& a, int which, uint64_t deadline) 
   return ok != 0;
 }
 
-// Publishes this CTA's writes (stage or result parts) to every rank: the barrier makes
-// them happen before thread 0's system-scope fence, which orders them before the flag
-// stores (release at system scope is cumulative over what the thread has observed).
+// Publishes this CTA's (local) writes to every rank: the barrier makes them happen before
+// thread 0's GPU-scope fence, which orders them before the flag stores.
 template <int W>
 __device__ __forceinline__ void cta_signal(const PeerArgs& a, int which, int c) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    __threadfence();
 #pragma unroll
-    for (int p = 0; p < W; ++p) st_release_sys(flag_ptr(a.region[p], a.cap, which, a.rank, c), a.epoch);
+    for (int p = 0; p < W; ++p) st_relaxed_sys(flag_ptr(a.region[p], a.cap, which, a.rank, c), a.epoch);
   }
 }
 
@@ -176,20 +183,29 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
         for (int p = 1; p < W; ++p) {
           acc.x += v[q][p].x; acc.y += v[q][p].y; acc.z += v[q][p].z; acc.w += v[q][p].w;
         }
-#pragma unroll
-        for (int p = 0; p < W; ++p) st4(a.region[p] + a.cap, u, a.n, acc);
+        st4(mine + a.cap, u, a.n, acc);
       }
     }
   }
   cta_signal<W>(a, 1, c);
-  // 3. part c of every slice of this rank's result area is final: copy it out
+  // 3. every rank's slice part c is final in its owner's result area: gather them
   if (!cta_wait_flags(a, 1, deadline)) return;
+  // all W slices' loads of a pass are issued before the first store
+  int64_t b0[W], b1[W], len = 0;
 #pragma unroll
   for (int s = 0; s < W; ++s) {
-    int64_t u0, u1;
-    part_range(a, s, c, &u0, &u1);
-    for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x)
-      st4(a.dst, u, a.n, ld4(mine + a.cap, u, a.n));
+    part_range(a, s, c, &b0[s], &b1[s]);
+    len = max(len, b1[s] - b0[s]);
+  }
+  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
+    float4 v[W];
+#pragma unroll
+    for (int s = 0; s < W; ++s)
+      v[s] = b0[s] + i < b1[s] ? ld4(a.region[s] + a.cap, b0[s] + i, a.n)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < W; ++s)
+      if (b0[s] + i < b1[s]) st4(a.dst, b0[s] + i, a.n, v[s]);
   }
 }
 

@@ -49,6 +49,19 @@ static_assert(SMEM <= 227 * 1024, "shared memory");
 static_assert(STAGE % 1024 == 0 && PBOX % 1024 == 0, "box alignment");
 }  // namespace pmix
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 struct PostMixMaps {
   CUtensorMap x, ho, phi, out;
 };
@@ -218,16 +231,17 @@ post_mix_tc_kernel(const __grid_constant__ PostMixMaps maps, const float* __rest
           break;
         }
         float csq = 0.f;
+        const uint32_t sbase = tc::smem_u32(stage_x(s, 0));
 #pragma unroll 2
         for (int cc = 0; cc < 4; ++cc) {
           // physical 16-byte column of logical column 4h+cc (128-byte swizzle): the same in
-          // all five boxes; the 8 rows of a swizzle atom use 8 different bank groups
-          const int off = r * 128 + (((4 * h + cc) ^ (r & 7)) << 4);
+          // all five boxes; the 8 rows of a swizzle atom use 8 different bank groups.
+          // Shared-window addresses: ld/st.shared, not generic loads.
+          const uint32_t off = sbase + r * 128 + (((4 * h + cc) ^ (r & 7)) << 4);
           float xf[N][8], hf[8];
 #pragma unroll
-          for (int jj = 0; jj < N; ++jj)
-            widen<E>(*reinterpret_cast<const uint4*>(stage_x(s, jj) + off), xf[jj]);
-          widen<E>(*reinterpret_cast<const uint4*>(stage_x(s, 4) + off), hf);
+          for (int jj = 0; jj < N; ++jj) widen<E>(lds128(off + jj * XBOX), xf[jj]);
+          widen<E>(lds128(off + 4 * XBOX), hf);
 #pragma unroll
           for (int i = 0; i < N; ++i) {
             float o[8];
@@ -243,7 +257,7 @@ post_mix_tc_kernel(const __grid_constant__ PostMixMaps maps, const float* __rest
             widen<E>(ov, of);
 #pragma unroll
             for (int e = 0; e < 8; ++e) csq = fmaf(of[e], of[e], csq);
-            *reinterpret_cast<uint4*>(stage_x(s, i) + off) = ov;  // out row i over x row i
+            sts128(off + i * XBOX, ov);  // out row i over x row i
           }
         }
         sq += csq;

@@ -27,8 +27,19 @@ namespace mhc {
 template <typename E, int N, bool VEC, bool SPLIT>
 __global__ void __launch_bounds__(256)
 pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
-                    float* __restrict__ gpre, int64_t T, int64_t D, int64_t xs, int64_t gys) {
+                    float* __restrict__ gpre, int64_t T, int64_t D, int64_t xs, int64_t gys,
+                    int ndots, const float* __restrict__ phi, E* __restrict__ p0,
+                    E* __restrict__ p1) {
   pdl_enter();
+  // blocks beyond the first ndots write the tensor-core pass's phi operand rows (they
+  // depend only on phi, and ride along with this streaming kernel instead of a launch
+  // of their own)
+  if ((int)blockIdx.x >= ndots) {
+    if constexpr (sizeof(E) == 2)
+      bwd_phi_prep_item<E>(phi, p0, p1, (int64_t)N * D, 1.f,
+                           (int64_t)(blockIdx.x - ndots) * blockDim.x + threadIdx.x);
+    return;
+  }
   constexpr int P = VEC ? Pack<E>::n : 1;
   const int lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5, w = threadIdx.x >> 5;
@@ -38,7 +49,7 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
   const int64_t chi_ = SPLIT ? nst * (w + 1) / nw * 32 : nchunk;
   const int64_t chi = chi_ < nchunk ? chi_ : nchunk;
   __shared__ double red[SPLIT ? 8 : 1][N];
-  const int64_t tstride = SPLIT ? gridDim.x : (int64_t)gridDim.x * nw;
+  const int64_t tstride = SPLIT ? ndots : (int64_t)ndots * nw;
   for (int64_t t = SPLIT ? blockIdx.x : (int64_t)blockIdx.x * nw + w; t < T; t += tstride) {
     // <gy, x[n]> cancels heavily (its terms have random signs), so each pack's fp32 sum
     // is added into an fp64 accumulator: the rounding of the long chain no longer
@@ -797,7 +808,8 @@ static int gphi_splits(int64_t T) {
 bool pre_bwd_tc_eligible(const PreBwdArgs& a);
 size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D);
 void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
-                             __nv_bfloat16** g1, __nv_bfloat16** gp);
+                             __nv_bfloat16** g1, __nv_bfloat16** gp, __nv_bfloat16** p0,
+                             __nv_bfloat16** p1);
 int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
                     cudaStream_t s);
 bool pre_bwd_tc8_eligible(const PreBwdArgs& a);
@@ -856,10 +868,13 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
                        pre_bwd_tc8_eligible(a);
   char* tc_ws = (char*)a.workspace + w.total;
-  __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr;
-  // bf16: pass 1 writes the operand rows; fp16: they need the maxima first (written from
-  // grad_mixes by pre_bwd_tc_main)
-  if (use_tc && is_bf16) pre_bwd_tc_operand_ptrs(tc_ws, T, D, &g0, &g1, &gp);
+  __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr, *p0 = nullptr, *p1 = nullptr;
+  // bf16: pass 1 writes the operand rows (and the dots kernel the phi operand rows); fp16:
+  // they need the maxima first (written from grad_mixes by pre_bwd_tc_main)
+  if (use_tc && is_bf16) pre_bwd_tc_operand_ptrs(tc_ws, T, D, &g0, &g1, &gp, &p0, &p1);
+  PreBwdArgs args = a;
+  args.phi_prepped = p0 != nullptr;
+  const int nphi = p0 ? (int)cdiv(3 * HC, 256) : 0;
   if (T == 0) {
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_alpha, 0, 3 * sizeof(float), s));
     MHC_CUDA_CHECK(cudaMemsetAsync(a.grad_base, 0, HM * sizeof(float), s));
@@ -872,15 +887,12 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   dim3 sgrid((unsigned)(want < cap ? want : cap));
   // small T (fewer than 8 tokens per SM): a block per token, its warps split the row
   const bool dsplit = T < cap;
-  if (vec && dsplit)
-    launch(pre_bwd_dots_kernel<E, N, true, true>, (unsigned)T, 256, 0, s, 
-        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts);
-  else if (vec)
-    launch(pre_bwd_dots_kernel<E, N, true, false>, sgrid, 256, 0, s, 
-        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts);
-  else
-    launch(pre_bwd_dots_kernel<E, N, false, false>, sgrid, 256, 0, s, 
-        (const E*)a.x, (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts);
+  const int ndots = dsplit ? (int)T : (int)sgrid.x;
+  auto dots = vec ? (dsplit ? pre_bwd_dots_kernel<E, N, true, true>
+                            : pre_bwd_dots_kernel<E, N, true, false>)
+                  : pre_bwd_dots_kernel<E, N, false, false>;
+  launch(dots, (unsigned)(ndots + nphi), 256, 0, s, (const E*)a.x, (const E*)a.grad_y, w.gpre, T,
+         D, a.x_ts, a.gy_ts, ndots, a.phi, (E*)p0, (E*)p1);
   MHC_LAUNCH_CHECK();
   // small-stage VJP.  Row-parallel (N lanes per token, N = 4, 8) while a thread per token
   // would not give every SM a block: its chain is N times shorter but it issues ~3N^2
@@ -906,7 +918,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   launch(pre_reduce_ab_kernel, (unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s, w.partials, nblk, HM,
                                                                        a.grad_alpha, a.grad_base);
   MHC_LAUNCH_CHECK();
-  if (use_tc) return pre_bwd_tc_main(a, tc_ws, w.gm, w.coef, s);
+  if (use_tc) return pre_bwd_tc_main(args, tc_ws, w.gm, w.coef, s);
   if (use_tc8) return pre_bwd_tc8_main(a, tc_ws, w.gm, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   launch(pre_bwd_gx_kernel<E, N>, ggrid, kGxCC, 0, s, (const E*)a.x, (const E*)a.grad_y, a.phi,

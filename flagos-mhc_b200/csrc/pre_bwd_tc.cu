@@ -511,38 +511,14 @@ pre_bwd_tc_kernel(const __grid_constant__ BwdTcMaps maps, const E* __restrict__ 
 
 // phi (fp32 [HM][HC]) -> per-column bf16 operand rows P' = [phi_hi | phi_hi | phi_lo | 0]
 // split into P0 [HC][64] and P1 [HC][16].
-// P0 [HC][64] = [phi_hi 0..23 | phi_hi 0..23 | phi_lo 0..15], P1 [HC][16] = [phi_lo 16..23 |
-// 0 x 8].  Thread (c, g) handles column c and mixes 8g..8g+7 (three threads per column).
+// P0 / P1: the phi operand rows (bwd_phi_prep_item), three threads per column.
 template <typename E>
 __global__ void pre_bwd_phi_prep_kernel(const float* __restrict__ phi, E* __restrict__ p0,
                                         E* __restrict__ p1, int64_t HC,
                                         const unsigned* __restrict__ scl) {
   pdl_enter();
-  using namespace bwdtc;
-  static_assert(HM == 24, "three groups of eight mixes");
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t c = idx / 3;
-  const int g = (int)(idx - c * 3);
-  if (c >= HC) return;
   const float sc = scl ? f16_operand_scale(scl[0]) : 1.f;
-  float hi[8], lo[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float p = phi[(int64_t)(8 * g + k) * HC + c] * sc;
-    hi[k] = from_e(to_e<E>(p));
-    lo[k] = p - hi[k];
-  }
-  uint4* d0 = reinterpret_cast<uint4*>(p0 + c * 64);
-  const uint4 vh = narrow<E>(hi), vl = narrow<E>(lo);
-  d0[g] = vh;
-  d0[3 + g] = vh;
-  if (g < 2) {
-    d0[6 + g] = vl;
-  } else {
-    uint4* d1 = reinterpret_cast<uint4*>(p1 + c * 16);
-    d1[0] = vl;
-    d1[1] = make_uint4(0u, 0u, 0u, 0u);
-  }
+  bwd_phi_prep_item<E>(phi, p0, p1, HC, sc, (int64_t)blockIdx.x * blockDim.x + threadIdx.x);
 }
 
 // grad_phi[k][n*D + g*128 + c] = sum over the cells of group g (in order) of slot 0,
@@ -556,9 +532,9 @@ pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ g
   pdl_enter();
   using namespace bwdtc;
   constexpr int64_t SLOT = (int64_t)N * HM * GC;
-  static_assert(SLOT % 256 == 0, "a block must not straddle two groups");
+  static_assert(SLOT % 1024 == 0, "a block (256 threads x 4 columns) stays in one group");
   __shared__ unsigned char split[kMaxCellsPerGroup];
-  const int64_t idx0 = (int64_t)blockIdx.x * blockDim.x;
+  const int64_t idx0 = (int64_t)blockIdx.x * blockDim.x * 4;
   const int64_t g = idx0 / SLOT;
   auto cell_split = [&](int64_t ci) -> bool {
     const int64_t lo = g * geo.ntiles + ci * geo.subt;
@@ -573,18 +549,27 @@ pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ g
   if (table)
     for (int64_t ci = threadIdx.x; ci < geo.cpg; ci += blockDim.x) split[ci] = cell_split(ci);
   __syncthreads();
-  const int64_t inner = idx0 - g * SLOT + threadIdx.x;  // (n, k, c) inside a slot
+  // four consecutive columns c of one (n, k) row per thread (GC is a multiple of 4)
+  const int64_t inner = idx0 - g * SLOT + 4 * (int64_t)threadIdx.x;  // (n, k, c) in a slot
   const int n = (int)(inner / (HM * GC));
   const int k = (int)((inner / GC) % HM);
   const int c = (int)(inner % GC);
-  float s = 0.f;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int64_t ci = 0; ci < geo.cpg; ++ci) {
     const int64_t cell = g * geo.cpg + ci;
-    s += part[(cell * 2) * SLOT + inner];
-    if (table ? split[ci] != 0 : cell_split(ci)) s += part[(cell * 2 + 1) * SLOT + inner];
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(part + (cell * 2) * SLOT + inner));
+    s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+    if (table ? split[ci] != 0 : cell_split(ci)) {
+      const float4 b =
+          __ldcg(reinterpret_cast<const float4*>(part + (cell * 2 + 1) * SLOT + inner));
+      s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+    }
   }
-  if (scl) s *= 1.f / f16_operand_scale(scl[2]);  // exact: a power of two
-  grad_phi[(int64_t)k * (N * D) + n * D + g * GC + c] = s;
+  if (scl) {  // exact: a power of two
+    const float f = 1.f / f16_operand_scale(scl[2]);
+    s.x *= f; s.y *= f; s.z *= f; s.w *= f;
+  }
+  *reinterpret_cast<float4*>(grad_phi + (int64_t)k * (N * D) + n * D + g * GC + c) = s;
 }
 
 // fp16 operands: maxima of |phi|, |grad_mixes| and |inv * grad_mixes| (atomicMax on the
@@ -719,11 +704,14 @@ size_t pre_bwd_tc_ws_bytes(int64_t T, int64_t D) { return bwd_tc_layout(nullptr,
 
 // Pointers to the bf16 operand rows pass 1 writes (inside the tc workspace region).
 void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
-                             __nv_bfloat16** g1, __nv_bfloat16** gp) {
+                             __nv_bfloat16** g1, __nv_bfloat16** gp, __nv_bfloat16** p0,
+                             __nv_bfloat16** p1) {
   BwdTcWs w = bwd_tc_layout((char*)ws, T, D);
   *g0 = w.g0;
   *g1 = w.g1;
   *gp = w.gp;
+  *p0 = w.p0;
+  *p1 = w.p1;
 }
 
 template <typename E>
@@ -744,9 +732,11 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
         gm, a.inv_rms, (__half*)w.g0, (__half*)w.g1, (__half*)w.gp, T, w.scl);
     MHC_LAUNCH_CHECK();
   }
-  launch(pre_bwd_phi_prep_kernel<E>, (unsigned)cdiv(3 * HC, 256), 256, 0, s, a.phi, (E*)w.p0, (E*)w.p1,
-                                                                     HC, scl);
-  MHC_LAUNCH_CHECK();
+  if (!a.phi_prepped) {  // bf16: pre_bwd_dots_kernel's extra blocks wrote P0 / P1
+    launch(pre_bwd_phi_prep_kernel<E>, (unsigned)cdiv(3 * HC, 256), 256, 0, s, a.phi,
+           (E*)w.p0, (E*)w.p1, HC, scl);
+    MHC_LAUNCH_CHECK();
+  }
   BwdTcMaps m;
   const CUtensorMapDataType bf =
       f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -790,7 +780,7 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
                                                     (E*)a.grad_x, w.part, T, D, geo, scl, a.gy_ts);
   MHC_LAUNCH_CHECK();
   const int64_t n = (D / GC) * N * HM * GC;
-  launch(pre_bwd_gphi_reduce_kernel, (unsigned)cdiv(n, 256), 256, 0, s, w.part, a.grad_phi, D, geo,
+  launch(pre_bwd_gphi_reduce_kernel, (unsigned)cdiv(n, 1024), 256, 0, s, w.part, a.grad_phi, D, geo,
                                                                    scl);
   MHC_LAUNCH_CHECK();
   return MHC_OK;

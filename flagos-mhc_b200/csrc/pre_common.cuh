@@ -50,7 +50,39 @@ struct PreBwdArgs {
   float* grad_base;
   void* workspace;
   size_t workspace_bytes;
+  bool phi_prepped;  // set internally: the phi operand rows are already written
 };
+
+// Backward phi operand rows for the N = 4 tensor-core pass, item idx = 3 * column + group:
+// P0 [HC][64] = [phi_hi 0..23 | phi_hi 0..23 | phi_lo 0..15], P1 [HC][16] = [phi_lo 16..23 |
+// 0 x 8]; item (c, g) writes column c's entries of mixes 8g..8g+7.  sc scales phi first
+// (fp16 operands; 1 for bf16).
+template <typename E>
+__device__ __forceinline__ void bwd_phi_prep_item(const float* __restrict__ phi,
+                                                  E* __restrict__ p0, E* __restrict__ p1,
+                                                  int64_t HC, float sc, int64_t idx) {
+  const int64_t c = idx / 3;
+  const int g = (int)(idx - c * 3);
+  if (c >= HC) return;
+  float hi[8], lo[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float p = phi[(int64_t)(8 * g + k) * HC + c] * sc;
+    hi[k] = from_e(to_e<E>(p));
+    lo[k] = p - hi[k];
+  }
+  uint4* d0 = reinterpret_cast<uint4*>(p0 + c * 64);
+  const uint4 vh = narrow<E>(hi), vl = narrow<E>(lo);
+  d0[g] = vh;
+  d0[3 + g] = vh;
+  if (g < 2) {
+    d0[6 + g] = vl;
+  } else {
+    uint4* d1 = reinterpret_cast<uint4*>(p1 + c * 16);
+    d1[0] = vl;
+    d1[1] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
 
 // a token-strided input whose every row start is aligned to A bytes
 inline bool rows_aligned(const void* p, int64_t ts, size_t esize, uintptr_t A) {
