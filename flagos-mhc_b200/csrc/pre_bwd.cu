@@ -22,6 +22,24 @@
 
 namespace mhc {
 
+// Arguments of the comb-VJP blocks that ride along with pre_bwd_dots_kernel (N = 4): 16
+// tokens per 256-thread block write d = dL/dlogit to dlog [T][16].
+struct VjpArgs {
+  const float* mixes;
+  const float* alpha;
+  const float* base;
+  const float* gcomb;
+  float* hist;
+  float* dlog;
+  SmallParams sp;
+  int nblk;  // blocks of this role (0: none)
+};
+
+__device__ __forceinline__ float comb_vjp_elem(float ml, float base_l, const SmallParams& sp,
+                                               float gcomb_e, float* __restrict__ hist,
+                                               int64_t T, int64_t t, int64_t tc, bool valid,
+                                               int e, int gl0);
+
 // SPLIT (small T): a block takes one token, warp w a contiguous range of its chunks; the
 // warps' sums are added in a fixed order.
 template <typename E, int N, bool VEC, bool SPLIT>
@@ -29,8 +47,26 @@ __global__ void __launch_bounds__(256)
 pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                     float* __restrict__ gpre, int64_t T, int64_t D, int64_t xs, int64_t gys,
                     int ndots, const float* __restrict__ phi, E* __restrict__ p0,
-                    E* __restrict__ p1) {
+                    E* __restrict__ p1, int nphi, VjpArgs va) {
   pdl_enter();
+  // blocks after the grad_pre and phi-operand blocks: the comb part of the small-stage
+  // VJP, which needs no grad_pre and so overlaps this streaming pass
+  if ((int)blockIdx.x >= ndots + nphi) {
+    if constexpr (N == 4) {
+      const int lane = threadIdx.x & 31, e = lane & 15, gl0 = lane & 16;
+      const int64_t t = (int64_t)(blockIdx.x - ndots - nphi) * (blockDim.x / 16) +
+                        threadIdx.x / 16;
+      const bool valid = t < T;
+      const int64_t tc = valid ? t : T - 1;
+      SmallParams sp = va.sp;
+      sp.a0 = va.alpha[0]; sp.a1 = va.alpha[1]; sp.a2 = va.alpha[2];
+      const float ml = va.mixes[tc * 24 + 8 + e];
+      const float d = comb_vjp_elem(ml, __ldg(va.base + 8 + e), sp, va.gcomb[tc * 16 + e],
+                                    va.hist, T, t, tc, valid, e, gl0);
+      if (valid) va.dlog[t * 16 + e] = d;
+    }
+    return;
+  }
   // blocks beyond the first ndots write the tensor-core pass's phi operand rows (they
   // depend only on phi, and ride along with this streaming kernel instead of a launch
   // of their own)
@@ -507,6 +543,92 @@ pre_small_bwd_rows_kernel(const float* __restrict__ mixes, const float* __restri
     partials[(int64_t)blockIdx.x * NP + i] = ((wred[0][i] + wred[1][i]) + wred[2][i]) + wred[3][i];
 }
 
+// The comb part of the N = 4 small-stage VJP for one token on a group of 16 lanes (lane e
+// owns element [e / 4][e % 4]): forward recompute of the clamp, row softmax, +eps and the
+// Sinkhorn iterations (iterates stored in hist [iter][T][16]), the VJP back through them
+// and through the softmax, and the clamp mask.  Returns d = dL/dlogit of the lane's
+// element.  It depends on mixes and grad_comb only -- not on grad_pre -- so it can run
+// while grad_pre is still being summed.  Every row / column sum gathers its 4 values by
+// shuffles and adds them in index order (the order of the row-parallel kernel).
+__device__ __forceinline__ float comb_vjp_elem(float ml, float base_l, const SmallParams& sp,
+                                               float gcomb_e, float* __restrict__ hist,
+                                               int64_t T, int64_t t, int64_t tc, bool valid,
+                                               int e, int gl0) {
+  constexpr int N = 4, NN = 16;
+  const int n = e / N, j = e % N;
+  auto at = [&](float v, int src) { return __shfl_sync(0xffffffffu, v, gl0 + src); };
+  auto rowsum = [&](float v) {  // sum of row n, column order
+    float r = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) r += at(v, n * N + jj);
+    return r;
+  };
+  auto colsum = [&](float v) {  // sum of column j, row order
+    float c = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) c += at(v, i * N + j);
+    return c;
+  };
+  // forward recompute: logit, clamp, softmax row, +eps, Sinkhorn
+  const float logit = ml * sp.a2 + base_l;
+  float P = sp.clamp_on ? fminf(fmaxf(logit, sp.clamp_min), sp.clamp_max) : logit;
+  {
+    float m = at(P, n * N);
+#pragma unroll
+    for (int jj = 1; jj < N; ++jj) m = fmaxf(m, at(P, n * N + jj));
+    const float ex = expf(P - m);
+    const float rs = 1.0f / rowsum(ex);
+    P = ex * rs;
+  }
+  float M = P + sp.hc_eps;
+  M *= 1.0f / (colsum(M) + sp.hc_eps);
+  for (int it = 1; it < sp.iters; ++it) {
+    if (valid) hist[((int64_t)(it - 1) * T + t) * NN + e] = M;
+    M *= 1.0f / (rowsum(M) + sp.hc_eps);
+    M *= 1.0f / (colsum(M) + sp.hc_eps);
+  }
+  // backward through the Sinkhorn iterations (the next older iterate is loaded ahead)
+  float g = gcomb_e;
+  auto load_el = [&](int it) {
+    return valid ? hist[((int64_t)(it - 1) * T + tc) * NN + e] : 0.f;
+  };
+  float Qn = sp.iters > 1 ? load_el(sp.iters - 1) : 0.f;
+  auto col_vjp = [&](float U, float cs) {  // dQ = (g - sum_i g*U) / colsum
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) s = fmaf(at(g, i * N + j), at(U, i * N + j), s);
+    g = (g - s) * cs;
+  };
+  for (int it = sp.iters - 1; it >= 1; --it) {
+    float Q = Qn;
+    if (it > 1) Qn = load_el(it - 1);
+    const float rs = 1.0f / (rowsum(Q) + sp.hc_eps);
+    Q *= rs;                                   // Q = M_in / (rowsum + eps)
+    const float cs = 1.0f / (colsum(Q) + sp.hc_eps);
+    const float U = Q * cs;                    // U = Q / (colsum + eps)
+    col_vjp(U, cs);
+    float s = 0.f;                             // row-norm VJP
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) s = fmaf(at(g, n * N + jj), at(Q, n * N + jj), s);
+    g = (g - s) * rs;
+  }
+  {  // iteration 0: U0 = M0 / cs0, M0 = P + eps
+    const float U0 = P + sp.hc_eps;
+    const float cs = 1.0f / (colsum(U0) + sp.hc_eps);
+    col_vjp(U0 * cs, cs);
+  }
+  // softmax VJP of row n: dl = P * (dP - sum_j dP*P); clamp passes where min <= l <= max
+  float d;
+  {
+    float s = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < N; ++jj) s = fmaf(at(g, n * N + jj), at(P, n * N + jj), s);
+    d = P * (g - s);
+    if (sp.clamp_on && !(logit >= sp.clamp_min && logit <= sp.clamp_max)) d = 0.f;
+  }
+  return d;
+}
+
 // Element-parallel small-stage VJP (N = 4): N*N = 16 lanes per token (two tokens per
 // warp), lane (n, j) owning element [n][j] of the Sinkhorn matrices.  Every row or column
 // sum gathers its N values by shuffles and adds them in index order -- the operations and
@@ -515,9 +637,10 @@ pre_small_bwd_rows_kernel(const float* __restrict__ mixes, const float* __restri
 // warps share the latency.  Used while the GPU would otherwise be short of warps (small
 // T).  The grad_alpha / grad_base contributions of a block's tokens are added in token
 // order through shared memory (deterministic), then by pre_reduce_ab_kernel.
-template <int N>
+template <int N, bool PRE_D>
 __global__ void __launch_bounds__(128)
-pre_small_bwd_elems_kernel(const float* __restrict__ mixes, const float* __restrict__ alpha,
+pre_small_bwd_elems_kernel(const float* __restrict__ dlog, const float* __restrict__ mixes,
+                           const float* __restrict__ alpha,
                            const float* __restrict__ base, const float* __restrict__ gpre,
                            const float* __restrict__ gpost, const float* __restrict__ gcomb,
                            const float* __restrict__ inv_rms, int64_t T, int64_t HC,
@@ -559,62 +682,12 @@ pre_small_bwd_elems_kernel(const float* __restrict__ mixes, const float* __restr
   };
   const float* mx = mixes + tc * HM;
   const float ml = mx[2 * N + n * N + j];
-  // forward recompute: logit, clamp, softmax row, +eps, Sinkhorn
-  const float logit = ml * sp.a2 + sbase[2 * N + n * N + j];
-  float P = sp.clamp_on ? fminf(fmaxf(logit, sp.clamp_min), sp.clamp_max) : logit;
-  {
-    float m = at(P, n * N);
-#pragma unroll
-    for (int jj = 1; jj < N; ++jj) m = fmaxf(m, at(P, n * N + jj));
-    const float ex = expf(P - m);
-    const float rs = 1.0f / rowsum(ex);
-    P = ex * rs;
-  }
-  float M = P + sp.hc_eps;
-  M *= 1.0f / (colsum(M) + sp.hc_eps);
-  for (int it = 1; it < sp.iters; ++it) {
-    if (valid) hist[((int64_t)(it - 1) * T + t) * NN + e] = M;
-    M *= 1.0f / (rowsum(M) + sp.hc_eps);
-    M *= 1.0f / (colsum(M) + sp.hc_eps);
-  }
-  // backward through the Sinkhorn iterations (the next older iterate is loaded ahead)
-  float g = gcomb[tc * NN + e];
-  auto load_el = [&](int it) {
-    return valid ? hist[((int64_t)(it - 1) * T + tc) * NN + e] : 0.f;
-  };
-  float Qn = sp.iters > 1 ? load_el(sp.iters - 1) : 0.f;
-  auto col_vjp = [&](float U, float cs) {  // dQ = (g - sum_i g*U) / colsum
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < N; ++i) s = fmaf(at(g, i * N + j), at(U, i * N + j), s);
-    g = (g - s) * cs;
-  };
-  for (int it = sp.iters - 1; it >= 1; --it) {
-    float Q = Qn;
-    if (it > 1) Qn = load_el(it - 1);
-    const float rs = 1.0f / (rowsum(Q) + sp.hc_eps);
-    Q *= rs;                                   // Q = M_in / (rowsum + eps)
-    const float cs = 1.0f / (colsum(Q) + sp.hc_eps);
-    const float U = Q * cs;                    // U = Q / (colsum + eps)
-    col_vjp(U, cs);
-    float s = 0.f;                             // row-norm VJP
-#pragma unroll
-    for (int jj = 0; jj < N; ++jj) s = fmaf(at(g, n * N + jj), at(Q, n * N + jj), s);
-    g = (g - s) * rs;
-  }
-  {  // iteration 0: U0 = M0 / cs0, M0 = P + eps
-    const float U0 = P + sp.hc_eps;
-    const float cs = 1.0f / (colsum(U0) + sp.hc_eps);
-    col_vjp(U0 * cs, cs);
-  }
-  // softmax VJP of row n: dl = P * (dP - sum_j dP*P); clamp passes where min <= l <= max
   float d;
-  {
-    float s = 0.f;
-#pragma unroll
-    for (int jj = 0; jj < N; ++jj) s = fmaf(at(g, n * N + jj), at(P, n * N + jj), s);
-    d = P * (g - s);
-    if (sp.clamp_on && !(logit >= sp.clamp_min && logit <= sp.clamp_max)) d = 0.f;
+  if constexpr (PRE_D) {
+    d = valid ? dlog[tc * NN + e] : 0.f;
+  } else {
+    d = comb_vjp_elem(ml, sbase[2 * N + e], sp, gcomb[tc * NN + e], hist, T, t, tc, valid, e,
+                      gl0);
   }
   const float gl = d * sp.a2;
   float c2 = 0.f;  // this row's fma chain over j, as the row-parallel kernel forms it
@@ -818,7 +891,7 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
                      cudaStream_t s);
 
 struct BwdWs {
-  float *gpre, *gm, *coef, *partials, *hist, *gphi_part;
+  float *gpre, *gm, *coef, *partials, *hist, *gphi_part, *dlog;
   size_t total;
 };
 
@@ -836,6 +909,7 @@ static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t ite
   w.partials = take((size_t)nblk * (3 + HM) * 4);
   w.hist = take((size_t)hist_n * 4);
   w.gphi_part = take((size_t)gphi_splits(T) * HM * HC * 4);
+  w.dlog = take((size_t)T * N * N * 4);
   w.total = off;
   return w;
 }
@@ -888,30 +962,36 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   // small T (fewer than 8 tokens per SM): a block per token, its warps split the row
   const bool dsplit = T < cap;
   const int ndots = dsplit ? (int)T : (int)sgrid.x;
-  auto dots = vec ? (dsplit ? pre_bwd_dots_kernel<E, N, true, true>
-                            : pre_bwd_dots_kernel<E, N, true, false>)
-                  : pre_bwd_dots_kernel<E, N, false, false>;
-  launch(dots, (unsigned)(ndots + nphi), 256, 0, s, (const E*)a.x, (const E*)a.grad_y, w.gpre, T,
-         D, a.x_ts, a.gy_ts, ndots, a.phi, (E*)p0, (E*)p1);
-  MHC_LAUNCH_CHECK();
   // small-stage VJP.  Row-parallel (N lanes per token, N = 4, 8) while a thread per token
   // would not give every SM a block: its chain is N times shorter but it issues ~3N^2
   // shuffles per lane and iteration, so once the GPU is full the one-thread kernel wins
-  // (T=32768, N=4: 1.169 vs 1.191 ms pre backward; T=1: 56 vs 49.5 us).
+  // (T=32768, N=4: 1.169 vs 1.191 ms pre backward; T=1: 56 vs 49.5 us).  For N=4 it runs
+  // element-parallel (16 lanes per token) and in two parts: the comb part, which needs no
+  // grad_pre, as extra blocks of the grad_pre kernel (hidden under its HBM stream), then a
+  // short kernel for the heads, the coefficients and the operand rows.
   constexpr bool rows_ok = N == 4 || N == 8;
   const bool rows = rows_ok && cdiv(T, 128) < sm_count();
-  const bool elems = rows && N == 4;  // 16 lanes per token: shorter chain, more warps
+  const bool elems = rows && N == 4;
+  VjpArgs va{a.mixes, a.alpha, a.base, a.grad_comb, w.hist, w.dlog, a.sp,
+             elems ? (int)cdiv(T, 16) : 0};
+  auto dots = vec ? (dsplit ? pre_bwd_dots_kernel<E, N, true, true>
+                            : pre_bwd_dots_kernel<E, N, true, false>)
+                  : pre_bwd_dots_kernel<E, N, false, false>;
+  launch(dots, (unsigned)(ndots + nphi + va.nblk), 256, 0, s, (const E*)a.x,
+         (const E*)a.grad_y, w.gpre, T, D, a.x_ts, a.gy_ts, ndots, a.phi, (E*)p0, (E*)p1, nphi,
+         va);
+  MHC_LAUNCH_CHECK();
   const int nblk = (int)cdiv(T, elems ? 128 / (N * N) : rows ? 128 / N : 128);
   if (elems)
-    launch(pre_small_bwd_elems_kernel<4>, nblk, 128, 0, s,
+    launch(pre_small_bwd_elems_kernel<4, true>, nblk, 128, 0, s, (const float*)w.dlog,
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   else if (rows)
-    launch(pre_small_bwd_rows_kernel<rows_ok ? N : 4>, nblk, 128, 0, s, 
+    launch(pre_small_bwd_rows_kernel<rows_ok ? N : 4>, nblk, 128, 0, s,
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   else
-    launch(pre_small_bwd_kernel<N>, nblk, 128, 0, s, 
+    launch(pre_small_bwd_kernel<N>, nblk, 128, 0, s,
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   MHC_LAUNCH_CHECK();

@@ -45,7 +45,9 @@ def _worker(rank, world, port, result_q):
         gathered = [None] * world
         dist.all_gather_object(gathered, gx)
         if rank == 0:
-            result_q.put((torch.cat(gathered), gphi_v.clone(), ga_v.clone(), gb_v.clone()))
+            # numpy arrays: pickled by value (torch tensors would travel as shared-memory
+            # handles that vanish when this process exits)
+            result_q.put(tuple(t.numpy().copy() for t in (torch.cat(gathered), gphi_v, ga_v, gb_v)))
     finally:
         dist.destroy_process_group()
 
@@ -60,7 +62,7 @@ def test_token_sharded_backward_matches_full_batch(world):
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = q.get(timeout=120)
+    got = [torch.from_numpy(a) for a in q.get(timeout=120)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -102,8 +104,9 @@ def _failing_worker(rank, world, port, mode, result_q):
     sys.path[:0] = [root, os.path.join(root, "flagos-mhc_b200")]
     from FlagOS_mhc.distributed import allreduce_pre_grads
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    # the group timeout also bounds the rendezvous, so it leaves room for a slow spawn
     dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=3))
+                            timeout=datetime.timedelta(seconds=15))
     buf = torch.ones(24 * 16 + 27)
     views = (buf[:24 * 16].view(24, 16), buf[24 * 16:24 * 16 + 3], buf[24 * 16 + 3:])
     if rank == 1:
