@@ -31,6 +31,7 @@ struct VjpArgs {
   const float* gcomb;
   float* hist;
   float* dlog;
+  unsigned* ticket;  // zeroed here for the element-parallel kernel's last-block sum
   SmallParams sp;
   int nblk;  // blocks of this role (0: none)
 };
@@ -49,6 +50,7 @@ pre_bwd_dots_kernel(const E* __restrict__ x, const E* __restrict__ gy,
                     int ndots, const float* __restrict__ phi, E* __restrict__ p0,
                     E* __restrict__ p1, int nphi, VjpArgs va) {
   pdl_enter();
+  if (va.nblk > 0 && blockIdx.x == 0 && threadIdx.x == 0) *va.ticket = 0u;
   // blocks after the grad_pre and phi-operand blocks: the comb part of the small-stage
   // VJP, which needs no grad_pre and so overlaps this streaming pass
   if ((int)blockIdx.x >= ndots + nphi) {
@@ -647,7 +649,8 @@ pre_small_bwd_elems_kernel(const float* __restrict__ dlog, const float* __restri
                            SmallParams sp, float* __restrict__ hist, float* __restrict__ gm_out,
                            float* __restrict__ coef_out, float* __restrict__ partials,
                            __nv_bfloat16* __restrict__ g0, __nv_bfloat16* __restrict__ g1,
-                           __nv_bfloat16* __restrict__ gp) {
+                           __nv_bfloat16* __restrict__ gp, unsigned* __restrict__ ticket,
+                           float* __restrict__ grad_alpha, float* __restrict__ grad_base) {
   pdl_enter();
   constexpr int HM = hc_mix(N);
   constexpr int NN = N * N;
@@ -749,6 +752,30 @@ pre_small_bwd_elems_kernel(const float* __restrict__ dlog, const float* __restri
     for (int k = 0; k < TPB; ++k) acc += sc[k][i];
     partials[(int64_t)blockIdx.x * NP + i] = acc;
   }
+  if (ticket == nullptr) return;
+  // the last block to finish adds every block's partials into grad_alpha / grad_base, in
+  // the order pre_reduce_ab_kernel uses (lane-strided blocks, then a fixed warp tree), so
+  // which block happens to be last does not change the result
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int o = w; o < NP; o += nw) {
+    float acc = 0.f;
+    for (int b = lane; b < (int)gridDim.x; b += 32) acc += __ldcg(partials + (int64_t)b * NP + o);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      if (o < 3) grad_alpha[o] = acc;
+      else grad_base[o - 3] = acc;
+    }
+  }
+  if (threadIdx.x == 0) *ticket = 0u;  // ready for the next call
 }
 
 // One warp per output value: lanes take strided partials, then a fixed-shape tree
@@ -892,6 +919,7 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
 
 struct BwdWs {
   float *gpre, *gm, *coef, *partials, *hist, *gphi_part, *dlog;
+  unsigned* ticket;
   size_t total;
 };
 
@@ -910,6 +938,7 @@ static BwdWs bwd_layout(char* base, int64_t T, int32_t N, int64_t D, int32_t ite
   w.hist = take((size_t)hist_n * 4);
   w.gphi_part = take((size_t)gphi_splits(T) * HM * HC * 4);
   w.dlog = take((size_t)T * N * N * 4);
+  w.ticket = (unsigned*)take(4);
   w.total = off;
   return w;
 }
@@ -972,7 +1001,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   constexpr bool rows_ok = N == 4 || N == 8;
   const bool rows = rows_ok && cdiv(T, 128) < sm_count();
   const bool elems = rows && N == 4;
-  VjpArgs va{a.mixes, a.alpha, a.base, a.grad_comb, w.hist, w.dlog, a.sp,
+  VjpArgs va{a.mixes, a.alpha, a.base, a.grad_comb, w.hist, w.dlog, w.ticket, a.sp,
              elems ? (int)cdiv(T, 16) : 0};
   auto dots = vec ? (dsplit ? pre_bwd_dots_kernel<E, N, true, true>
                             : pre_bwd_dots_kernel<E, N, true, false>)
@@ -985,7 +1014,8 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   if (elems)
     launch(pre_small_bwd_elems_kernel<4, true>, nblk, 128, 0, s, (const float*)w.dlog,
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
-        w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
+        w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp, w.ticket,
+        a.grad_alpha, a.grad_base);
   else if (rows)
     launch(pre_small_bwd_rows_kernel<rows_ok ? N : 4>, nblk, 128, 0, s,
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
@@ -995,9 +1025,11 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
         a.mixes, a.alpha, a.base, w.gpre, a.grad_post, a.grad_comb, a.inv_rms, T, HC, a.sp,
         w.hist, (use_tc && is_bf16) ? nullptr : w.gm, w.coef, w.partials, g0, g1, gp);
   MHC_LAUNCH_CHECK();
-  launch(pre_reduce_ab_kernel, (unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s, w.partials, nblk, HM,
-                                                                       a.grad_alpha, a.grad_base);
-  MHC_LAUNCH_CHECK();
+  if (!elems) {  // the element-parallel kernel's last block adds the partials itself
+    launch(pre_reduce_ab_kernel, (unsigned)cdiv((3 + HM) * 32, 256), 256, 0, s, w.partials,
+           nblk, HM, a.grad_alpha, a.grad_base);
+    MHC_LAUNCH_CHECK();
+  }
   if (use_tc) return pre_bwd_tc_main(args, tc_ws, w.gm, w.coef, s);
   if (use_tc8) return pre_bwd_tc8_main(a, tc_ws, w.gm, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
