@@ -25,8 +25,11 @@
 // premix gets two layers per K range (one per warp half: its mix components, zeros
 // elsewhere, and its share of the sum of squares); the consumer adds the layers.
 // A stage is released when its MMAs have completed and the four store warps' bulk
-// stores have read it.  (32-column chunks with a 64-byte swizzle and four stages were
-// slower: 64-byte row pieces are a poor DRAM access pattern.)
+// stores have read it.  Measured alternatives, all slower: 32-column chunks with a 64-byte
+// swizzle and four stages (64-byte row pieces are a poor DRAM read pattern); out stored
+// from registers in 32-byte pieces (1.03 ms at T=32768, scattered sectors); TMA stores
+// without an L2 policy (0.98 ms); this kernel: 0.87 ms, against 0.58 ms with no out
+// stores at all, so the store path is what still costs.
 // Every wait is bounded (MHC_ERR_TIMEOUT).  No TMA multicast.
 #include "pre_common.cuh"
 #include "tc.cuh"
@@ -206,6 +209,9 @@ post_mix_tc_kernel(const __grid_constant__ PostMixMaps maps, const float* __rest
     const int r = q * 32 + lane;     // token row within the tile
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const float dsc = descale ? *descale : 1.f;
+    // out leaves L2 first: with the default policy its TMA stores made the L2 read ~40% of
+    // their bytes back from DRAM (0.98 ms against 0.87 ms at T=32768)
+    const uint64_t pol_out = tc::l2_evict_first();
     const int kb = h ? 16 : 0, kn = h ? HM - 16 : 16;  // mix components this warp folds
     uint32_t it = 0, j = 0;
     bool ok = true;
@@ -279,8 +285,9 @@ post_mix_tc_kernel(const __grid_constant__ PostMixMaps maps, const float* __rest
             if (tile * 128 + q * 32 < T) {
 #pragma unroll
               for (int i = 0; i < N; ++i)
-                tc::tma_store_2d(&maps.out, stage_x(s, i) + q * 32 * 128, (int)(i * D) + kc * BOX,
-                                 (int)(tile * 128 + q * 32));
+                tc::tma_store_2d_hint(&maps.out, stage_x(s, i) + q * 32 * 128,
+                                      (int)(i * D) + kc * BOX, (int)(tile * 128 + q * 32),
+                                      pol_out);
             }
             tc::bulk_commit_group();
             tc::bulk_wait_read<0>();  // the stores have read the stage
