@@ -624,7 +624,6 @@ def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=N
     for _ in range(min(int(n.item()), 20000)):
         run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -634,7 +633,7 @@ def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=N
         clocks.mark_start()
     start.record()
     for k in range(K):
-        run_step(M, inp, world, evs[k], x_scaled=x_scaled, reducer=reducer)
+        run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
     stop.record()
     torch.cuda.synchronize()
     if clocks is not None:
@@ -647,6 +646,12 @@ def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=N
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
+    # the per-operator split comes from separate steps: an event between two operators
+    # stops the next one's launch from overlapping the previous kernel's tail (~3 us each)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+    for k in range(K):
+        run_step(M, inp, world, evs[k], x_scaled=x_scaled, reducer=reducer)
+    torch.cuda.synchronize()
     return ms_total, evs, launches
 
 

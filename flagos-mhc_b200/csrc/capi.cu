@@ -34,12 +34,23 @@ int tc_host_device_error();
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
-bool pdl_enabled() {
-  static const bool on = [] {
+// MHC_PDL: 0 = no launch carries the attribute; 1 = every launch does; 2 (default) =
+// every launch but the first of each entry point call.
+static int pdl_mode() {
+  static const int m = [] {
     const char* v = getenv("MHC_PDL");
-    return !(v && v[0] == '0');
+    return (v && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : 2;
   }();
-  return on;
+  return m;
+}
+bool pdl_enabled() { return pdl_mode() != 0; }
+
+static thread_local bool g_first_launch = false;
+void pdl_new_call() { g_first_launch = true; }
+bool pdl_first_launch() {
+  const bool f = g_first_launch;
+  g_first_launch = false;
+  return f && pdl_mode() == 2;
 }
 
 // Per-device cache of the SM count and of the sm_100 check (set once per device).
@@ -59,6 +70,7 @@ int sm_count() {
 }
 
 static int check_device() {
+  pdl_new_call();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MHC_ERR_CUDA;
   if (dev < 0 || dev >= 64) return MHC_ERR_DEVICE;

@@ -315,6 +315,10 @@ __device__ __forceinline__ void pdl_enter() {
 
 // MHC_PDL=0 in the environment launches without the attribute (A/B measurements).
 bool pdl_enabled();
+// Each entry point calls pdl_new_call() before its first launch; that launch then goes
+// without the attribute, so PDL links the kernels of one call only.
+void pdl_new_call();
+bool pdl_first_launch();
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -328,7 +332,7 @@ inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = (!pdl_first_launch() && pdl_enabled()) ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

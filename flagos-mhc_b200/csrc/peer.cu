@@ -302,6 +302,7 @@ int mhc_grad_sum_peers(const float* src, float* dst, int64_t n, void* const* reg
                                        peer_grad_sum_kernel<3>, peer_grad_sum_kernel<4>,
                                        peer_grad_sum_kernel<5>, peer_grad_sum_kernel<6>,
                                        peer_grad_sum_kernel<7>, peer_grad_sum_kernel<8>};
+  pdl_new_call();
   launch(kernels[world - 1], a.ctas, kPeerThreads, 0, (cudaStream_t)stream, a);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? MHC_OK : MHC_ERR_CUDA;

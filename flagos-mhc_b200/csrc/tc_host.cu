@@ -65,6 +65,7 @@ int tc_host_device_error() { return read_and_clear_tu_error(); }
 
 extern "C" int mhc_selftest_wait_timeout(uint32_t spin_limit, void* stream) {
   if (spin_limit == 0) return MHC_ERR_INVALID_ARGUMENT;
+  mhc::pdl_new_call();
   mhc::launch(mhc::wait_selftest_kernel, 1, 32, 0, (cudaStream_t)stream, spin_limit);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
