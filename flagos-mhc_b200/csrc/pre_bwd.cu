@@ -768,7 +768,18 @@ pre_small_bwd_elems_kernel(const float* __restrict__ dlog, const float* __restri
   const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int o = w; o < NP; o += nw) {
     float acc = 0.f;
-    for (int b = lane; b < (int)gridDim.x; b += 32) acc += __ldcg(partials + (int64_t)b * NP + o);
+    // eight loads in flight per lane, added in block order
+    for (int b0 = lane; b0 < (int)gridDim.x; b0 += 32 * 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int b = b0 + 32 * u;
+        v[u] = b < (int)gridDim.x ? __ldcg(partials + (int64_t)b * NP + o) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (b0 + 32 * u < (int)gridDim.x) acc += v[u];
+    }
     acc = warp_sum(acc);
     if (lane == 0) {
       if (o < 3) grad_alpha[o] = acc;
@@ -948,10 +959,10 @@ static bool tc_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
 }
 
 static bool tc8_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
-  return dtype == MHC_BF16 && N == 8 && D % 64 == 0 && T > 0;
+  return (dtype == MHC_BF16 || dtype == MHC_F16) && N == 8 && D % 64 == 0 && T > 0;
 }
 
-// generic region, then (bf16, N=4, D%128==0 or N=8, D%64==0) the tensor-core region
+// generic region, then (bf16 / fp16, N=4, D%128==0 or N=8, D%64==0) the tensor-core region
 size_t pre_bwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype, int32_t iters) {
   size_t n = bwd_layout(nullptr, T, N, D, iters).total;
   if (tc_shape(T, N, D, dtype)) n += align_up(pre_bwd_tc_ws_bytes(T, D));
@@ -968,7 +979,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   constexpr bool is_bf16 = std::is_same<E, __nv_bfloat16>::value;
   const bool use_tc = sizeof(E) == 2 && acc_ok &&
                       pre_bwd_tc_eligible(a);
-  const bool use_tc8 = std::is_same<E, __nv_bfloat16>::value && acc_ok &&
+  const bool use_tc8 = sizeof(E) == 2 && acc_ok &&
                        pre_bwd_tc8_eligible(a);
   char* tc_ws = (char*)a.workspace + w.total;
   __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr, *p0 = nullptr, *p1 = nullptr;

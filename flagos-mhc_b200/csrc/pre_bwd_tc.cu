@@ -576,19 +576,18 @@ pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ g
 // bits of non-negative floats, which order like the floats).
 __global__ void pre_bwd_f16_max_kernel(const float* __restrict__ phi, int64_t nphi,
                                        const float* __restrict__ gm,
-                                       const float* __restrict__ inv_rms, int64_t T,
+                                       const float* __restrict__ inv_rms, int64_t T, int hm,
                                        unsigned* __restrict__ scl) {
   pdl_enter();
-  using namespace bwdtc;
   float mp = 0.f, mg = 0.f, mgp = 0.f;
-  const int64_t ng = T * HM, n = nphi > ng ? nphi : ng;
+  const int64_t ng = T * hm, n = nphi > ng ? nphi : ng;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     if (i < nphi) mp = fmaxf(mp, fabsf(phi[i]));
     if (i < ng) {
       const float g = fabsf(gm[i]);
       mg = fmaxf(mg, g);
-      mgp = fmaxf(mgp, g * inv_rms[i / HM]);
+      mgp = fmaxf(mgp, g * inv_rms[i / hm]);
     }
   }
 #pragma unroll
@@ -726,7 +725,7 @@ static int pre_bwd_tc_run(const PreBwdArgs& a, void* ws, const float* gm, const 
   if (f16) {
     MHC_CUDA_CHECK(cudaMemsetAsync(w.scl, 0, 3 * sizeof(unsigned), s));
     const int64_t n = std::max<int64_t>((int64_t)HM * HC, T * HM);
-    launch(pre_bwd_f16_max_kernel, (unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 4), 256, 0, s, a.phi, (int64_t)HM * HC, gm, a.inv_rms, T, w.scl);
+    launch(pre_bwd_f16_max_kernel, (unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 4), 256, 0, s, a.phi, (int64_t)HM * HC, gm, a.inv_rms, T, HM, w.scl);
     MHC_LAUNCH_CHECK();
     launch(pre_bwd_g_prep_f16_kernel, (unsigned)cdiv(T, 128), 128, 0, s, 
         gm, a.inv_rms, (__half*)w.g0, (__half*)w.g1, (__half*)w.gp, T, w.scl);

@@ -1,5 +1,5 @@
 // pre_bwd_tc8.cu -- mhc_pre_clamp_sinkhorn backward, tensor-core main pass for N = 8
-// (hcMix = 80, bf16 x, D % 64 == 0).
+// (hcMix = 80, bf16 or fp16 x, D % 64 == 0).
 //
 // After pass 1 (pre_bwd.cu: grad_pre dots + small-stage VJP, which writes grad_mixes
 // and coef in fp32), two streaming tcgen05 kernels produce grad_x and grad_phi:
@@ -28,6 +28,12 @@
 #include "tc.cuh"
 
 namespace mhc {
+
+// fp16 operand maxima (pre_bwd_tc.cu)
+__global__ void pre_bwd_f16_max_kernel(const float* __restrict__ phi, int64_t nphi,
+                                       const float* __restrict__ gm,
+                                       const float* __restrict__ inv_rms, int64_t T, int hm,
+                                       unsigned* __restrict__ scl);
 
 namespace bwd8 {
 constexpr int N = 8;
@@ -79,12 +85,16 @@ static_assert(SMEM <= 232448, "shared memory");
 }  // namespace gp
 }  // namespace bwd8
 
-// phi (fp32 [80][HC]) -> P' [HC][256] bf16: [phi_hi | phi_hi | phi_lo | 0] per column.
-// Thread per (column, 8-element chunk): the 16-byte stores of a warp are contiguous.
-__global__ void bwd8_phi_prep_kernel(const float* __restrict__ phi, __nv_bfloat16* __restrict__ p,
-                                     int64_t HC) {
+// phi (fp32 [80][HC]) -> P' [HC][256] (E = bf16 or fp16): [phi_hi | phi_hi | phi_lo | 0]
+// per column.  Thread per (column, 8-element chunk): the 16-byte stores of a warp are
+// contiguous.  fp16: phi is scaled by 2^s from max|phi| (scl[0]) first, so that the lo
+// halves stay clear of fp16's subnormal range; the epilogue divides it out (exact).
+template <typename E>
+__global__ void bwd8_phi_prep_kernel(const float* __restrict__ phi, E* __restrict__ p,
+                                     int64_t HC, const unsigned* __restrict__ scl) {
   pdl_enter();
   using namespace bwd8;
+  const float sc = scl ? f16_operand_scale(scl[0]) : 1.f;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= HC * (KG / 8)) return;
   const int64_t c = i / (KG / 8);
@@ -95,23 +105,27 @@ __global__ void bwd8_phi_prep_kernel(const float* __restrict__ phi, __nv_bfloat1
     const int k = 8 * j + e;
     float r = 0.f;
     if (k < 2 * HM) {
-      r = __bfloat162float(__float2bfloat16_rn(phi[(int64_t)(k % HM) * HC + c]));
+      r = from_e(to_e<E>(phi[(int64_t)(k % HM) * HC + c] * sc));
     } else if (k < 3 * HM) {
-      const float f = phi[(int64_t)(k - 2 * HM) * HC + c];
-      r = f - __bfloat162float(__float2bfloat16_rn(f));
+      const float f = phi[(int64_t)(k - 2 * HM) * HC + c] * sc;
+      r = f - from_e(to_e<E>(f));
     }
     v[e] = r;
   }
-  reinterpret_cast<uint4*>(p + c * KG)[j] = narrow<__nv_bfloat16>(v);
+  reinterpret_cast<uint4*>(p + c * KG)[j] = narrow<E>(v);
 }
 
 // grad_mixes (fp32 [T][80]) and inv_rms -> G' [T][256] = [g_hi | g_lo | g_hi | 0] and
-// Gp [T][192] = [(inv g)_hi | (inv g)_lo | 0] (bf16).  Thread per (token, 8-chunk).
+// Gp [T][192] = [(inv g)_hi | (inv g)_lo | 0] (E).  Thread per (token, 8-chunk).  fp16:
+// g and inv g are scaled by 2^s from their maxima (scl[1], scl[2]).
+template <typename E>
 __global__ void bwd8_g_prep_kernel(const float* __restrict__ gm, const float* __restrict__ inv_rms,
-                                   __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ gpo,
-                                   int64_t T) {
+                                   E* __restrict__ g, E* __restrict__ gpo,
+                                   int64_t T, const unsigned* __restrict__ scl) {
   pdl_enter();
   using namespace bwd8;
+  const float sg = scl ? f16_operand_scale(scl[1]) : 1.f;
+  const float sgp = scl ? f16_operand_scale(scl[2]) : 1.f;
   constexpr int CH = KG / 8 + GPW / 8;  // 56 chunks per token
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * CH) return;
@@ -125,13 +139,13 @@ __global__ void bwd8_g_prep_kernel(const float* __restrict__ gm, const float* __
       const int k = 8 * j + e;
       float r = 0.f;
       if (k < 3 * HM) {
-        const float f = gr[k % HM];
-        const float hi = __bfloat162float(__float2bfloat16_rn(f));
+        const float f = gr[k % HM] * sg;
+        const float hi = from_e(to_e<E>(f));
         r = (k >= HM && k < 2 * HM) ? f - hi : hi;
       }
       v[e] = r;
     }
-    reinterpret_cast<uint4*>(g + t * KG)[j] = narrow<__nv_bfloat16>(v);
+    reinterpret_cast<uint4*>(g + t * KG)[j] = narrow<E>(v);
   } else {
     const int jj = j - KG / 8;
     const float inv = inv_rms[t];
@@ -140,13 +154,13 @@ __global__ void bwd8_g_prep_kernel(const float* __restrict__ gm, const float* __
       const int k = 8 * jj + e;
       float r = 0.f;
       if (k < 2 * HM) {
-        const float f = gr[k % HM] * inv;
-        const float hi = __bfloat162float(__float2bfloat16_rn(f));
+        const float f = gr[k % HM] * inv * sgp;
+        const float hi = from_e(to_e<E>(f));
         r = k < HM ? hi : f - hi;
       }
       v[e] = r;
     }
-    reinterpret_cast<uint4*>(gpo + t * GPW)[jj] = narrow<__nv_bfloat16>(v);
+    reinterpret_cast<uint4*>(gpo + t * GPW)[jj] = narrow<E>(v);
   }
 }
 
@@ -176,11 +190,13 @@ struct Gx8Cursor {
   }
 };
 
-template <bool ACC>
+// E: bf16 or fp16 (x, grad_y, grad_x and the operand rows).  scl: fp16 only, the
+// operand maxima; gxs then carries the factor 2^(s_g + s_phi), divided out with inv.
+template <bool ACC, typename E>
 __global__ void __launch_bounds__(bwd8::gx::THREADS, 1)
 bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict__ inv_rms,
                const float* __restrict__ coef, const float* __restrict__ pre, int64_t T,
-               int64_t D, int64_t total_steps) {
+               int64_t D, int64_t total_steps, const unsigned* __restrict__ scl) {
   pdl_enter();
   using namespace bwd8;
   using namespace bwd8::gx;
@@ -284,7 +300,7 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_bf16(128, CB, false, false);
+      constexpr uint32_t idesc = tc::idesc_16<E>(128, CB, false, false);
       const uint32_t sg = tc::smem_u32(sm + OFF_G), sp = tc::smem_u32(sm + OFF_P);
       Gx8Cursor c;
       c.init(s0, S);
@@ -332,13 +348,15 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
     c.init(s0, S);
     uint32_t yi = 0;
     float inv = 0.f, cf = 0.f;
+    const float unscale =
+        scl ? 1.f / (f16_operand_scale(scl[1]) * f16_operand_scale(scl[0])) : 1.f;
     uint4 gyv[4];
     for (int64_t gs = s0; gs < s1; ++gs, c.next()) {
       const uint32_t k = (uint32_t)(gs - s0);
       const int64_t t = c.tile * 128 + r;
       const bool live = t < T;
       if (c.tile_start) {
-        inv = live ? inv_rms[t] : 0.f;
+        inv = live ? inv_rms[t] * unscale : 0.f;
         cf = live ? coef[t] : 0.f;
       }
       const float prn = live ? pre[t * N + c.n] : 0.f;
@@ -399,8 +417,8 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
         for (int jj = 0; jj < 2; ++jj) {
           const int jv = 2 * jp + jj;
           float xf[8], gf[8], o[8];
-          widen<__nv_bfloat16>(xv[jv], xf);
-          widen<__nv_bfloat16>(gyv[jv], gf);
+          widen<E>(xv[jv], xf);
+          widen<E>(gyv[jv], gf);
 #pragma unroll
           for (int u = 0; u < 8; u += 2) {
             const float2 cx = __fmul2_rn(ncf2, make_float2(xf[u], xf[u + 1]));
@@ -412,11 +430,11 @@ bwd8_gx_kernel(const __grid_constant__ Bwd8GxMaps maps, const float* __restrict_
           }
           if (ld_acc) {
             float a8[8];
-            widen<__nv_bfloat16>(*reinterpret_cast<const uint4*>(orow + ((jv ^ osw) << 4)), a8);
+            widen<E>(*reinterpret_cast<const uint4*>(orow + ((jv ^ osw) << 4)), a8);
 #pragma unroll
             for (int u = 0; u < 8; ++u) o[u] += a8[u];
           }
-          *reinterpret_cast<uint4*>(orow + ((jv ^ osw) << 4)) = narrow<__nv_bfloat16>(o);
+          *reinterpret_cast<uint4*>(orow + ((jv ^ osw) << 4)) = narrow<E>(o);
         }
       }
       tc::fence_proxy_async();  // generic smem writes -> TMA store reads
@@ -448,6 +466,7 @@ __host__ __device__ inline int64_t bwd8_cta_of_step(int64_t s, int64_t total, in
   return ((s + 1) * G - 1) / total;
 }
 
+template <typename E>
 __global__ void __launch_bounds__(bwd8::gp::THREADS, 1)
 bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ part,
                  int64_t ntiles, int64_t total_steps, int maxslot) {
@@ -520,7 +539,7 @@ bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ pa
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_bf16(128, NPH, true, true);
+      constexpr uint32_t idesc = tc::idesc_16<E>(128, NPH, true, true);
       const uint32_t sbase = tc::smem_u32(sm);
       int64_t ct = s0 / ntiles, tile = s0 - ct * ntiles;
       uint32_t seg = 0;
@@ -611,7 +630,8 @@ bwd8_gphi_kernel(const __grid_constant__ Bwd8GpMaps maps, float* __restrict__ pa
 // grad_phi[k][ct*256 + cc] = sum over the CTAs that touched column tile ct, in CTA order.
 __global__ void bwd8_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ gphi,
                                         int64_t HC, int64_t ntiles, int64_t total_steps,
-                                        int64_t G, int maxslot) {
+                                        int64_t G, int maxslot,
+                                        const unsigned* __restrict__ scl) {
   pdl_enter();
   using namespace bwd8;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -623,6 +643,7 @@ __global__ void bwd8_gphi_reduce_kernel(const float* __restrict__ part, float* _
   float s = 0.f;
   for (int64_t sl = 0; sl <= b1 - b0; ++sl)
     s += part[((ct * maxslot + sl) * HM + kx) * gp::CT + cc];
+  if (scl) s *= 1.f / f16_operand_scale(scl[2]);  // exact: a power of two
   gphi[i] = s;
 }
 
@@ -631,7 +652,7 @@ __global__ void bwd8_gphi_reduce_kernel(const float* __restrict__ part, float* _
 // ---------------------------------------------------------------------------
 bool pre_bwd_tc8_eligible(const PreBwdArgs& a) {
   const int64_t T = a.T, D = a.D;
-  return a.dtype == MHC_BF16 && a.N == 8 && D % bwd8::CB == 0 && T > 0 &&
+  return (a.dtype == MHC_BF16 || a.dtype == MHC_F16) && a.N == 8 && D % bwd8::CB == 0 && T > 0 &&
          T <= (int64_t)INT32_MAX - 256 && (int64_t)a.N * D <= INT32_MAX &&
          rows_aligned(a.x, a.x_ts, 2, 16) && rows_aligned(a.grad_y, a.gy_ts, 2, 16) &&
          aligned16(a.grad_x);
@@ -661,8 +682,9 @@ static Bwd8Geom bwd8_geometry(int64_t T, int64_t D) {
 }
 
 struct Bwd8Ws {
-  __nv_bfloat16 *g, *gp, *p;
+  __nv_bfloat16 *g, *gp, *p;  // fp16 x: the same buffers hold fp16 rows
   float* part;
+  unsigned* scl;  // fp16: max |phi|, |grad_mixes|, |inv * grad_mixes| (float bits)
   size_t total;
 };
 
@@ -677,25 +699,39 @@ static Bwd8Ws bwd8_layout(char* base, int64_t T, int64_t D) {
   w.gp = (__nv_bfloat16*)take((size_t)T * GPW * 2);
   w.p = (__nv_bfloat16*)take((size_t)HC * KG * 2);
   w.part = (float*)take((size_t)geo.ncol * geo.maxslot * HM * gp::CT * 4);
+  w.scl = (unsigned*)take(256);
   w.total = off;
   return w;
 }
 
 size_t pre_bwd_tc8_ws_bytes(int64_t T, int64_t D) { return bwd8_layout(nullptr, T, D).total; }
 
-int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
-                     cudaStream_t s) {
+template <typename E>
+static int pre_bwd_tc8_run(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                           cudaStream_t s) {
   using namespace bwd8;
+  constexpr bool f16 = std::is_same<E, __half>::value;
   const int64_t T = a.T, D = a.D, HC = N * D;
   const Bwd8Geom geo = bwd8_geometry(T, D);
   Bwd8Ws w = bwd8_layout((char*)ws, T, D);
-  launch(bwd8_phi_prep_kernel, (unsigned)cdiv(HC * (KG / 8), 256), 256, 0, s, a.phi, w.p, HC);
+  const unsigned* scl = f16 ? w.scl : nullptr;
+  if (f16) {
+    MHC_CUDA_CHECK(cudaMemsetAsync(w.scl, 0, 3 * sizeof(unsigned), s));
+    const int64_t n = std::max<int64_t>((int64_t)HM * HC, T * HM);
+    launch(pre_bwd_f16_max_kernel,
+           (unsigned)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 4), 256, 0, s,
+           a.phi, (int64_t)HM * HC, gm, a.inv_rms, T, HM, w.scl);
+    MHC_LAUNCH_CHECK();
+  }
+  launch(bwd8_phi_prep_kernel<E>, (unsigned)cdiv(HC * (KG / 8), 256), 256, 0, s, a.phi,
+         (E*)w.p, HC, scl);
   MHC_LAUNCH_CHECK();
-  launch(bwd8_g_prep_kernel, (unsigned)cdiv(T * (KG / 8 + GPW / 8), 256), 256, 0, s, 
-      gm, a.inv_rms, w.g, w.gp, T);
+  launch(bwd8_g_prep_kernel<E>, (unsigned)cdiv(T * (KG / 8 + GPW / 8), 256), 256, 0, s,
+         gm, a.inv_rms, (E*)w.g, (E*)w.gp, T, scl);
   MHC_LAUNCH_CHECK();
 
-  const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType bf =
+      f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int st;
   Bwd8GxMaps mx;
   if ((st = make_tmap_2d(&mx.x, a.x, bf, 2, HC, T, a.x_ts * 2, 64, 128,
@@ -728,27 +764,33 @@ int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel<false>,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel<false, E>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, gx::SMEM));
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel<true>,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gx_kernel<true, E>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, gx::SMEM));
-    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gphi_kernel,
+    MHC_CUDA_CHECK(cudaFuncSetAttribute(bwd8_gphi_kernel<E>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, gp::SMEM));
     attr_set[dev] = true;
   }
   const int64_t total_gx = geo.ntiles * (HC / CB);
   int ngx = sm_count();
   if (total_gx < ngx) ngx = (int)total_gx;
-  auto kgx = a.grad_x_acc ? bwd8_gx_kernel<true> : bwd8_gx_kernel<false>;
-  launch(kgx, ngx, gx::THREADS, gx::SMEM, s, mx, a.inv_rms, coef, a.pre, T, D, total_gx);
+  auto kgx = a.grad_x_acc ? bwd8_gx_kernel<true, E> : bwd8_gx_kernel<false, E>;
+  launch(kgx, ngx, gx::THREADS, gx::SMEM, s, mx, a.inv_rms, coef, a.pre, T, D, total_gx, scl);
   MHC_LAUNCH_CHECK();
-  launch(bwd8_gphi_kernel, geo.grid_gp, gp::THREADS, gp::SMEM, s, mp, w.part, geo.ntiles,
+  launch(bwd8_gphi_kernel<E>, geo.grid_gp, gp::THREADS, gp::SMEM, s, mp, w.part, geo.ntiles,
                                                               geo.total_gp, geo.maxslot);
   MHC_LAUNCH_CHECK();
   launch(bwd8_gphi_reduce_kernel, (unsigned)cdiv((int64_t)HM * HC, 256), 256, 0, s, 
-      w.part, a.grad_phi, HC, geo.ntiles, geo.total_gp, geo.grid_gp, geo.maxslot);
+      w.part, a.grad_phi, HC, geo.ntiles, geo.total_gp, geo.grid_gp, geo.maxslot, scl);
   MHC_LAUNCH_CHECK();
   return MHC_OK;
+}
+
+int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                     cudaStream_t s) {
+  if (a.dtype == MHC_F16) return pre_bwd_tc8_run<__half>(a, ws, gm, coef, s);
+  return pre_bwd_tc8_run<__nv_bfloat16>(a, ws, gm, coef, s);
 }
 
 int pre_bwd_tc8_device_error() { return read_and_clear_tu_error(); }

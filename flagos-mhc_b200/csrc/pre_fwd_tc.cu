@@ -520,6 +520,7 @@ pre_mix_finish_elems_kernel(const float* __restrict__ part, int ksplit,
   auto at = [&](float v, int src) { return __shfl_sync(0xffffffffu, v, gl0 + src); };
   // components of this lane: the logit mix of element e; row heads (j == 0); sum of squares
   float mlog = 0.f, mpre = 0.f, mpost = 0.f, sq = 0.f;
+#pragma unroll 4
   for (int p = 0; p < ksplit; ++p) {
     const float* src = part + ((int64_t)p * T + tc) * (HM + 1);
     mlog += src[2 * N + e];

@@ -397,7 +397,7 @@ def test_pre_bwd_n8_tensor_core(T, D):
 
 
 @pytest.mark.parametrize("T,N,D,dt", [(300, 4, 256, torch.bfloat16), (300, 4, 256, torch.float16),
-                                      (300, 8, 128, torch.bfloat16),
+                                      (300, 8, 128, torch.bfloat16), (300, 8, 128, torch.float16),
                                       (37, 4, 100, torch.bfloat16), (130, 4, 64, torch.float32)])
 def test_pre_bwd_grad_x_accumulate(T, N, D, dt):
     """grad_x_accumulate (layer fusion: the post backward's grad_x added inside the pre
@@ -463,11 +463,13 @@ def test_pre_bwd_n8_iteration_counts(iters):
         assert rel_err(a, b) <= TOL_FP32, name
 
 
-def test_pre_bwd_fp16_tensor_core_many_tiles():
+@pytest.mark.parametrize("N,D", [(4, 256), (8, 192)])
+def test_pre_bwd_fp16_tensor_core_many_tiles(N, D):
     """fp16 x on the tensor-core backward (fp16 operand rows scaled by powers of two from
-    the maxima of phi, grad_mixes and inv*grad_mixes): many tiles, a ragged last tile,
-    against the fp64 oracle on the same saved tensors."""
-    T, N, D = 148 * 128 + 77, 4, 256
+    the maxima of phi, grad_mixes and inv*grad_mixes; N=4 single pass, N=8 gx + grad_phi
+    kernels): many tiles, a ragged last tile, against the fp64 oracle on the same saved
+    tensors."""
+    T = 148 * 128 + 77
     x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.float16, seed=5,
                                                        phi_std=2.0 / (N * D) ** 0.5)
     kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-4.0, clamp_max=4.0, iter_times=20)
