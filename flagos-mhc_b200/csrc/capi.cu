@@ -20,6 +20,7 @@ int post_bwd_dispatch(int32_t N, int32_t dtype, const void* gy, const void* x,
 int pre_fwd_tc_device_error();
 int pre_bwd_tc_device_error();
 int pre_bwd_tc8_device_error();
+int pre_bwd_tc32_device_error();
 int peer_device_error();
 int post_mix_device_error();
 bool post_mix_eligible(int64_t T, int32_t N, int64_t D, int32_t dtype, const void* x,
@@ -144,7 +145,8 @@ int mhc_device_status(void) {
   const int d = peer_device_error();
   const int e = tc_host_device_error();
   const int f = post_mix_device_error();
-  const int all[6] = {a, b, c, d, e, f};
+  const int g = pre_bwd_tc32_device_error();
+  const int all[7] = {a, b, c, d, e, f, g};
   for (int v : all)
     if (v != MHC_OK) return v;
   return MHC_OK;

@@ -169,6 +169,11 @@ __device__ __forceinline__ float f16_operand_scale(unsigned max_bits) {
   return ldexpf(1.f, 14 - e);
 }
 
+// v with the low 13 mantissa bits cleared: the part of an fp32 operand kind::tf32 uses.
+__device__ __forceinline__ float tf32_hi(float v) {
+  return __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+}
+
 __device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
 
 // ---------------------------------------------------------------------------

@@ -924,6 +924,10 @@ void pre_bwd_tc_operand_ptrs(void* ws, int64_t T, int64_t D, __nv_bfloat16** g0,
 int pre_bwd_tc_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
                     cudaStream_t s);
 bool pre_bwd_tc8_eligible(const PreBwdArgs& a);
+bool pre_bwd_tc32_eligible(const PreBwdArgs& a);
+size_t pre_bwd_tc32_ws_bytes(int64_t T, int32_t N, int64_t D);
+int pre_bwd_tc32_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
+                      cudaStream_t s);
 size_t pre_bwd_tc8_ws_bytes(int64_t T, int64_t D);
 int pre_bwd_tc8_main(const PreBwdArgs& a, void* ws, const float* gm, const float* coef,
                      cudaStream_t s);
@@ -962,11 +966,14 @@ static bool tc8_shape(int64_t T, int32_t N, int64_t D, int32_t dtype) {
   return (dtype == MHC_BF16 || dtype == MHC_F16) && N == 8 && D % 64 == 0 && T > 0;
 }
 
-// generic region, then (bf16 / fp16, N=4, D%128==0 or N=8, D%64==0) the tensor-core region
+// generic region, then (bf16 / fp16, N=4, D%128==0 or N=8, D%64==0; fp32, N=4 or 8,
+// D%32==0) the tensor-core region
 size_t pre_bwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype, int32_t iters) {
   size_t n = bwd_layout(nullptr, T, N, D, iters).total;
   if (tc_shape(T, N, D, dtype)) n += align_up(pre_bwd_tc_ws_bytes(T, D));
   if (tc8_shape(T, N, D, dtype)) n += align_up(pre_bwd_tc8_ws_bytes(T, D));
+  if (dtype == MHC_F32 && (N == 4 || N == 8) && D % 32 == 0 && T > 0)
+    n += align_up(pre_bwd_tc32_ws_bytes(T, N, D));
   return n;
 }
 
@@ -981,6 +988,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
                       pre_bwd_tc_eligible(a);
   const bool use_tc8 = sizeof(E) == 2 && acc_ok &&
                        pre_bwd_tc8_eligible(a);
+  const bool use_tc32 = sizeof(E) == 4 && pre_bwd_tc32_eligible(a);
   char* tc_ws = (char*)a.workspace + w.total;
   __nv_bfloat16 *g0 = nullptr, *g1 = nullptr, *gp = nullptr, *p0 = nullptr, *p1 = nullptr;
   // bf16: pass 1 writes the operand rows (and the dots kernel the phi operand rows); fp16:
@@ -1043,6 +1051,7 @@ static int pre_bwd_impl(const PreBwdArgs& a, cudaStream_t s) {
   }
   if (use_tc) return pre_bwd_tc_main(args, tc_ws, w.gm, w.coef, s);
   if (use_tc8) return pre_bwd_tc8_main(a, tc_ws, w.gm, w.coef, s);
+  if (use_tc32) return pre_bwd_tc32_main(a, tc_ws, w.gm, w.coef, s);
   dim3 ggrid((unsigned)cdiv(T, kGxTT), (unsigned)cdiv(HC, kGxCC));
   launch(pre_bwd_gx_kernel<E, N>, ggrid, kGxCC, 0, s, (const E*)a.x, (const E*)a.grad_y, a.phi,
                                                   w.gm, a.inv_rms, w.coef, a.pre,

@@ -197,7 +197,7 @@ pre_apply_x16_kernel(const E* __restrict__ x, const float* __restrict__ inv_rms,
 // Host side
 // ---------------------------------------------------------------------------
 bool pre_fwd_tc_eligible(const PreFwdArgs& a);
-size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D);
+size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype);
 int pre_fwd_tc_mix(const PreFwdArgs& a, cudaStream_t s);
 int pre_fwd_finish_premix(const PreFwdArgs& a, cudaStream_t s);
 
@@ -205,8 +205,7 @@ int pre_fwd_finish_premix(const PreFwdArgs& a, cudaStream_t s);
 size_t pre_fwd_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype) {
   const int HM = hc_mix(N);
   const size_t generic = align_up((size_t)T * HM * 4) + align_up((size_t)T * 4);
-  const size_t tc = ((dtype == MHC_BF16 || dtype == MHC_F16) && (N == 4 || N == 8))
-                        ? pre_fwd_tc_ws_bytes(T, N, D) : 0;
+  const size_t tc = (N == 4 || N == 8) ? pre_fwd_tc_ws_bytes(T, N, D, dtype) : 0;
   return generic > tc ? generic : tc;
 }
 
@@ -220,7 +219,7 @@ static int pre_fwd_impl(const PreFwdArgs& a, cudaStream_t s) {
   if (T > 0 && a.premix != nullptr) {
     const int st = pre_fwd_finish_premix(a, s);
     if (st != MHC_OK) return st;
-  } else if (T > 0 && sizeof(E) == 2 && pre_fwd_tc_eligible(a)) {
+  } else if (T > 0 && pre_fwd_tc_eligible(a)) {
     const int st = pre_fwd_tc_mix(a, s);
     if (st != MHC_OK) return st;
   } else if (T > 0) {

@@ -48,6 +48,66 @@ struct MixCfg {
   static constexpr int THREADS = 192;
 };
 
+// fp32 x (kind::tf32): the tensor core reads the top 19 bits of an fp32 operand (sign,
+// exponent, 10 mantissa bits).  x is used as stored, so the MMA sees x_hi = x with the low
+// 13 mantissa bits cleared; the sum-of-squares warps write x_lo = x - x_hi (exact in fp32)
+// into a second buffer of the stage.  phi is split the same way into rows [phi_hi;
+// phi_lo] (pre_phi_split_tf32_kernel), and D = x_hi.[phi_hi;phi_lo]^T + x_lo.[phi_hi;
+// phi_lo]^T, so columns [0,HM) + [HM,2HM) hold x.phi^T up to the tf32 rounding of the
+// lo parts (~2^-21 relative per product).
+template <int N, int NB, typename E>
+struct MixCfgE : MixCfg<N, NB> {
+  static constexpr bool F32 = false;
+  static constexpr int XL_BYTES = 0;
+};
+template <int N, int NB>
+struct MixCfgE<N, NB, float> {
+  static constexpr bool F32 = true;
+  static constexpr int HM = hc_mix(N);
+  static constexpr int NP = (2 * HM + 15) / 16 * 16;
+  static constexpr int BUFCOL = (NP + 16 + 31) / 32 * 32;
+  static constexpr int TMEM_COLS = (2 * BUFCOL <= 32) ? 32 : (2 * BUFCOL <= 64) ? 64
+                                   : (2 * BUFCOL <= 128) ? 128 : (2 * BUFCOL <= 256) ? 256 : 512;
+  static constexpr int BOX = 32;                                 // fp32 columns per box (128 B)
+  static constexpr int KC = BOX * NB;
+  static constexpr int KSEG = 8 / NB;                            // 64 MMAs per segment
+  static constexpr int A_BOX = 128 * BOX * 4;                    // 16 KB
+  static constexpr int A_BYTES = A_BOX * NB;
+  static constexpr int XL_BYTES = A_BYTES;
+  static constexpr int B_BOX = NP * BOX * 4;
+  static constexpr int B_BOX_STRIDE = (B_BOX + 1023) / 1024 * 1024;
+  static constexpr int B_BYTES = B_BOX * NB;
+  static constexpr int B_STRIDE = B_BOX_STRIDE * NB;
+  static constexpr int STAGES = (200 * 1024) / (2 * A_BYTES + B_STRIDE) > 8
+                                    ? 8 : (200 * 1024) / (2 * A_BYTES + B_STRIDE);
+  static constexpr int SMEM = 1024 + STAGES * (2 * A_BYTES + B_STRIDE) + 256;
+  static constexpr int THREADS = 192;
+};
+
+// phi (fp32 [HM][HC]) -> [NP][HC] fp32 rows for kind::tf32: [0,HM) = phi with the low 13
+// mantissa bits cleared, [HM,2HM) = the remainder, the rest 0.  Vectorised: HC % 4 == 0.
+__global__ void pre_phi_split_tf32_kernel(const float* __restrict__ phi, float* __restrict__ hl,
+                                          int HM, int NP, int64_t HC) {
+  pdl_enter();
+  const int r = blockIdx.y;
+  const int64_t n4 = HC / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  float4* dhi = reinterpret_cast<float4*>(hl + (int64_t)r * HC);
+  if (r < HM) {
+    const float4* src = reinterpret_cast<const float4*>(phi + (int64_t)r * HC);
+    float4* dlo = reinterpret_cast<float4*>(hl + (int64_t)(HM + r) * HC);
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n4; j += stride) {
+      const float4 a = __ldg(src + j);
+      const float4 h = make_float4(tf32_hi(a.x), tf32_hi(a.y), tf32_hi(a.z), tf32_hi(a.w));
+      dhi[j] = h;
+      dlo[j] = make_float4(a.x - h.x, a.y - h.y, a.z - h.z, a.w - h.w);
+    }
+  } else if (r >= 2 * HM) {
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n4; j += stride)
+      dhi[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
 // fp16 operands (x fp16): phi is split after scaling by 2^s so that max|phi| * 2^s < 2^14,
 // keeping the lo halves out of fp16's subnormal range and the hi halves finite; the mix
 // is multiplied by 2^-s afterwards (exact).  This kernel finds max|phi| (the bit patterns
@@ -137,15 +197,18 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                   float* __restrict__ logits_out, int ksplit, float* __restrict__ part,
                   const float* __restrict__ descale) {
   pdl_enter();
-  using C = MixCfg<N, NB>;
+  using C = MixCfgE<N, NB, E>;
   constexpr int HM = C::HM, S = C::STAGES;
+  constexpr bool F32 = C::F32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * C::A_BYTES;
-  uint64_t* full = (uint64_t*)(sB + S * C::B_STRIDE);
+  uint8_t* sXL = sB + S * C::B_STRIDE;  // fp32: x_lo of each stage
+  uint64_t* full = (uint64_t*)(sXL + S * C::XL_BYTES);
   uint64_t* empty = full + S;
-  uint64_t* tfull = empty + S;
+  uint64_t* xready = empty + S;         // fp32: the stage's x_lo is written
+  uint64_t* tfull = xready + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* tdone = tempty + 2;
   uint32_t* tmem_slot = (uint32_t*)(tdone + 1);
@@ -161,6 +224,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
     for (int s = 0; s < S; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1 + 4);
+      tc::mbar_init(&xready[s], 4);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
@@ -212,7 +276,8 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_16<E>(128, C::NP, false, false);
+      constexpr uint32_t idesc = F32 ? tc::idesc_tf32(128, C::NP, false, false)
+                                     : tc::idesc_16<E>(128, C::NP, false, false);
       uint32_t it = 0, j = 0;
       bool ok = true;
       for (int64_t u = blockIdx.x; u < ntiles * ksplit && ok; u += gridDim.x) {
@@ -229,6 +294,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
           for (int kc = kc0; kc < kc1; ++kc, ++it) {
             const int s = it % S;
             if (!tc::mbar_wait(&full[s], (it / S) & 1, abort_flag)) { ok = false; break; }
+            if (F32 && !tc::mbar_wait(&xready[s], (it / S) & 1, abort_flag)) { ok = false; break; }
             tc::tc_fence_after();
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
@@ -237,10 +303,22 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
               const uint64_t b0 = tc::smem_desc(
                   tc::smem_u32(sB + s * C::B_STRIDE + b * C::B_BOX_STRIDE), 16, 1024,
                   tc::kSwizzle128);
+              if constexpr (F32) {
+                const uint64_t l0 = tc::smem_desc(
+                    tc::smem_u32(sXL + s * C::XL_BYTES + b * C::A_BOX), 16, 1024,
+                    tc::kSwizzle128);
 #pragma unroll
-              for (int k = 0; k < C::BOX / 16; ++k)
-                tc::mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc,
-                             (kc != kc0 || b != 0 || k != 0) ? 1u : 0u);
+                for (int k = 0; k < C::BOX / 8; ++k) {  // K = 8 tf32 (32 B) per MMA
+                  tc::mma_tf32(d, a0 + 2 * k, b0 + 2 * k, idesc,
+                               (kc != kc0 || b != 0 || k != 0) ? 1u : 0u);
+                  tc::mma_tf32(d, l0 + 2 * k, b0 + 2 * k, idesc, 1u);
+                }
+              } else {
+#pragma unroll
+                for (int k = 0; k < C::BOX / 16; ++k)
+                  tc::mma_bf16(d, a0 + 2 * k, b0 + 2 * k, idesc,
+                               (kc != kc0 || b != 0 || k != 0) ? 1u : 0u);
+              }
             }
             tc::mma_commit(&empty[s]);
           }
@@ -276,6 +354,7 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
           break;
         }
         float csq = 0.f;
+        constexpr int EPC = 16 / (int)sizeof(E);  // elements per 16-byte chunk
 #pragma unroll
         for (int bc = 0; bc < 8 * NB; ++bc) {
           const uint4* row =
@@ -283,17 +362,29 @@ pre_mix_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
           const int c = bc & 7;
           // visit the row's 16-byte chunks in swizzled order: the 8 rows of an atom then
           // hit 8 different bank groups (a plain c order is a 32-way bank conflict)
-          float f[8];
-          widen<E>(row[c ^ (r & 7)], f);
+          const uint4 v = row[c ^ (r & 7)];
+          float f[EPC];
+          widen<E>(v, f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) csq = fmaf(f[e], f[e], csq);
+          for (int e = 0; e < EPC; ++e) csq = fmaf(f[e], f[e], csq);
+          if constexpr (F32) {
+            uint4* lrow = reinterpret_cast<uint4*>(sXL + s * C::XL_BYTES + (bc >> 3) * C::A_BOX +
+                                                   r * 128);
+            lrow[c ^ (r & 7)] = make_uint4(__float_as_uint(f[0] - tf32_hi(f[0])),
+                                           __float_as_uint(f[1] - tf32_hi(f[1])),
+                                           __float_as_uint(f[2] - tf32_hi(f[2])),
+                                           __float_as_uint(f[3] - tf32_hi(f[3])));
+          }
         }
         sq += csq;
         // the stage is refilled by TMA (async proxy): order these generic-proxy reads
-        // before that write, then release the stage
+        // (and, fp32, the x_lo writes the MMAs read) before that, then release the stage
         tc::fence_proxy_async();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&empty[s]);
+        if (lane == 0) {
+          if constexpr (F32) tc::mbar_arrive(&xready[s]);
+          tc::mbar_arrive(&empty[s]);
+        }
         if ((kc - kcb + 1) % C::KSEG == 0 || kc + 1 == kce) {
           // end of a K segment: fold its TMEM partial (hi + lo rows) into registers
           const int buf = j & 1;
@@ -580,44 +671,58 @@ pre_mix_finish_elems_kernel(const float* __restrict__ part, int ksplit,
 // ---------------------------------------------------------------------------
 bool pre_fwd_tc_eligible(const PreFwdArgs& a) {
   const int64_t HC = (int64_t)a.N * a.D;
-  return (a.dtype == MHC_BF16 || a.dtype == MHC_F16) && (a.N == 4 || a.N == 8) && HC % 8 == 0 &&
-         rows_aligned(a.x, a.x_ts, 2, 16) &&
-         a.T > 0 && a.T <= (int64_t)INT32_MAX - 256;
+  const bool f32 = a.dtype == MHC_F32;
+  return (a.dtype == MHC_BF16 || a.dtype == MHC_F16 || f32) && (a.N == 4 || a.N == 8) &&
+         HC % 8 == 0 && rows_aligned(a.x, a.x_ts, f32 ? 4 : 2, 16) &&
+         (!f32 || aligned16(a.phi)) && a.T > 0 && a.T <= (int64_t)INT32_MAX - 256;
+}
+
+// K elements per pipeline stage: two 64-column boxes (16-bit, N=4), one (16-bit, N=8), one
+// 32-column box (fp32).
+static int64_t mix_stage_k(int32_t N, int32_t dtype) {
+  return dtype == MHC_F32 ? 32 : (N <= 4 ? 2 : 1) * 64;
 }
 
 // Split K across CTAs when the tiles cannot fill the GPU (small T): K ranges per tile.
-static int mix_ksplit(int64_t T, int32_t N, int64_t D) {
+static int mix_ksplit(int64_t T, int32_t N, int64_t D, int32_t dtype) {
   const int64_t ntiles = cdiv(T, 128), sms = sm_count();
   if (ntiles <= 0 || 2 * ntiles > sms) return 1;
-  const int64_t nk = cdiv((int64_t)N * D, (N <= 4 ? 2 : 1) * 64);
+  const int64_t nk = cdiv((int64_t)N * D, mix_stage_k(N, dtype));
   int64_t k = sms / ntiles;
   if (k > nk / 4) k = nk / 4;  // at least 4 K chunks per range
   return (int)(k < 1 ? 1 : k);
 }
 
-// workspace: phi as 16-bit hi/lo rows, (split K only) the partials [ksplit][T][HM+1], then
-// the fp16 scale slots (max|phi| bits, 2^-s)
-size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D) {
+// workspace: phi as hi/lo rows (16-bit, or fp32 for kind::tf32), (split K only) the
+// partials [ksplit][T][HM+1], then the fp16 scale slots (max|phi| bits, 2^-s)
+size_t pre_fwd_tc_ws_bytes(int64_t T, int32_t N, int64_t D, int32_t dtype) {
   const int HM = hc_mix(N);
   const int NP = (2 * HM + 15) / 16 * 16;
-  const int ks = mix_ksplit(T, N, D);
-  return align_up((size_t)NP * N * D * 2) +
+  const int ks = mix_ksplit(T, N, D, dtype);
+  return align_up((size_t)NP * N * D * (dtype == MHC_F32 ? 4 : 2)) +
          (ks > 1 ? align_up((size_t)ks * T * (HM + 1) * 4) : 0) + 256;
 }
 
 template <int N, int NB, typename E>
 static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
-  using C = MixCfg<N, NB>;
+  using C = MixCfgE<N, NB, E>;
   constexpr bool f16 = std::is_same<E, __half>::value;
+  constexpr bool f32 = std::is_same<E, float>::value;
   const int64_t T = a.T, HC = (int64_t)N * a.D;
-  const int ks = mix_ksplit(T, N, a.D);
+  const int ks = mix_ksplit(T, N, a.D, a.dtype);
   E* phi_hl = (E*)a.workspace;
-  float* part = ks > 1 ? (float*)((char*)a.workspace + align_up((size_t)C::NP * HC * 2)) : nullptr;
-  char* slots = (char*)a.workspace + align_up((size_t)C::NP * HC * 2) +
+  const size_t phi_bytes = align_up((size_t)C::NP * HC * sizeof(E));
+  float* part = ks > 1 ? (float*)((char*)a.workspace + phi_bytes) : nullptr;
+  char* slots = (char*)a.workspace + phi_bytes +
                 (ks > 1 ? align_up((size_t)ks * T * (C::HM + 1) * 4) : 0);
   unsigned* maxslot = f16 ? (unsigned*)slots : nullptr;
   float* descale = f16 ? (float*)(slots + 16) : nullptr;
-  {
+  if constexpr (f32) {
+    const int64_t bx = std::min<int64_t>(cdiv(HC / 4, 256), 64);
+    launch(pre_phi_split_tf32_kernel, dim3((unsigned)bx, (unsigned)C::NP), 256, 0, s, a.phi,
+           (float*)phi_hl, C::HM, C::NP, HC);
+    MHC_LAUNCH_CHECK();
+  } else {
     const int64_t n = (int64_t)C::NP * HC;
     const int grid = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 8);
     if (f16) {
@@ -637,12 +742,14 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
     MHC_LAUNCH_CHECK();
   }
   const CUtensorMapDataType dt =
-      f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+          : f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  constexpr int eb = (int)sizeof(E);
   CUtensorMap tx, tp;
-  int st = make_tmap_2d(&tx, a.x, dt, 2, HC, T, a.x_ts * 2, C::BOX, 128,
+  int st = make_tmap_2d(&tx, a.x, dt, eb, HC, T, a.x_ts * eb, C::BOX, 128,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
-  st = make_tmap_2d(&tp, phi_hl, dt, 2, HC, C::NP, HC * 2, C::BOX, C::NP,
+  st = make_tmap_2d(&tp, phi_hl, dt, eb, HC, C::NP, HC * eb, C::BOX, C::NP,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != MHC_OK) return st;
   static bool attr_set[64];
@@ -683,6 +790,7 @@ static int pre_fwd_tc_nb(const PreFwdArgs& a, cudaStream_t s) {
 // ring still holds several stages.
 template <int N>
 static int pre_fwd_tc_n(const PreFwdArgs& a, cudaStream_t s) {
+  if (a.dtype == MHC_F32) return pre_fwd_tc_nb<N, 1, float>(a, s);
   if (a.dtype == MHC_F16) return pre_fwd_tc_nb<N, (N <= 4 ? 2 : 1), __half>(a, s);
   return pre_fwd_tc_nb<N, (N <= 4 ? 2 : 1), __nv_bfloat16>(a, s);
 }

@@ -163,6 +163,16 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D(tmem) (+)= A * B, kind::tf32 (fp32 operands in shared memory, of which the tensor core
+// uses the sign, the exponent and the top 10 mantissa bits; fp32 accumulate).
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive on `bar` once every tcgen05.mma issued so far by this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
@@ -219,6 +229,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major,
                                                  bool b_mn_major) {
   return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// Instruction descriptor: kind::tf32, A = B = tf32, D = fp32.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major,
+                                                  bool b_mn_major) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
 }
 template <typename E>
 __host__ __device__ constexpr uint32_t idesc_16(int M, int N, bool a_mn_major, bool b_mn_major) {

@@ -277,12 +277,14 @@ def test_deterministic_backward():
         assert torch.equal(u, v)
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("N", [4, 8])
-def test_pre_many_tiles_ragged(N):
+def test_pre_many_tiles_ragged(N, dt):
     """More 128-token tiles than SMs (each persistent CTA runs several tiles,
-    alternating TMEM buffers) and a ragged last tile."""
-    T, D = 148 * 128 * 2 + 77, 64
-    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.bfloat16, seed=N,
+    alternating TMEM buffers) and a ragged last tile; fp32 x runs the kind::tf32 mix
+    (x_hi and x_lo against phi_hi and phi_lo)."""
+    T, D = 148 * 128 * 2 + 77, 64 if dt == torch.bfloat16 else 72
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, dt, seed=N,
                                                        phi_std=2.0 / (N * D) ** 0.5)
     kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-4.0, clamp_max=4.0, iter_times=20)
     out = M.mhc_pre_clamp_sinkhorn(x.to(DEV), phi.to(DEV), alpha.to(DEV), base.to(DEV),
@@ -291,7 +293,7 @@ def test_pre_many_tiles_ragged(N):
     for k in ("post_out", "inv_rms", "mixes", "h_res_logits", "pre"):
         assert rel_err(out[k], ref[k]) <= TOL_FP32, k
     assert abs_err(out["comb_frag"], ref["comb_frag"]) <= TOL_SINKHORN_ABS
-    assert rel_err(out["y"], ref["y"]) <= TOL_BF16
+    assert rel_err(out["y"], ref["y"]) <= _tol(dt)
     from FlagOS_mhc import _C
     assert _C.lib().mhc_device_status() == 0
 
@@ -461,6 +463,30 @@ def test_pre_bwd_n8_iteration_counts(iters):
     assert rel_err(got[0], want[0]) <= TOL_BF16
     for a, b, name in zip(got[1:], want[1:], ("grad_phi", "grad_alpha", "grad_base")):
         assert rel_err(a, b) <= TOL_FP32, name
+
+
+@pytest.mark.parametrize("N,D", [(4, 96), (8, 64)])
+def test_pre_bwd_fp32_tensor_core_many_tiles(N, D):
+    """fp32 x on the tensor-core backward: grad_x from the bf16 operand rows (gxs) with an
+    fp32 epilogue, grad_phi on kind::tf32 (x as stored plus x_lo written in shared memory,
+    against the tf32 hi / lo parts of inv*grad_mixes): many tiles, a ragged last tile, fp32
+    tolerances against the fp64 oracle on the same saved tensors."""
+    T = 148 * 64 * 3 + 41
+    x, phi, alpha, base, gy, gpost, gcomb = pre_inputs(T, N, D, torch.float32, seed=7 + N,
+                                                       phi_std=2.0 / (N * D) ** 0.5)
+    kw = dict(norm_eps=1e-6, hc_eps=1e-6, clamp_min=-4.0, clamp_max=4.0, iter_times=20)
+    d = [t.to(DEV) for t in (x, phi, alpha, base, gy, gpost, gcomb)]
+    out = M.mhc_pre_clamp_sinkhorn(d[0], d[1], d[2], d[3], need_backward=True, **kw)
+    got = M.mhc_pre_clamp_sinkhorn_backward(
+        d[0], d[1], d[2], d[3], out["inv_rms"], out["x_scaled"], out["mixes"],
+        out["h_res_logits"], out["pre"], d[4], d[5], d[6], **kw)
+    want = O.pre_bwd_from_saved(x, phi, alpha, base, out["inv_rms"].cpu(), out["mixes"].cpu(),
+                                out["pre"].cpu(), gy, gpost, gcomb, hc_eps=1e-6,
+                                clamp_min=-4.0, clamp_max=4.0, iter_times=20, dtype=F64)
+    for a, b, name in zip(got, want, ("grad_x", "grad_phi", "grad_alpha", "grad_base")):
+        assert rel_err(a, b) <= TOL_FP32, name
+    from FlagOS_mhc import _C
+    assert _C.lib().mhc_device_status() == 0
 
 
 @pytest.mark.parametrize("N,D", [(4, 256), (8, 192)])
