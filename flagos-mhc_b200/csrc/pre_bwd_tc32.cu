@@ -54,7 +54,8 @@ struct Cfg {
   static constexpr int OUT_BYTES = 32 * 16 * 4;   // per epilogue warp: [32 tok][16 col], SW64
   static constexpr int EPI_WARPS = CB / 4;        // 4 lane quarters x CB/16 column halves
   static constexpr int GX_THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int PS = 2, XS = 4;
+  // P' (from L2) and x (from DRAM) rings deep enough to run several steps ahead
+  static constexpr int PS = 4, XS = N == 4 ? 4 : 2;
   static constexpr int OFF_G = 0;
   static constexpr int OFF_P = OFF_G + G_BYTES;
   static constexpr int OFF_X = OFF_P + PS * P_BYTES;
@@ -71,17 +72,22 @@ struct Cfg {
   static constexpr int XT_BYTES = (CT / 32) * XBOX;  // 16 KB: x tile, and x^T / x_lo^T
   static constexpr int GP_BYTES = NPH * TT * 4;   // Gp^T [NPH][32 tok] SW128
   static constexpr int GP_STRIDE = (GP_BYTES + 1023) / 1024 * 1024;
-  static constexpr int STAGE = 3 * XT_BYTES + GP_STRIDE;  // x, x^T, x_lo^T, Gp^T
-  static constexpr int S = (220 * 1024) / STAGE > 4 ? 4 : (220 * 1024) / STAGE;
+  // TMA stages [x tile | Gp^T] (deep: they cover the DRAM latency) and two buffers of
+  // [x^T | x_lo^T] (the MMA operands the transpose warps write)
+  static constexpr int XSTAGE = XT_BYTES + GP_STRIDE;
+  static constexpr int TB_BYTES = 2 * XT_BYTES;
+  static constexpr int S = (220 * 1024 - 2 * TB_BYTES) / XSTAGE > 8
+                               ? 8 : (220 * 1024 - 2 * TB_BYTES) / XSTAGE;
+  static constexpr int OFF_TB = S * XSTAGE;
   static constexpr int SUBT = 8;                  // steps per TMEM segment (64 MMAs)
   static constexpr int GP_THREADS = 32 * 10;      // TMA, MMA, 4 x_lo warps, 4 fold warps
-  static constexpr int GP_OFF_BAR = S * STAGE;
+  static constexpr int GP_OFF_BAR = OFF_TB + 2 * TB_BYTES;
   static constexpr int GP_SMEM = 1024 + GP_OFF_BAR + 256;
   static constexpr int DCOL = (NPH + 31) / 32 * 32;  // TMEM columns per D buffer
   static constexpr int GP_TMEM = 2 * DCOL <= 128 ? 128 : 2 * DCOL <= 256 ? 256 : 512;
   static_assert(GX_SMEM <= 232448 && GP_SMEM <= 232448, "shared memory");
   static_assert(OFF_P % 1024 == 0 && OFF_X % 1024 == 0 && OFF_GY % 1024 == 0 &&
-                OFF_OUT % 1024 == 0 && XBOX % 1024 == 0 && STAGE % 1024 == 0, "alignment");
+                OFF_OUT % 1024 == 0 && XBOX % 1024 == 0 && XSTAGE % 1024 == 0, "alignment");
 };
 }  // namespace bwd32
 
@@ -474,10 +480,11 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bar = (uint64_t*)(sm + C::GP_OFF_BAR);
-  uint64_t* full = bar;            // [S] x and Gp landed
-  uint64_t* lready = full + S;     // [S] x^T and x_lo^T written (4 warps)
-  uint64_t* empty = lready + S;    // [S] the step's MMAs are done with the stage
-  uint64_t* dfull = empty + S;     // [2] segment accumulated in TMEM buffer b
+  uint64_t* full = bar;            // [S] x tile and Gp^T landed
+  uint64_t* empty = full + S;      // [S] the step's MMAs are done with the stage
+  uint64_t* lready = empty + S;    // [2] x^T and x_lo^T written into buffer b (4 warps)
+  uint64_t* tfree = lready + 2;    // [2] the MMAs are done with buffer b
+  uint64_t* dfull = tfree + 2;     // [2] segment accumulated in TMEM buffer b
   uint64_t* dempty = dfull + 2;    // [2] the fold warps read buffer b
   uint64_t* tdone = dempty + 2;
   uint32_t* tmem_slot = (uint32_t*)(tdone + 1);
@@ -491,10 +498,11 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
   if (threadIdx.x == 0) {
     for (int b = 0; b < S; ++b) {
       tc::mbar_init(&full[b], 1);
-      tc::mbar_init(&lready[b], 4);
       tc::mbar_init(&empty[b], 1);
     }
     for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&lready[b], 4);
+      tc::mbar_init(&tfree[b], 1);
       tc::mbar_init(&dfull[b], 1);
       tc::mbar_init(&dempty[b], 4);
     }
@@ -530,11 +538,11 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
         const int s = k % S;
         if (!tc::mbar_wait(&empty[s], ((k / S) & 1) ^ 1, abort_flag)) break;
         tc::mbar_arrive_expect_tx(&full[s], C::XT_BYTES + C::GP_BYTES);
-        uint8_t* st = sm + s * C::STAGE;
+        uint8_t* st = sm + s * C::XSTAGE;
         for (int b = 0; b < C::CT / 32; ++b)
           tc::tma_load_2d_hint(st + b * C::XBOX, &maps.x, &full[s], (int)(ct * C::CT + 32 * b),
                                (int)(tile * C::TT), pol_stream);
-        tc::tma_load_2d_hint(st + 3 * C::XT_BYTES, &maps.gpt, &full[s], (int)(tile * C::TT), 0,
+        tc::tma_load_2d_hint(st + C::XT_BYTES, &maps.gpt, &full[s], (int)(tile * C::TT), 0,
                              pol_keep);
         if (++tile == ntiles) { tile = 0; ++ct; }
       }
@@ -552,11 +560,12 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
         const int s = k % S;
         const int db = seg & 1;
         if (seg_first && !tc::mbar_wait(&dempty[db], ((seg >> 1) & 1) ^ 1, abort_flag)) break;
+        const int tb = k & 1;
         if (!tc::mbar_wait(&full[s], (k / S) & 1, abort_flag)) break;
-        if (!tc::mbar_wait(&lready[s], (k / S) & 1, abort_flag)) break;
+        if (!tc::mbar_wait(&lready[tb], (k >> 1) & 1, abort_flag)) break;
         tc::tc_fence_after();
-        const uint32_t sxt = sbase + s * C::STAGE + C::XT_BYTES, slt = sxt + C::XT_BYTES,
-                       sgp = slt + C::XT_BYTES;
+        const uint32_t sxt = sbase + C::OFF_TB + tb * C::TB_BYTES, slt = sxt + C::XT_BYTES,
+                       sgp = sbase + s * C::XSTAGE + C::XT_BYTES;
         const uint32_t d = tmem + db * C::DCOL;
         // K-major, 128B swizzle: rows of 32 tokens, 8-row atoms of 1 KB; K = 8 tokens
         // (32 B) per MMA
@@ -569,6 +578,7 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
           tc::mma_tf32(d, al + 2 * kk, bg + 2 * kk, idesc, 1u);
         }
         tc::mma_commit(&empty[s]);
+        tc::mma_commit(&tfree[tb]);
         seg_first = false;
         if (seg_end(gs, tile)) {
           tc::mma_commit(&dfull[db]);
@@ -591,12 +601,14 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
     const int csw = c & 7;
     for (int64_t gs = s0; gs < s1; ++gs) {
       const uint32_t k = (uint32_t)(gs - s0);
-      const int s = k % S;
+      const int s = k % S, tb = k & 1;
       if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (k / S) & 1, abort_flag))) break;
-      uint8_t* st = sm + s * C::STAGE;
-      const float* xb = reinterpret_cast<const float*>(st + b * C::XBOX);
-      uint4* xt = reinterpret_cast<uint4*>(st + C::XT_BYTES + c * 128);
-      uint4* lt = reinterpret_cast<uint4*>(st + 2 * C::XT_BYTES + c * 128);
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&tfree[tb], ((k >> 1) & 1) ^ 1, abort_flag)))
+        break;
+      const float* xb = reinterpret_cast<const float*>(sm + s * C::XSTAGE + b * C::XBOX);
+      uint8_t* tbuf = sm + C::OFF_TB + tb * C::TB_BYTES;
+      uint4* xt = reinterpret_cast<uint4*>(tbuf + c * 128);
+      uint4* lt = reinterpret_cast<uint4*>(tbuf + C::XT_BYTES + c * 128);
 #pragma unroll
       for (int j = 0; j < C::TT / 4; ++j) {
         float v[4];
@@ -614,7 +626,7 @@ bwd32_gphi_kernel(const __grid_constant__ Bwd32GpMaps maps, float* __restrict__ 
       }
       tc::fence_proxy_async();  // generic writes -> the MMAs (async proxy) read them
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&lready[s]);
+      if (lane == 0) tc::mbar_arrive(&lready[tb]);
     }
   } else {
     // ------------------------------------------------------------ fold warps
