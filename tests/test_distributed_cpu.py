@@ -120,6 +120,9 @@ def _failing_worker(rank, world, port, mode, result_q):
         result_q.put(("no error", time.time() - t0))
     except Exception as e:  # noqa: BLE001 -- any error from the collective is the point
         result_q.put((type(e).__name__, time.time() - t0))
+    # flush the queue's feeder thread before the hard exit (os._exit skips it)
+    result_q.close()
+    result_q.join_thread()
     os._exit(0)
 
 
