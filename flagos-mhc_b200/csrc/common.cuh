@@ -143,6 +143,23 @@ __device__ __forceinline__ U8 ld_global_32B(const void* p) {
   return v;
 }
 
+// Compensated (Kahan) summation: s + c carries the running sum with the low-order bits
+// that s alone would drop.  Every fixed-order partial reduction of the parameter
+// gradients (grad_phi, grad_alpha, grad_base) goes through it.
+struct Kahan {
+  float s = 0.f, c = 0.f;
+  __device__ __forceinline__ void add(float v) {
+    const float y = v - c;
+    const float t = s + y;
+    c = (t - s) - y;
+    s = t;
+  }
+};
+__device__ __forceinline__ float4 kahan_add4(Kahan* k, float4 v) {
+  k[0].add(v.x); k[1].add(v.y); k[2].add(v.z); k[3].add(v.w);
+  return make_float4(k[0].s, k[1].s, k[2].s, k[3].s);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

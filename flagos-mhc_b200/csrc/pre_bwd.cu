@@ -767,7 +767,7 @@ pre_small_bwd_elems_kernel(const float* __restrict__ dlog, const float* __restri
   __threadfence();
   const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int o = w; o < NP; o += nw) {
-    float acc = 0.f;
+    Kahan k;
     // eight loads in flight per lane, added in block order
     for (int b0 = lane; b0 < (int)gridDim.x; b0 += 32 * 8) {
       float v[8];
@@ -778,9 +778,9 @@ pre_small_bwd_elems_kernel(const float* __restrict__ dlog, const float* __restri
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (b0 + 32 * u < (int)gridDim.x) acc += v[u];
+        if (b0 + 32 * u < (int)gridDim.x) k.add(v[u]);
     }
-    acc = warp_sum(acc);
+    const float acc = warp_sum(k.s);
     if (lane == 0) {
       if (o < 3) grad_alpha[o] = acc;
       else grad_base[o - 3] = acc;
@@ -798,9 +798,9 @@ __global__ void pre_reduce_ab_kernel(const float* __restrict__ partials, int nbl
   const int NP = 3 + HM;
   const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (w >= NP) return;
-  float acc = 0.f;
-  for (int b = lane; b < nblk; b += 32) acc += partials[(int64_t)b * NP + w];
-  acc = warp_sum(acc);
+  Kahan k;
+  for (int b = lane; b < nblk; b += 32) k.add(partials[(int64_t)b * NP + w]);
+  const float acc = warp_sum(k.s);
   if (lane == 0) {
     if (w < 3) grad_alpha[w] = acc;
     else grad_base[w - 3] = acc;
@@ -903,9 +903,9 @@ __global__ void pre_reduce_gphi_kernel(const float* __restrict__ part, int nspli
   pdl_enter();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  float s = 0.f;
-  for (int p = 0; p < nsplit; ++p) s += part[(int64_t)p * n + i];
-  out[i] = s;
+  Kahan s;
+  for (int p = 0; p < nsplit; ++p) s.add(part[(int64_t)p * n + i]);
+  out[i] = s.s;
 }
 
 // ---------------------------------------------------------------------------

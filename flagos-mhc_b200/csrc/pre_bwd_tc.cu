@@ -554,15 +554,16 @@ pre_bwd_gphi_reduce_kernel(const float* __restrict__ part, float* __restrict__ g
   const int n = (int)(inner / (HM * GC));
   const int k = (int)((inner / GC) % HM);
   const int c = (int)(inner % GC);
+  Kahan k4[4];
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int64_t ci = 0; ci < geo.cpg; ++ci) {
     const int64_t cell = g * geo.cpg + ci;
     const float4 a = __ldcg(reinterpret_cast<const float4*>(part + (cell * 2) * SLOT + inner));
-    s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+    s = kahan_add4(k4, a);
     if (table ? split[ci] != 0 : cell_split(ci)) {
       const float4 b =
           __ldcg(reinterpret_cast<const float4*>(part + (cell * 2 + 1) * SLOT + inner));
-      s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+      s = kahan_add4(k4, b);
     }
   }
   if (scl) {  // exact: a power of two

@@ -699,9 +699,9 @@ __global__ void bwd32_gphi_reduce_kernel(const float* __restrict__ part,
   const int64_t ct = c / CT, cc = c - ct * CT;
   const int64_t b0 = bwd32_cta_of_step(ct * ntiles, total_steps, G);
   const int64_t b1 = bwd32_cta_of_step(ct * ntiles + ntiles - 1, total_steps, G);
-  float s = 0.f;
-  for (int64_t sl = 0; sl <= b1 - b0; ++sl) s += part[((ct * maxslot + sl) * HM + kx) * CT + cc];
-  gphi[i] = s;
+  Kahan k;
+  for (int64_t sl = 0; sl <= b1 - b0; ++sl) k.add(part[((ct * maxslot + sl) * HM + kx) * CT + cc]);
+  gphi[i] = k.s;
 }
 
 // ---------------------------------------------------------------------------

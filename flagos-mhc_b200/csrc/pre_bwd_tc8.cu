@@ -640,9 +640,9 @@ __global__ void bwd8_gphi_reduce_kernel(const float* __restrict__ part, float* _
   const int64_t ct = c / gp::CT, cc = c - ct * gp::CT;
   const int64_t b0 = bwd8_cta_of_step(ct * ntiles, total_steps, G);
   const int64_t b1 = bwd8_cta_of_step(ct * ntiles + ntiles - 1, total_steps, G);
-  float s = 0.f;
-  for (int64_t sl = 0; sl <= b1 - b0; ++sl)
-    s += part[((ct * maxslot + sl) * HM + kx) * gp::CT + cc];
+  Kahan k;
+  for (int64_t sl = 0; sl <= b1 - b0; ++sl) k.add(part[((ct * maxslot + sl) * HM + kx) * gp::CT + cc]);
+  float s = k.s;
   if (scl) s *= 1.f / f16_operand_scale(scl[2]);  // exact: a power of two
   gphi[i] = s;
 }
