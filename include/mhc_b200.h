@@ -295,8 +295,8 @@ int mhc_pre_fwd_premixed(const void* x, const float* premix,
  * allocator that owns the device budget; a cgo/JNI/C binding with no device
  * allocator).  Returns MHC_ERR_SCRATCH_LIMIT when
  * mhc_pre_fwd_workspace_bytes(T,N,D,dtype) exceeds the array: N=4 at D <= 7168
- * fits up to T = 167,770 tokens, N=8 at D = 4096 up to T = 51,780, and N=8 at
- * D = 7168 never fits.  All calls on a device share the array: calls that
+ * fits up to T = 167,770 tokens (any dtype), N=8 at D = 4096 up to T = 51,780
+ * (16-bit x; fp32 x: up to D = 2048), and N=8 at D = 7168 never fits.  All calls on a device share the array: calls that
  * overlap on the GPU race.  Every call made outside stream capture looks the
  * array's address up for the current device and context (so a context re-created
  * after cudaDeviceReset is handled); a call inside a capture reuses the address of

@@ -91,3 +91,7 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     assert L.mhc_pre_fwd_workspace_bytes(167771, 4, 7168, _C.MHC_BF16) > limit
     assert L.mhc_pre_fwd_workspace_bytes(51780, 8, 4096, _C.MHC_BF16) <= limit
     assert L.mhc_pre_fwd_workspace_bytes(51781, 8, 4096, _C.MHC_BF16) > limit
+    # fp32 x: the tf32 phi rows are fp32, so N=8 fits only up to D=2048
+    assert L.mhc_pre_fwd_workspace_bytes(1, 8, 4096, _C.MHC_F32) > limit
+    assert L.mhc_pre_fwd_workspace_bytes(51780, 8, 2048, _C.MHC_F32) <= limit
+    assert L.mhc_pre_fwd_workspace_bytes(167770, 4, 7168, _C.MHC_F32) <= limit
