@@ -389,6 +389,38 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
                          "frac_of_peak": nbytes / (ms / 1e3) / 1e9 / peak}
     del x, phi
     torch.cuda.empty_cache()
+    # ---- dtype breadth at the C1 shape: fp32 / fp16 x (N=4) and N=8, pre forward +
+    # backward, each on its tensor-core path
+    dt_res = {}
+    for (N, dt) in [(4, torch.float32), (4, torch.float16), (8, torch.float32),
+                    (8, torch.float16), (8, bf)]:
+        T, D = 16384, 4096
+        HM = N * (N + 2)
+        g = torch.Generator(device=dev).manual_seed(1)
+        x = torch.randn(T, N, D, generator=g, device=dev).to(dt)
+        phi = torch.randn(HM, N * D, generator=g, device=dev) / (N * D) ** 0.5
+        alpha = torch.rand(3, generator=g, device=dev) + 0.5
+        base = torch.randn(HM, generator=g, device=dev) * 0.1
+        gy = torch.randn(T, D, generator=g, device=dev).to(dt)
+        gpost = torch.randn(T, N, generator=g, device=dev)
+        gcomb = torch.randn(T, N, N, generator=g, device=dev)
+        saved = {}
+
+        def fwd_bwd(ev):
+            ev[0].record() if ev is not None else None
+            o = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
+            ev[1].record() if ev is not None else None
+            M.mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, o["inv_rms"],
+                                              o["x_scaled"], o["mixes"], o["h_res_logits"],
+                                              o["pre"], gy, gpost, gcomb, **KW)
+            ev[2].record() if ev is not None else None
+            saved["o"] = o
+        t = _timed(fwd_bwd, steps, warmup, 3)
+        name = {torch.float32: "f32", torch.float16: "f16", bf: "bf16"}[dt]
+        dt_res[f"N{N}_{name}"] = {"shape": [T, N, D], "pre_fwd_ms": t[0], "pre_bwd_ms": t[1]}
+        del x, gy, saved
+        torch.cuda.empty_cache()
+    res["pre_dtypes"] = dt_res
     # ---- layer boundary at C3 shapes: post forward of layer l, then the pre forward of
     # layer l+1 on its output; unfused (two passes over x_{l+1}) against the fused pair
     # (post forward writing the next layer's mix partials, pre forward from them)
