@@ -637,24 +637,48 @@ def e2e_measure(M, inp, world, steps, x_scaled, reducer, dist, dev):
 
 
 # ----------------------------------------------------------------------------- GPU arm
-def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=None):
-    """K steps between two events (after a barrier and a synchronize), preceded by
-    untimed soak steps for about soak_s seconds.  Returns (max-over-ranks ms, per-step
-    op events, launches)."""
+def capture_step(M, inp, world, x_scaled, reducer, dev):
+    """One step (the same public-API calls as run_step, the cross-GPU sum included)
+    captured in a CUDA graph.  Returns (graph, library kernel launches per step) or
+    (None, reason) if the capture failed."""
     from FlagOS_mhc import _C
+    try:
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        n0 = _C.lib().mhc_kernel_launches()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+        torch.cuda.synchronize()
+        return g, _C.lib().mhc_kernel_launches() - n0
+    except Exception as e:  # noqa: BLE001 -- reported in the JSON line, eager timing used
+        torch.cuda.synchronize()
+        return None, f"{type(e).__name__}: {e}"[:200]
+
+
+def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=None,
+                graph=None, graph_launches=0):
+    """K steps between two events (after a barrier and a synchronize), preceded by
+    untimed soak steps for about soak_s seconds; with `graph`, each step is a replay of
+    the captured step.  Returns (max-over-ranks ms, per-step op events, launches)."""
+    from FlagOS_mhc import _C
+    step = (lambda: graph.replay()) if graph is not None else (
+        lambda: run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer))
     if clocks is not None:
         clocks.mark_load()
     # soak: the same number of steps on every rank (each step holds a collective), about
     # soak_s seconds' worth as timed from one step
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+    step()
     torch.cuda.synchronize()
     n = torch.tensor([int(soak_s / max(time.perf_counter() - t0, 1e-4))], device=dev)
     if world > 1:
         dist.all_reduce(n, op=dist.ReduceOp.MAX)
     for _ in range(min(int(n.item()), 20000)):
-        run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+        step()
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -665,12 +689,12 @@ def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=N
         clocks.mark_start()
     start.record()
     for k in range(K):
-        run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+        step()
     stop.record()
     torch.cuda.synchronize()
     if clocks is not None:
         clocks.mark_stop()
-    launches = _C.lib().mhc_kernel_launches() - n0
+    launches = _C.lib().mhc_kernel_launches() - n0 + (graph_launches * K if graph else 0)
     if world > 1:
         dist.barrier()
     ms_total = start.elapsed_time(stop)
@@ -678,8 +702,13 @@ def timed_steps(M, inp, world, K, x_scaled, reducer, dist, dev, soak_s, clocks=N
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
-    # the per-operator split comes from separate steps: an event between two operators
-    # stops the next one's launch from overlapping the previous kernel's tail (~3 us each)
+    # the per-operator split comes from separate eager steps (an event between two
+    # operators stops the next one's launch from overlapping the previous kernel's tail,
+    # ~3 us each); two untimed ones first, so that allocations made outside a captured
+    # graph's memory pool are not timed
+    for _ in range(2):
+        run_step(M, inp, world, x_scaled=x_scaled, reducer=reducer)
+    torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
     for k in range(K):
         run_step(M, inp, world, evs[k], x_scaled=x_scaled, reducer=reducer)
@@ -744,6 +773,8 @@ def main():
                     help="skip the C1 / C4 measurements reported beside the headline")
     ap.add_argument("--configs-only", action="store_true",
                     help="run only the C1 / C4 measurements (--steps / --warmup apply)")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the step as eager calls instead of replays of its CUDA graph")
     ap.add_argument("--skip-x-scaled", action="store_true",
                     help="opt-in variant: the forward does not write the fp32 x_scaled "
                          "(not the reference contract; the default keeps it)")
@@ -792,12 +823,30 @@ def main():
         run_step(M, inp, world, x_scaled=xs_on, reducer=reducer)
     torch.cuda.synchronize()
 
+    # the step as a CUDA graph (the library's calls and the cross-GPU sum captured once,
+    # replayed each step); every rank must have captured it, else all run eagerly
+    graph, glaunch, graph_note = None, 0, "eager (--eager)"
+    if not args.eager:
+        graph, glaunch = capture_step(M, inp, world, xs_on, reducer, dev)
+        ok = torch.tensor([1 if graph is not None else 0], device=dev)
+        if world > 1:
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if graph is None or int(ok.item()) == 0:
+            graph_note = f"eager (capture failed: {glaunch})" if graph is None else \
+                "eager (capture failed on another rank)"
+            graph, glaunch = None, 0
+        else:
+            graph_note = "cuda_graph"
     clocks = ClockSampler(local)
     clocks.start()
     ms_total, evs, launches = timed_steps(M, inp, world, K, xs_on, reducer, dist, dev,
-                                          args.soak_s, clocks)
+                                          args.soak_s, clocks, graph=graph,
+                                          graph_launches=glaunch)
     ck = clocks.stop()
     ms_step = ms_total / K
+    eager_ms = None
+    if graph is not None:  # the same K steps as eager calls, for reference
+        eager_ms = timed_steps(M, inp, world, K, xs_on, reducer, dist, dev, 0.0)[0] / K
     value = T_global * K / (ms_total / 1e3)
 
     names = ["pre_fwd", "post_fwd", "post_bwd", "pre_bwd", "grad_sum"]
@@ -847,8 +896,8 @@ def main():
                     "c0": cpu_c0()}
 
     if rank == 0:
-        coll = {"fused": "one fused peer-memory kernel (grad_phi partial reduce + cross-GPU "
-                         "sum over NVLink)", "nccl": "packed NCCL all-reduce"}[args.collective]
+        coll = {"fused": "one library kernel over NVLink peer memory (rank-order sum)",
+                "nccl": "packed NCCL all-reduce"}[args.collective]
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -868,6 +917,7 @@ def main():
                          "frac": achieved / peak, "algorithmic_bytes": ab[dom],
                          "traffic": traffic,
                          "traffic_source": ncu_traffic().get("source")},
+            "step_mode": graph_note, "eager_ms_per_step": eager_ms,
             "ops": ops, "grad_sum_ms": op_ms["grad_sum"],
             "gpu_launches": int(launches),
             "clocks": ck, "e2e": e2e, "cpu_baseline": cpu_base,

@@ -69,7 +69,8 @@ class PeerGradReducer:
     Construction is collective: every rank of `group` allocates its peer region,
     the CUDA IPC handles are exchanged with ``all_gather_object`` and each rank maps
     the others' regions.  Calls must then be made by every rank in the same order
-    (the epoch counter advances once per call on every rank).  A wait that runs
+    (each rank's epoch counter, kept in device memory, advances once per call, so a
+    call can be captured in a CUDA graph and replayed).  A wait that runs
     past `timeout_s` makes the kernel return early with MHC_ERR_TIMEOUT recorded
     (``_C.lib().mhc_device_status()``); the reducer is then unusable.  The result
     is bitwise identical on every rank (rank-order sum)."""
@@ -87,7 +88,6 @@ class PeerGradReducer:
         if self.world > 8:
             raise ValueError("PeerGradReducer: at most 8 ranks (one node)")
         self.timeout_ns = int(timeout_s * 1e9)
-        self.epoch = 0
         self._opened = []
         with torch.cuda.device(self.device):
             reg = ctypes.c_void_p()
@@ -115,10 +115,9 @@ class PeerGradReducer:
         """In-place sum over the ranks of a contiguous fp32 CUDA vector of n floats."""
         from . import _C
         assert buf.dtype == torch.float32 and buf.is_contiguous() and buf.numel() == self.n
-        self.epoch += 1
+        # epoch 0: the kernel takes the call's epoch from the region's device counter
         st = self.L.mhc_grad_sum_peers(_C.ptr(buf), _C.ptr(buf), self.n, self.ptrs, self.rank,
-                                       self.world, self.epoch, self.timeout_ns,
-                                       _C.stream_of(buf))
+                                       self.world, 0, self.timeout_ns, _C.stream_of(buf))
         _C.check(st, "PeerGradReducer")
         return buf
 

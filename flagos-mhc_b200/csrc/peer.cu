@@ -9,7 +9,12 @@
 // mapped into the other ranks' address spaces with CUDA IPC):
 //
 //   [ stage: n floats ][ result: n floats ][ flags: 2 x kMaxRanks x kMaxCtas u32 ]
+//   [ control: epoch u32, ticket u32 ]
 //
+// The call's epoch comes from the host (nonzero) or, when the host passes 0, from this
+// rank's control word: every CTA reads it at the start and uses it + 1; the last CTA to
+// finish stores the new value.  The device-kept epoch makes the call capturable in a CUDA
+// graph (a replay cannot change a kernel argument).
 // (stage: this rank's input; result: the sum over the ranks of the slice it owns)
 //
 // The packed vector is cut into `world` slices (rank r owns slice r) and every
@@ -83,13 +88,13 @@ __device__ __forceinline__ uint32_t* flag_ptr(float* region, int64_t cap, int wh
 }
 
 // Threads 0..world-1 each poll one rank's flag; the CTA agrees on the outcome.
-__device__ bool cta_wait_flags(const PeerArgs& a, int which, uint64_t deadline) {
+__device__ bool cta_wait_flags(const PeerArgs& a, int which, uint32_t epoch, uint64_t deadline) {
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
   if (threadIdx.x < a.world) {
     const uint32_t* f = flag_ptr(a.region[a.rank], a.cap, which, threadIdx.x, blockIdx.x);
-    while ((int32_t)(ld_acquire_sys(f) - a.epoch) < 0) {
+    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
       if (gtimer() > deadline) {
         ok = 0;
         atomicExch(&g_peer_error, MHC_ERR_TIMEOUT);
@@ -105,12 +110,12 @@ __device__ bool cta_wait_flags(const PeerArgs& a, int which, uint64_t deadline) 
 // Publishes this CTA's (local) writes to every rank: the barrier makes them happen before
 // thread 0's GPU-scope fence, which orders them before the flag stores.
 template <int W>
-__device__ __forceinline__ void cta_signal(const PeerArgs& a, int which, int c) {
+__device__ __forceinline__ void cta_signal(const PeerArgs& a, int which, int c, uint32_t epoch) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
 #pragma unroll
-    for (int p = 0; p < W; ++p) st_relaxed_sys(flag_ptr(a.region[p], a.cap, which, a.rank, c), a.epoch);
+    for (int p = 0; p < W; ++p) st_relaxed_sys(flag_ptr(a.region[p], a.cap, which, a.rank, c), epoch);
   }
 }
 
@@ -143,9 +148,12 @@ __device__ __forceinline__ void st4(float* p, int64_t u, int64_t n, float4 v) {
     if (4 * u + k < n) __stcg(p + 4 * u + k, w[k]);
 }
 
+__host__ __device__ inline int64_t peer_ctrl_offset(int64_t cap) {  // in floats
+  return 2 * cap + 2 * kMaxRanks * kMaxCtas;
+}
+
 template <int W>
-__global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerArgs a) {
-  pdl_enter();
+__device__ void peer_grad_sum_body(const PeerArgs& a, uint32_t epoch) {
   const int c = blockIdx.x;
   const uint64_t deadline = gtimer() + a.timeout_ns;
   float* mine = a.region[a.rank];
@@ -156,11 +164,11 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
     part_range(a, s, c, &u0, &u1);
     for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) st4(mine, u, a.n, ld4(a.src, u, a.n));
   }
-  cta_signal<W>(a, 0, c);
+  cta_signal<W>(a, 0, c, epoch);
   // 2. sum part c of this rank's slice over the ranks, in rank order; scatter it.
   // U units per thread and pass, all W*U loads issued before the first add, so many
   // NVLink requests are in flight per thread.
-  if (!cta_wait_flags(a, 0, deadline)) return;
+  if (!cta_wait_flags(a, 0, epoch, deadline)) return;
   {
     constexpr int U = W <= 4 ? 4 : 2;
     int64_t u0, u1;
@@ -187,9 +195,9 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
       }
     }
   }
-  cta_signal<W>(a, 1, c);
+  cta_signal<W>(a, 1, c, epoch);
   // 3. every rank's slice part c is final in its owner's result area: gather them
-  if (!cta_wait_flags(a, 1, deadline)) return;
+  if (!cta_wait_flags(a, 1, epoch, deadline)) return;
   // all W slices' loads of a pass are issued before the first store
   int64_t b0[W], b1[W], len = 0;
 #pragma unroll
@@ -206,6 +214,26 @@ __global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerA
 #pragma unroll
     for (int s = 0; s < W; ++s)
       if (b0[s] + i < b1[s]) st4(a.dst, b0[s] + i, a.n, v[s]);
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(kPeerThreads) peer_grad_sum_kernel(const PeerArgs a) {
+  pdl_enter();
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(a.region[a.rank] + peer_ctrl_offset(a.cap));
+  const uint32_t epoch = a.epoch != 0 ? a.epoch : *(volatile uint32_t*)ctrl + 1u;
+  peer_grad_sum_body<W>(a, epoch);
+  if (a.epoch != 0) return;
+  // device-kept epoch: the last CTA to finish (every CTA has read the old value by then)
+  // stores the new one for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ctrl + 1, 1u) == (unsigned)gridDim.x - 1) {
+      ctrl[0] = epoch;
+      ctrl[1] = 0u;
+      __threadfence();
+    }
   }
 }
 
@@ -227,7 +255,7 @@ extern "C" {
 
 size_t mhc_peer_region_bytes(int64_t n) {
   if (n <= 0) return 0;
-  return (size_t)(peer_flag_offset(peer_cap(n)) * 4 + 2 * kMaxRanks * kMaxCtas * 4);
+  return (size_t)(peer_ctrl_offset(peer_cap(n)) * 4 + 256);
 }
 
 int mhc_peer_region_alloc(int64_t n, void** region) {
@@ -280,7 +308,7 @@ int mhc_grad_sum_peers(const float* src, float* dst, int64_t n, void* const* reg
                        int32_t rank, int32_t world, uint32_t epoch, uint64_t timeout_ns,
                        void* stream) {
   if (n < 0 || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !regions ||
-      epoch == 0 || timeout_ns == 0)
+      timeout_ns == 0)
     return MHC_ERR_INVALID_ARGUMENT;
   if (n == 0) return MHC_OK;
   if (!src || !dst || ((uintptr_t)src & 15) || ((uintptr_t)dst & 15))

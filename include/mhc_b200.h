@@ -183,8 +183,12 @@ int mhc_pre_bwd_accumulate(const void* x, const float* phi, const float* alpha,
  *                                                        mhc_peer_handle_bytes())
  *   exchange the handles (any host channel), then for every other rank p
  *              mhc_peer_open(handle_p, &regions[p]);    regions[rank] = region
- * Per call (all ranks, same n, same epoch sequence 1, 2, 3, ...):
+ * Per call (all ranks, same n, same order of calls):
  *   mhc_grad_sum_peers(src, dst, n, regions, rank, world, epoch, timeout_ns, s)
+ * epoch: 0 = the kernel takes the call's epoch from a counter in this rank's region
+ * (device memory; it advances once per call), so the call can be captured in a CUDA
+ * graph and replayed; nonzero = the host numbers the calls 1, 2, 3, ... on every rank.
+ * Use one of the two forms for the life of a set of regions.
  * writes the sum over the ranks of src (n floats) into dst (may equal src), in
  * rank order, so every rank gets bitwise the same vector.  One kernel launch,
  * stream-ordered.  Every wait for a peer gives up after timeout_ns; the kernel

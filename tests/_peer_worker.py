@@ -3,7 +3,7 @@
 Checks PeerGradReducer (the fused NVLink gradient sum) against the same sum formed
 in rank order on the device from all ranks' vectors (bitwise), against NCCL's
 all-reduce (within fp32 rounding), over several calls in a row and several sizes,
-and prints PEER_OK on rank 0 when every check passed."""
+and through replays of a CUDA graph that captured one call, and prints PEER_OK on rank 0 when every check passed."""
 import os
 import sys
 
@@ -50,6 +50,33 @@ def main():
     torch.cuda.synchronize()
     k = world * (world + 1) / 2
     assert torch.equal(phi, torch.arange(phi.numel(), device=dev, dtype=torch.float32) * k)
+    red.close()
+    # captured once in a CUDA graph, replayed with new inputs: the device-kept epoch
+    # advances on every replay, so each one is a fresh, correct sum
+    n = 4099
+    red = PeerGradReducer(n, dev)
+    buf = torch.zeros(n, device=dev)
+    red.reduce_(buf)                          # one eager call first (epoch 1)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            red.reduce_(buf)
+    torch.cuda.synchronize()
+    for rep in range(3):
+        g = torch.Generator(device=dev).manual_seed(77 + rep)
+        allv = torch.randn(world, n, generator=g, device=dev)
+        buf.copy_(allv[rank])
+        want = allv[0].clone()
+        for p in range(1, world):
+            want += allv[p]
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(buf, want), (rep, (buf - want).abs().max().item())
+    assert _C.lib().mhc_device_status() == 0
+    del graph
     red.close()
     dist.barrier()
     if rank == 0:

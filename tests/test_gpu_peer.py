@@ -62,6 +62,18 @@ def test_peer_grad_sum_one_rank_is_identity():
         assert torch.equal(x, y)
     assert L.mhc_device_status() == 0
     assert L.mhc_peer_region_free(reg) == 0
+    # the device-kept epoch (epoch argument 0), several calls in a row on a fresh region
+    reg = _region(n)
+    ptrs = (ctypes.c_void_p * 8)(reg.value)
+    for call in range(3):
+        x = torch.randn(n, device="cuda")
+        st = L.mhc_grad_sum_peers(_C.ptr(x), _C.ptr(y), n, ptrs, 0, 1, 0, 10 ** 9,
+                                  _C.stream_of(x))
+        assert st == 0
+        torch.cuda.synchronize()
+        assert torch.equal(x, y)
+    assert L.mhc_device_status() == 0
+    assert L.mhc_peer_region_free(reg) == 0
 
 
 def test_peer_wait_times_out_and_reports():
@@ -96,5 +108,5 @@ def test_peer_argument_checks():
     s = _C.stream_of(x)
     assert L.mhc_grad_sum_peers(_C.ptr(x), _C.ptr(x), 8, ptrs, 0, 9, 1, 1, s) == 1   # world > 8
     assert L.mhc_grad_sum_peers(_C.ptr(x), _C.ptr(x), 8, ptrs, 2, 2, 1, 1, s) == 1   # rank
-    assert L.mhc_grad_sum_peers(_C.ptr(x), _C.ptr(x), 8, ptrs, 0, 1, 0, 1, s) == 1   # epoch 0
+    assert L.mhc_grad_sum_peers(_C.ptr(x), _C.ptr(x), 8, ptrs, 0, 1, 1, 0, s) == 1   # timeout 0
     assert L.mhc_grad_sum_peers(_C.ptr(x), _C.ptr(x), 8, ptrs, 0, 1, 1, 1, s) == 1   # null region
