@@ -322,9 +322,11 @@ def reference_arm(args, rank, world):
     host's cores: each step is one T_s-token slice of the benchmark workload."""
     if rank != 0:
         return 0
-    # calibrate the slice so one step is ~3 s of CPU work (the run stays a few minutes)
+    # calibrate the slice so the whole --steps K --warmup W run is ~2 minutes of CPU work
+    # (at most 3 s per step), whatever K is
     rate0, _ = cpu_ref_rate(128, steps=1, warmup=1)
-    T_s = int(max(64, min(4096, rate0 * 3.0)) // 64 * 64)
+    per_step_s = min(3.0, 120.0 / max(1, args.steps + args.warmup))
+    T_s = int(max(64, min(4096, rate0 * per_step_s)) // 64 * 64)
     rate, times = cpu_ref_rate(T_s, steps=args.steps, warmup=args.warmup)
     cores = torch.get_num_threads()
     ms = 1e3 * sum(times) / len(times)
@@ -752,7 +754,8 @@ def grad_sum_bench(MD, dist, dev, world, rank, K, W):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=500,
+                    help="timed steps (default: a timed region of >= 2 s at N=1)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--global-tokens", type=int, default=T_TOK,
