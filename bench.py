@@ -391,12 +391,12 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
                          "frac_of_peak": nbytes / (ms / 1e3) / 1e9 / peak}
     del x, phi
     torch.cuda.empty_cache()
-    # ---- dtype breadth at the C1 shape: fp32 / fp16 x (N=4) and N=8, pre forward +
-    # backward, each on its tensor-core path
+    # ---- dtype breadth at the C1 shape (fp32 / fp16 x, N=4 and N=8) and fp32 x at the C3
+    # shape: pre forward + backward, each on its tensor-core path
     dt_res = {}
-    for (N, dt) in [(4, torch.float32), (4, torch.float16), (8, torch.float32),
-                    (8, torch.float16), (8, bf)]:
-        T, D = 16384, 4096
+    for (N, dt, T, D) in [(4, torch.float32, 16384, 4096), (4, torch.float16, 16384, 4096),
+                          (8, torch.float32, 16384, 4096), (8, torch.float16, 16384, 4096),
+                          (8, bf, 16384, 4096), (4, torch.float32, 32768, 7168)]:
         HM = N * (N + 2)
         g = torch.Generator(device=dev).manual_seed(1)
         x = torch.randn(T, N, D, generator=g, device=dev).to(dt)
@@ -419,7 +419,8 @@ def other_configs(M, dev, peak, steps=5, warmup=2):
             saved["o"] = o
         t = _timed(fwd_bwd, steps, warmup, 3)
         name = {torch.float32: "f32", torch.float16: "f16", bf: "bf16"}[dt]
-        dt_res[f"N{N}_{name}"] = {"shape": [T, N, D], "pre_fwd_ms": t[0], "pre_bwd_ms": t[1]}
+        key = f"N{N}_{name}" + ("_C3" if (T, D) == (32768, 7168) else "")
+        dt_res[key] = {"shape": [T, N, D], "pre_fwd_ms": t[0], "pre_bwd_ms": t[1]}
         del x, gy, saved
         torch.cuda.empty_cache()
     res["pre_dtypes"] = dt_res
