@@ -364,158 +364,163 @@ def _timed(fn, steps, warmup, nev):
             for i in range(nev - 1)]
 
 
-def other_configs(M, dev, peak, steps=5, warmup=2):
-    """Config C1 (pre forward, need_backward) and config C4 (the N=8 layer step:
+def other_configs(M, dev, peak, steps=5, warmup=2, only=None):
+    """`only`: a set of group names (C1, pre_dtypes, C3_boundary, C4) to run, or None for
+    all.  Config C1 (pre forward, need_backward) and config C4 (the N=8 layer step:
     pre -> h_out = y.W (cuBLAS) -> post, then the backward of the same chain), synthetic
     inputs with the configs' distributions.  Reported beside the headline number."""
     res = {}
     bf = torch.bfloat16
-    # ---- C1: T=16384, N=4, D=4096, pre forward with need_backward=True
-    T, N, D = 16384, 4, 4096
-    g = torch.Generator(device=dev).manual_seed(1)
-    x = torch.randn(T, N, D, generator=g, device=dev).to(bf)
-    phi = torch.randn(24, N * D, generator=g, device=dev) / 128.0
-    alpha = torch.rand(3, generator=g, device=dev) + 0.5
-    base = torch.randn(24, generator=g, device=dev) * 0.1
-
-    def c1(ev):
-        if ev is not None:
-            ev[0].record()
-        M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
-        if ev is not None:
-            ev[1].record()
-    ms = _timed(c1, steps, warmup, 2)[0]
-    nbytes = T * 106756
-    res["C1_pre_fwd"] = {"shape": [T, N, D], "ms": ms, "tokens_per_s": T / (ms / 1e3),
-                         "GB/s": nbytes / (ms / 1e3) / 1e9,
-                         "frac_of_peak": nbytes / (ms / 1e3) / 1e9 / peak}
-    del x, phi
-    torch.cuda.empty_cache()
-    # ---- dtype breadth at the C1 shape (fp32 / fp16 x, N=4 and N=8) and fp32 x at the C3
-    # shape: pre forward + backward, each on its tensor-core path
-    dt_res = {}
-    for (N, dt, T, D) in [(4, torch.float32, 16384, 4096), (4, torch.float16, 16384, 4096),
-                          (8, torch.float32, 16384, 4096), (8, torch.float16, 16384, 4096),
-                          (8, bf, 16384, 4096), (4, torch.float32, 32768, 7168)]:
-        HM = N * (N + 2)
+    if only is None or "C1" in only:
+        # ---- C1: T=16384, N=4, D=4096, pre forward with need_backward=True
+        T, N, D = 16384, 4, 4096
         g = torch.Generator(device=dev).manual_seed(1)
-        x = torch.randn(T, N, D, generator=g, device=dev).to(dt)
-        phi = torch.randn(HM, N * D, generator=g, device=dev) / (N * D) ** 0.5
+        x = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+        phi = torch.randn(24, N * D, generator=g, device=dev) / 128.0
+        alpha = torch.rand(3, generator=g, device=dev) + 0.5
+        base = torch.randn(24, generator=g, device=dev) * 0.1
+
+        def c1(ev):
+            if ev is not None:
+                ev[0].record()
+            M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
+            if ev is not None:
+                ev[1].record()
+        ms = _timed(c1, steps, warmup, 2)[0]
+        nbytes = T * 106756
+        res["C1_pre_fwd"] = {"shape": [T, N, D], "ms": ms, "tokens_per_s": T / (ms / 1e3),
+                             "GB/s": nbytes / (ms / 1e3) / 1e9,
+                             "frac_of_peak": nbytes / (ms / 1e3) / 1e9 / peak}
+        del x, phi
+        torch.cuda.empty_cache()
+    if only is None or "pre_dtypes" in only:
+        # ---- dtype breadth at the C1 shape (fp32 / fp16 x, N=4 and N=8) and fp32 x at the C3
+        # shape: pre forward + backward, each on its tensor-core path
+        dt_res = {}
+        for (N, dt, T, D) in [(4, torch.float32, 16384, 4096), (4, torch.float16, 16384, 4096),
+                              (8, torch.float32, 16384, 4096), (8, torch.float16, 16384, 4096),
+                              (8, bf, 16384, 4096), (4, torch.float32, 32768, 7168)]:
+            HM = N * (N + 2)
+            g = torch.Generator(device=dev).manual_seed(1)
+            x = torch.randn(T, N, D, generator=g, device=dev).to(dt)
+            phi = torch.randn(HM, N * D, generator=g, device=dev) / (N * D) ** 0.5
+            alpha = torch.rand(3, generator=g, device=dev) + 0.5
+            base = torch.randn(HM, generator=g, device=dev) * 0.1
+            gy = torch.randn(T, D, generator=g, device=dev).to(dt)
+            gpost = torch.randn(T, N, generator=g, device=dev)
+            gcomb = torch.randn(T, N, N, generator=g, device=dev)
+            saved = {}
+
+            def fwd_bwd(ev):
+                ev[0].record() if ev is not None else None
+                o = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
+                ev[1].record() if ev is not None else None
+                M.mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, o["inv_rms"],
+                                                  o["x_scaled"], o["mixes"], o["h_res_logits"],
+                                                  o["pre"], gy, gpost, gcomb, **KW)
+                ev[2].record() if ev is not None else None
+                saved["o"] = o
+            t = _timed(fwd_bwd, steps, warmup, 3)
+            name = {torch.float32: "f32", torch.float16: "f16", bf: "bf16"}[dt]
+            key = f"N{N}_{name}" + ("_C3" if (T, D) == (32768, 7168) else "")
+            dt_res[key] = {"shape": [T, N, D], "pre_fwd_ms": t[0], "pre_bwd_ms": t[1]}
+            del x, gy, saved
+            torch.cuda.empty_cache()
+        res["pre_dtypes"] = dt_res
+    if only is None or "C3_boundary" in only:
+        # ---- layer boundary at C3 shapes: post forward of layer l, then the pre forward of
+        # layer l+1 on its output; unfused (two passes over x_{l+1}) against the fused pair
+        # (post forward writing the next layer's mix partials, pre forward from them)
+        T, N, D = 32768, 4, 7168
+        g = torch.Generator(device=dev).manual_seed(3)
+        xl = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+        ho = torch.randn(T, D, generator=g, device=dev).to(bf)
+        hr = torch.softmax(torch.randn(T, N, N, generator=g, device=dev), -1)
+        hp = 2 * torch.sigmoid(torch.randn(T, N, generator=g, device=dev))
+        phi = torch.randn(24, N * D, generator=g, device=dev) / (N * D) ** 0.5
+        alpha = torch.rand(3, generator=g, device=dev) + 0.5
+        base = torch.randn(24, generator=g, device=dev) * 0.1
+
+        def boundary(ev, fused):
+            ev[0].record() if ev is not None else None
+            if fused:
+                x1, pm = M.mhc_post(xl, hr, ho, hp, next_phi=phi)
+            else:
+                x1, pm = M.mhc_post(xl, hr, ho, hp), None
+            ev[1].record() if ev is not None else None
+            M.mhc_pre_clamp_sinkhorn(x1, phi, alpha, base, need_backward=True, premix=pm, **KW)
+            ev[2].record() if ev is not None else None
+        tu = _timed(lambda ev: boundary(ev, False), steps, warmup, 3)
+        tf = _timed(lambda ev: boundary(ev, True), steps, warmup, 3)
+        res["C3_layer_boundary_fwd"] = {
+            "shape": [T, N, D],
+            "unfused_ms": {"post_fwd": tu[0], "pre_fwd": tu[1], "total": tu[0] + tu[1]},
+            "fused_ms": {"post_fwd_with_next_mix": tf[0], "pre_fwd_from_premix": tf[1],
+                         "total": tf[0] + tf[1]},
+            "saves_ms": (tu[0] + tu[1]) - (tf[0] + tf[1]),
+            "note": "x_{l+1} is read once instead of twice across the layer boundary"}
+        del xl, ho, hr, hp, phi
+        torch.cuda.empty_cache()
+    if only is None or "C4" in only:
+        # ---- C4: T=65536, N=8, D=4096 layer step
+        T, N, D = 65536, 8, 4096
+        HM = N * (N + 2)
+        g = torch.Generator(device=dev).manual_seed(4)
+        x = torch.randn(T, N, D, generator=g, device=dev).to(bf)
+        phi = torch.randn(HM, N * D, generator=g, device=dev) / 181.0
         alpha = torch.rand(3, generator=g, device=dev) + 0.5
         base = torch.randn(HM, generator=g, device=dev) * 0.1
-        gy = torch.randn(T, D, generator=g, device=dev).to(dt)
-        gpost = torch.randn(T, N, generator=g, device=dev)
-        gcomb = torch.randn(T, N, N, generator=g, device=dev)
-        saved = {}
+        W = (torch.randn(D, D, generator=g, device=dev) / 64.0).to(bf)
+        gz = torch.randn(T, N, D, generator=g, device=dev).to(bf)
 
-        def fwd_bwd(ev):
-            ev[0].record() if ev is not None else None
-            o = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
-            ev[1].record() if ev is not None else None
-            M.mhc_pre_clamp_sinkhorn_backward(x, phi, alpha, base, o["inv_rms"],
-                                              o["x_scaled"], o["mixes"], o["h_res_logits"],
-                                              o["pre"], gy, gpost, gcomb, **KW)
-            ev[2].record() if ev is not None else None
-            saved["o"] = o
-        t = _timed(fwd_bwd, steps, warmup, 3)
-        name = {torch.float32: "f32", torch.float16: "f16", bf: "bf16"}[dt]
-        key = f"N{N}_{name}" + ("_C3" if (T, D) == (32768, 7168) else "")
-        dt_res[key] = {"shape": [T, N, D], "pre_fwd_ms": t[0], "pre_bwd_ms": t[1]}
-        del x, gy, saved
-        torch.cuda.empty_cache()
-    res["pre_dtypes"] = dt_res
-    # ---- layer boundary at C3 shapes: post forward of layer l, then the pre forward of
-    # layer l+1 on its output; unfused (two passes over x_{l+1}) against the fused pair
-    # (post forward writing the next layer's mix partials, pre forward from them)
-    T, N, D = 32768, 4, 7168
-    g = torch.Generator(device=dev).manual_seed(3)
-    xl = torch.randn(T, N, D, generator=g, device=dev).to(bf)
-    ho = torch.randn(T, D, generator=g, device=dev).to(bf)
-    hr = torch.softmax(torch.randn(T, N, N, generator=g, device=dev), -1)
-    hp = 2 * torch.sigmoid(torch.randn(T, N, generator=g, device=dev))
-    phi = torch.randn(24, N * D, generator=g, device=dev) / (N * D) ** 0.5
-    alpha = torch.rand(3, generator=g, device=dev) + 0.5
-    base = torch.randn(24, generator=g, device=dev) * 0.1
-
-    def boundary(ev, fused):
-        ev[0].record() if ev is not None else None
-        if fused:
-            x1, pm = M.mhc_post(xl, hr, ho, hp, next_phi=phi)
-        else:
-            x1, pm = M.mhc_post(xl, hr, ho, hp), None
-        ev[1].record() if ev is not None else None
-        M.mhc_pre_clamp_sinkhorn(x1, phi, alpha, base, need_backward=True, premix=pm, **KW)
-        ev[2].record() if ev is not None else None
-    tu = _timed(lambda ev: boundary(ev, False), steps, warmup, 3)
-    tf = _timed(lambda ev: boundary(ev, True), steps, warmup, 3)
-    res["C3_layer_boundary_fwd"] = {
-        "shape": [T, N, D],
-        "unfused_ms": {"post_fwd": tu[0], "pre_fwd": tu[1], "total": tu[0] + tu[1]},
-        "fused_ms": {"post_fwd_with_next_mix": tf[0], "pre_fwd_from_premix": tf[1],
-                     "total": tf[0] + tf[1]},
-        "saves_ms": (tu[0] + tu[1]) - (tf[0] + tf[1]),
-        "note": "x_{l+1} is read once instead of twice across the layer boundary"}
-    del xl, ho, hr, hp, phi
-    torch.cuda.empty_cache()
-    # ---- C4: T=65536, N=8, D=4096 layer step
-    T, N, D = 65536, 8, 4096
-    HM = N * (N + 2)
-    g = torch.Generator(device=dev).manual_seed(4)
-    x = torch.randn(T, N, D, generator=g, device=dev).to(bf)
-    phi = torch.randn(HM, N * D, generator=g, device=dev) / 181.0
-    alpha = torch.rand(3, generator=g, device=dev) + 0.5
-    base = torch.randn(HM, generator=g, device=dev) * 0.1
-    W = (torch.randn(D, D, generator=g, device=dev) / 64.0).to(bf)
-    gz = torch.randn(T, N, D, generator=g, device=dev).to(bf)
-
-    def c4(ev, fused=False):
-        rec = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
-        rec(0)
-        out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
-        rec(1)
-        h_out = out["y"] @ W
-        rec(2)
-        M.mhc_post(x, out["comb_frag"], h_out, out["post_out"])
-        rec(3)
-        gxp, ghres, ghout, ghpost = M.mhc_post_backward(gz, x, out["comb_frag"], h_out,
-                                                        out["post_out"])
-        rec(4)
-        gy = ghout @ W.t()
-        gW = out["y"].t() @ ghout
-        rec(5)
-        if fused:
-            # x feeds both ops: the post backward's grad_x is added inside the pre backward
-            M.mhc_pre_clamp_sinkhorn_backward(
-                x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
-                out["h_res_logits"], out["pre"], gy, ghpost, ghres, grad_x_accumulate=gxp,
-                **KW)
-            rec(6)
-        else:
-            gxq = M.mhc_pre_clamp_sinkhorn_backward(
-                x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
-                out["h_res_logits"], out["pre"], gy, ghpost, ghres, **KW)[0]
-            rec(6)
-            gxp.add_(gxq)
-        rec(7)
-        return gW
-    t = _timed(c4, steps, warmup, 8)
-    tf = _timed(lambda ev: c4(ev, fused=True), steps, warmup, 8)
-    mhc_ms = t[0] + t[2] + t[3] + t[5]
-    nbytes = T * 698728
-    res["C4_layer_step"] = {
-        "shape": [T, N, D],
-        "ms": {"pre_fwd": t[0], "gemm_fwd": t[1], "post_fwd": t[2], "post_bwd": t[3],
-               "gemm_bwd": t[4], "pre_bwd": t[5], "grad_x_sum": t[6]},
-        "fused_grad_x_sum": {"pre_bwd_with_grad_x_accumulate": tf[5],
-                             "saves_ms": t[5] + t[6] - tf[5]},
-        "mhc_ms": mhc_ms, "mhc_tokens_per_s": T / (mhc_ms / 1e3),
-        "mhc_GB/s": nbytes / (mhc_ms / 1e3) / 1e9,
-        "mhc_frac_of_peak": nbytes / (mhc_ms / 1e3) / 1e9 / peak,
-        "note": "mhc_* = the four mHC ops (698,728 algorithmic B/token); the y.W GEMMs "
-                "(cuBLAS) and the torch grad_x sum are timed separately; fused_grad_x_sum "
-                "runs the same step with the post backward's grad_x added inside the pre "
-                "backward (grad_x_accumulate) instead of the torch sum",
-    }
+        def c4(ev, fused=False):
+            rec = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
+            rec(0)
+            out = M.mhc_pre_clamp_sinkhorn(x, phi, alpha, base, need_backward=True, **KW)
+            rec(1)
+            h_out = out["y"] @ W
+            rec(2)
+            M.mhc_post(x, out["comb_frag"], h_out, out["post_out"])
+            rec(3)
+            gxp, ghres, ghout, ghpost = M.mhc_post_backward(gz, x, out["comb_frag"], h_out,
+                                                            out["post_out"])
+            rec(4)
+            gy = ghout @ W.t()
+            gW = out["y"].t() @ ghout
+            rec(5)
+            if fused:
+                # x feeds both ops: the post backward's grad_x is added inside the pre backward
+                M.mhc_pre_clamp_sinkhorn_backward(
+                    x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+                    out["h_res_logits"], out["pre"], gy, ghpost, ghres, grad_x_accumulate=gxp,
+                    **KW)
+                rec(6)
+            else:
+                gxq = M.mhc_pre_clamp_sinkhorn_backward(
+                    x, phi, alpha, base, out["inv_rms"], out["x_scaled"], out["mixes"],
+                    out["h_res_logits"], out["pre"], gy, ghpost, ghres, **KW)[0]
+                rec(6)
+                gxp.add_(gxq)
+            rec(7)
+            return gW
+        t = _timed(c4, steps, warmup, 8)
+        tf = _timed(lambda ev: c4(ev, fused=True), steps, warmup, 8)
+        mhc_ms = t[0] + t[2] + t[3] + t[5]
+        nbytes = T * 698728
+        res["C4_layer_step"] = {
+            "shape": [T, N, D],
+            "ms": {"pre_fwd": t[0], "gemm_fwd": t[1], "post_fwd": t[2], "post_bwd": t[3],
+                   "gemm_bwd": t[4], "pre_bwd": t[5], "grad_x_sum": t[6]},
+            "fused_grad_x_sum": {"pre_bwd_with_grad_x_accumulate": tf[5],
+                                 "saves_ms": t[5] + t[6] - tf[5]},
+            "mhc_ms": mhc_ms, "mhc_tokens_per_s": T / (mhc_ms / 1e3),
+            "mhc_GB/s": nbytes / (mhc_ms / 1e3) / 1e9,
+            "mhc_frac_of_peak": nbytes / (mhc_ms / 1e3) / 1e9 / peak,
+            "note": "mhc_* = the four mHC ops (698,728 algorithmic B/token); the y.W GEMMs "
+                    "(cuBLAS) and the torch grad_x sum are timed separately; fused_grad_x_sum "
+                    "runs the same step with the post backward's grad_x added inside the pre "
+                    "backward (grad_x_accumulate) instead of the torch sum",
+        }
     return res
 
 
@@ -777,6 +782,9 @@ def main():
                     help="skip the C1 / C4 measurements reported beside the headline")
     ap.add_argument("--configs-only", action="store_true",
                     help="run only the C1 / C4 measurements (--steps / --warmup apply)")
+    ap.add_argument("--configs", default=None,
+                    help="with --configs-only: comma-separated groups (C1, pre_dtypes, "
+                         "C3_boundary, C4); default all")
     ap.add_argument("--eager", action="store_true",
                     help="time the step as eager calls instead of replays of its CUDA graph")
     ap.add_argument("--skip-x-scaled", action="store_true",
@@ -804,8 +812,9 @@ def main():
 
     if args.configs_only:
         peak, peak_kind = hbm_peak()
+        only = set(args.configs.split(",")) if args.configs else None
         print(json.dumps({"other_configs": other_configs(M, dev, peak, steps=args.steps,
-                                                         warmup=args.warmup),
+                                                         warmup=args.warmup, only=only),
                           "peak_kind": peak_kind}), flush=True)
         return 0
 
