@@ -76,6 +76,24 @@ def test_workspace_sizes():
     assert a > 0 and b > 0
     assert L.mhc_pre_bwd_workspace_bytes(32768, 4, 7168, 2, 40) > b   # Sinkhorn history grows
     assert L.mhc_pre_fwd_workspace_bytes(32768, 11, 7168, 2) == 0      # unsupported N
+    # the tensor-core regions: fp32 x adds its own (tf32 phi rows, bwd32 operand rows),
+    # larger than the 16-bit ones
+    assert L.mhc_pre_fwd_workspace_bytes(4096, 4, 4096, 0) > \
+        L.mhc_pre_fwd_workspace_bytes(4096, 4, 4096, 2)
+    assert L.mhc_pre_bwd_workspace_bytes(4096, 8, 4096, 0, 20) > \
+        L.mhc_pre_bwd_workspace_bytes(4096, 8, 4096, 2, 20)
+
+
+def test_peer_region_layout():
+    """[stage | result | flags 2 x 8 ranks x 256 CTAs | control block]: the stage and result
+    areas are n rounded up to 64 floats; the control block (device-kept epoch) is 256 B."""
+    from FlagOS_mhc import _C
+    L = _C.lib()
+    for n in (1, 64, 65, 24 * 28672 + 27):
+        cap = (n + 63) // 64 * 64
+        assert L.mhc_peer_region_bytes(n) == 4 * (2 * cap + 2 * 8 * 256) + 256
+    assert L.mhc_peer_region_bytes(0) == 0
+    assert L.mhc_peer_handle_bytes() == 64
 
 
 def test_cpu_tensors_raise_no_fallback():
